@@ -1,0 +1,175 @@
+"""Regenerates the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a checkout that has the reference sources and the reference library
+built from them (``make -f oracle/Makefile.ref REF=<reference checkout>``):
+
+    python tests/golden/make_golden.py
+
+Every fixture holds inputs drawn from fixed seeds and the outputs of the
+reference's own code (oracle/_ref/liboracle_ref.so): ggml's fp16 and Q4_0
+conversions, HEAD's fused Snake callback, ggml mul_mat, and whole decodes
+through the reference's L1 graph functions and (for Q4_0 models) through
+HEAD's AudioVAE::decode.  Models are not stored: they are regenerated
+bit-identically from their seeds by vxb_synth.make_model, and each fixture
+records the sha256 of the model bytes it was made from.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+import vxb_synth as S  # noqa: E402
+
+# Decode fixtures: name -> (model kwargs, latent kwargs, run L2 too)
+DECODE_CASES = {
+    "f16_full_t6": (dict(quant="f16", seed=0), dict(steps=2, T=6, seed=1), False),
+    "f16_3d_full_t6": (dict(quant="f16", seed=0, convt_3d=True), dict(steps=1, T=6, seed=1), False),
+    "q4_full_t6": (dict(quant="q4_0", seed=0), dict(steps=2, T=6, seed=1), True),
+    "f16_full_t1": (dict(quant="f16", seed=0), dict(steps=1, T=1, seed=3), False),
+    "f16_full_t32_ar": (dict(quant="f16", seed=0), dict(steps=1, T=32, seed=4, ar=0.9), False),
+    "q4_full_t32_ar": (dict(quant="q4_0", seed=0), dict(steps=1, T=32, seed=4, ar=0.9), True),
+    "q4_small_rates": (dict(quant="q4_0", seed=5, decoder_dim=512, rates=(4, 5, 2, 3)),
+                       dict(steps=2, T=8, seed=6), True),
+    "f16_small_t3": (dict(quant="f16", seed=7, decoder_dim=256, rates=(2, 2, 2, 2)),
+                     dict(steps=3, T=3, seed=8), False),
+}
+
+
+def lib():
+    path = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
+    L = ctypes.CDLL(path)
+    vp, i, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    L.ref_open.restype = vp
+    L.ref_open.argtypes = [ctypes.c_char_p, i]
+    L.ref_close.argtypes = [vp]
+    for f in ("ref_decode_l1", "ref_decode_l2"):
+        getattr(L, f).argtypes = [vp, vp, i, vp]
+    L.ref_dequant_q4_0.argtypes = [vp, ll, vp]
+    L.ref_quantize_q4_0.argtypes = [vp, ll, vp]
+    L.ref_fp32_to_fp16.argtypes = [ctypes.c_float]
+    L.ref_fp32_to_fp16.restype = ctypes.c_ushort
+    L.ref_fp16_to_fp32.argtypes = [ctypes.c_ushort]
+    L.ref_fp16_to_fp32.restype = ctypes.c_float
+    L.ref_snake_fused.argtypes = [vp, vp, vp, i, i, vp]
+    L.ref_mul_mat.argtypes = [vp, i, i, i, vp, i, vp, i]
+    return L
+
+
+def P(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def fp16_fixture(L):
+    rng = np.random.default_rng(11)
+    specials = np.array([0.0, -0.0, 1.0, -1.0, 65504.0, 65520.0, 1e6, -1e6, 6.1e-5, 5.96e-8,
+                         2.98e-8, 3e-8, 1e-10, 0.1, 1 / 3, 2049.0, 2051.0, 1.00048828125,
+                         1.000732421875, np.inf, -np.inf], dtype=np.float32)
+    x = np.concatenate([specials, rng.standard_normal(2000).astype(np.float32) * 10 ** rng.uniform(
+        -9, 5, 2000).astype(np.float32)]).astype(np.float32)
+    h = np.array([L.ref_fp32_to_fp16(float(v)) for v in x], dtype=np.uint16)
+    bits = np.arange(0, 65536, 7, dtype=np.uint16)
+    back = np.array([L.ref_fp16_to_fp32(int(b)) for b in bits], dtype=np.float32)
+    np.savez_compressed(os.path.join(HERE, "fp16.npz"), x=x, h=h, bits=bits, back=back)
+
+
+def q4_fixture(L):
+    rng = np.random.default_rng(12)
+    rows = [rng.standard_normal(32 * 64).astype(np.float32) * 0.05,
+            np.zeros(32, np.float32),                                   # all-zero block
+            np.full(32, -0.25, np.float32),                             # constant block
+            np.linspace(-1, 1, 32, dtype=np.float32),                   # symmetric extremes
+            (np.arange(32, dtype=np.float32) - 16) / 8.0,               # exact half steps
+            rng.standard_normal(32 * 8).astype(np.float32) * 1e3]
+    x = np.concatenate(rows).astype(np.float32)
+    q = np.zeros((x.size // 32, 18), np.uint8)
+    L.ref_quantize_q4_0(P(x), x.size, P(q))
+    # random blocks with finite scales for the dequantiser
+    rb = rng.integers(0, 256, (96, 18), dtype=np.uint8)
+    rb[:, 0:2] = rng.standard_normal(96).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    deq = np.zeros(96 * 32, np.float32)
+    L.ref_dequant_q4_0(P(rb), 96 * 32, P(deq))
+    np.savez_compressed(os.path.join(HERE, "q4_0.npz"), x=x, q=q, blocks=rb, deq=deq)
+
+
+def snake_fixture(L):
+    rng = np.random.default_rng(13)
+    C, T = 96, 40
+    x = (rng.standard_normal((T, C)) * 3).astype(np.float32)
+    x[0, :8] = [0, -0.0, 1e-30, 800.0, -1000.0, 1100.0, -4000.0, 3.14159265]
+    alpha = rng.uniform(0.5, 1.5, C).astype(np.float16).astype(np.float32)
+    inv = (np.float32(1.0) / (alpha + np.float32(1e-9))).astype(np.float32)
+    y = np.zeros_like(x)
+    L.ref_snake_fused(P(x), P(alpha), P(inv), C, T, P(y))
+    np.savez_compressed(os.path.join(HERE, "snake.npz"), x=x, alpha=alpha, inv=inv, y=y)
+
+
+def mulmat_fixture(L):
+    rng = np.random.default_rng(14)
+    out = {}
+    for tag, K, M, N in (("a", 64, 96, 6), ("b", 384, 192, 40), ("c", 96, 96, 17)):
+        W = (rng.standard_normal((M, K)) * (0.5 / np.sqrt(K))).astype(np.float32)
+        x = rng.standard_normal((N, K)).astype(np.float32)
+        for wt, raw in (("f16", W.astype(np.float16)), ("q4", S.quantize_q4_0(W))):
+            y = np.zeros((N, M), np.float32)
+            L.ref_mul_mat(P(np.ascontiguousarray(raw)), 1 if wt == "f16" else 2, K, M, P(x), N, P(y), 4)
+            out[f"{tag}_{wt}_w"] = raw.view(np.uint8).reshape(-1) if wt == "q4" else raw
+            out[f"{tag}_{wt}_y"] = y
+        out[f"{tag}_x"] = x
+        out[f"{tag}_shape"] = np.array([K, M, N])
+    np.savez_compressed(os.path.join(HERE, "mulmat.npz"), **out)
+
+
+def decode_fixture(L, name, mk, lk, do_l2):
+    data = S.make_model(**mk)
+    sha = hashlib.sha256(data).hexdigest()
+    z = S.make_latents(**lk)
+    rates = mk.get("rates", S.DEFAULT_RATES)
+    hop = int(np.prod(rates))
+    T = lk["T"]
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "m.gguf")
+        with open(path, "wb") as f:
+            f.write(data)
+        h = L.ref_open(path.encode(), os.cpu_count() or 4)
+        assert h, "reference failed to open the model"
+        l1 = np.zeros((z.shape[0], hop * T), np.float32)
+        l2 = np.zeros_like(l1)
+        for s in range(z.shape[0]):
+            zs = np.ascontiguousarray(z[s, 0])
+            n = L.ref_decode_l1(h, P(zs), T, P(l1[s]))
+            assert n == hop * T, n
+            if do_l2:
+                n = L.ref_decode_l2(h, P(zs), T, P(l2[s]))
+                assert n == hop * T, n
+        L.ref_close(h)
+    arrs = dict(z=z[:, 0], l1=l1, sha=np.array(sha), model=np.array(repr(mk)),
+                latents=np.array(repr(lk)))
+    if do_l2:
+        arrs["l2"] = l2
+    np.savez_compressed(os.path.join(HERE, f"decode_{name}.npz"), **arrs)
+    print(name, sha[:12], "max|y| %.3f" % np.abs(l1).max(),
+          ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
+
+
+def main():
+    L = lib()
+    fp16_fixture(L)
+    q4_fixture(L)
+    snake_fixture(L)
+    mulmat_fixture(L)
+    only = sys.argv[1:]
+    for name, (mk, lk, do_l2) in DECODE_CASES.items():
+        if not only or name in only:
+            decode_fixture(L, name, mk, lk, do_l2)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,347 @@
+"""Benchmark: AudioVAE decode on B200 (decoded audio-seconds per second).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c1|c3|c4|c5f|c5q]
+                    [--impl ours|reference]
+
+Workloads (seeded synthetic weights in the reference's GGUF layout and seeded
+latents; the reference's own VoxCPM checkpoints and mock captures are not
+distributed):
+  c2  (default) streaming replay, Q4_0-mixed weights: each step decodes one
+      independent z=[1,64,6]; the last 640 samples (40 ms) are emitted.
+  c1  the same with F16 weights.
+  c3  one 60 s utterance, z=[1,64,1500] (AR(1) 0.9), F16; a step = the decode.
+  c4  256 independent streams per step, z=[256,64,6], Q4_0-mixed, split
+      evenly over the ranks (strong scaling).
+  c5f / c5q  64 utterances z=[64,64,750] (AR(1) 0.9), F16 / Q4_0-mixed, split
+      evenly over the ranks (strong scaling).
+A step is one decode of the per-rank batch.  For c2/c1 every rank replays its
+own stream (weak scaling).  Under torchrun each rank drives one GPU; nothing
+crosses GPUs on the data path (the path shards with no exchange).
+
+value = emitted audio seconds / device time of the K timed steps (max over
+ranks), CUDA events on the launching stream, L2 flushed (256 MiB memset)
+before every step and excluded from the timed events.  e2e = the same metric
+through vxb_decode() with pinned host buffers: host->device copy of the
+latent, decode, device->host copy of the waveform, per step (host clock,
+the call is blocking).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+import vxb_synth as S  # noqa: E402
+
+SR = 16000
+HOP = 640
+WORKLOADS = {
+    # name: (quant, streams per step (global), T, emitted samples per stream-step, scaling, ar)
+    "c2": ("q4_0", 1, 6, 640, "weak", None),
+    "c1": ("f16", 1, 6, 640, "weak", None),
+    "c3": ("f16", 1, 1500, 1500 * HOP, "weak", 0.9),
+    "c4": ("q4_0", 256, 6, 640, "strong", None),
+    "c5f": ("f16", 64, 750, 750 * HOP, "strong", 0.9),
+    "c5q": ("q4_0", 64, 750, 750 * HOP, "strong", 0.9),
+}
+DESCR = {
+    "c2": "streaming replay z=[1,64,6] per step, Q4_0-mixed (17 decoder matrices Q4_0)",
+    "c1": "streaming replay z=[1,64,6] per step, F16",
+    "c3": "long-form z=[1,64,1500] (60 s) AR(1) 0.9, F16",
+    "c4": "batched streaming z=[256,64,6] per step, Q4_0-mixed",
+    "c5f": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, F16",
+    "c5q": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, Q4_0-mixed",
+}
+FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return j["hbm_gbs"], j["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" == r[5 + i].strip()})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: float = 20.0):
+    """Times the reference's own CPU decode (oracle/_ref, built from its sources)
+    on all host cores over a bounded sample of the workload.  Returns
+    (seconds per stream-step, steps timed, path label, cores)."""
+    import ctypes
+
+    so = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
+    if not os.path.exists(so):
+        return None
+    L = ctypes.CDLL(so)
+    L.ref_open.restype = ctypes.c_void_p
+    L.ref_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.ref_close.argtypes = [ctypes.c_void_p]
+    for f in ("ref_decode_l1", "ref_decode_l2"):
+        getattr(L, f).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    cores = os.cpu_count() or 1
+    h = L.ref_open(model_path.encode(), cores)
+    quant = WORKLOADS[workload][0]
+    # HEAD's AudioVAE::decode only runs Q4_0 checkpoints; F16 goes through the
+    # reference's L1 graph functions.
+    fn, label = (L.ref_decode_l2, "HEAD AudioVAE::decode (L2)") if quant == "q4_0" else \
+        (L.ref_decode_l1, "L1 graph functions (HEAD decode aborts on F16)")
+    T = z_all.shape[-1]
+    out = np.zeros(T * HOP, np.float32)
+    z0 = np.ascontiguousarray(z_all[0])
+    fn(h, z0.ctypes.data, T, out.ctypes.data)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    for i in range(z_all.shape[0]):
+        z = np.ascontiguousarray(z_all[i])
+        t0 = time.perf_counter()
+        fn(h, z.ctypes.data, T, out.ctypes.data)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    L.ref_close(h)
+    return statistics.median(times), len(times), label, cores, times
+
+
+def build_inputs(workload: str, rank: int, per_rank: int, steps: int):
+    quant, _, T, _, _, ar = WORKLOADS[workload]
+    z = S.make_latents(steps, T, seed=1000 + rank, ar=ar, batch=per_rank)
+    return z  # [steps, per_rank, 64, T]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    quant, streams, T, emit, scaling, ar = WORKLOADS[args.workload]
+    per_rank = streams if scaling == "weak" else max(1, streams // ws)
+    emitted_s_per_step = per_rank * emit / SR  # per rank
+    hbm, tfl, peak_src = peaks()
+    tmpdir = tempfile.mkdtemp(prefix="vxb_bench_")
+    model = os.path.join(tmpdir, f"{quant}.gguf")
+    S.write_model(model, quant=quant, seed=0)
+    cfg = {"workload": f"{args.workload}: {DESCR[args.workload]}", "weights": quant, "batch_per_gpu": per_rank,
+           "frames": T, "emitted_samples_per_stream_step": emit, "sample_rate": SR,
+           "l2": "flushed before every step (256 MiB memset outside the timed events)",
+           "parallelism": f"dp{ws} (independent streams per GPU, no collective)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        k = min(args.steps, 40)
+        z = build_inputs(args.workload, 0, 1, k)[:, 0]
+        r = reference_time(args.workload, model, z)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/liboracle_ref.so not built"}))
+            return
+        sec, n, label, cores, times = r
+        val = (emit / SR) / sec
+        line = {"impl": "reference", "metric": "decoded audio-sec/sec (emitted)", "value": val,
+                "unit": "audio-s/s", "n_gpus": ws, "steps": n, "warmup": 1, "ms_per_step": sec * 1e3,
+                "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": cfg,
+                "latency_ms": {"p50": sec * 1e3, "p99": float(np.percentile(times, 99)) * 1e3},
+                "cpu_baseline": {"value": val, "unit": "audio-s/s", "cores": cores, "kind": "reference",
+                                 "sample": f"{n} stream-steps of one stream, {label}, {cores} threads"},
+                "e2e": {"value": val, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import vxb
+
+    d = vxb.Decoder(local)
+    d.load_gguf(model)
+    d.prepare()
+    d.build_plan(per_rank, T, graph=True)
+    nops = len(d.ops())
+    K, W = args.steps, max(3, args.warmup)
+    z_host = build_inputs(args.workload, rank, per_rank, K + W)
+    z_dev = torch.from_numpy(z_host).cuda()
+    out_dev = torch.empty((per_rank, T * HOP), dtype=torch.float32, device="cuda")
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)  # events, flushes and decodes all on this stream
+    clocks = ClockSampler(local)  # nvidia-smi needs ~0.2 s per sample: start early, stop after the last timed work
+    time.sleep(0.5)
+
+    def step(i):
+        d.decode_device(z_dev[i], out_dev, stream)
+
+    for i in range(W):
+        step(K + i)
+    d.sync()
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        ev0[i].record(stream)
+        step(i)
+        ev1[i].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    d.sync()
+    step_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+    total_ms = sum(step_ms)
+    if dist:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    audio_total = emitted_s_per_step * K * ws
+    value = audio_total / (total_ms / 1e3)
+
+    # e2e: the public blocking call with pinned host buffers
+    z_pin = torch.from_numpy(z_host).pin_memory()
+    out_pin = torch.empty((per_rank, T * HOP), dtype=torch.float32).pin_memory()
+    for i in range(W):
+        d.decode_host_ptrs(z_pin[K + i].data_ptr(), out_pin.data_ptr())
+    e2e_ms = []
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        d.decode_host_ptrs(z_pin[i].data_ptr(), out_pin.data_ptr())
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e_total = sum(e2e_ms)
+    if dist:
+        t = torch.tensor([e2e_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = audio_total / (e2e_total / 1e3)
+
+    # per-op device times (same plan, L2 flushed before each rep) -> roofline
+    op_ms = d.time_ops(reps=10, flush=flush, flush_bytes=FLUSH_BYTES)
+    clk = clocks.stop()
+    ops = d.ops()
+    top = int(np.argmax(op_ms))
+    o = ops[top]
+    t_s = op_ms[top] / 1e3
+    intensity = o["flops"] / max(o["bytes"], 1.0)
+    if intensity > (tfl * 1e12) / (hbm * 1e9):
+        roof = {"bound": "tensor", "achieved": o["flops"] / t_s / 1e12, "peak": tfl, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": o["bytes"] / t_s / 1e9, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = peak_src
+    roof["kernel"] = o["name"]
+    roof["ms_per_launch"] = op_ms[top]
+    roof["share"] = op_ms[top] / sum(op_ms)
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            traffic = json.load(f).get(args.workload, {}).get(o["name"])
+    roof["traffic"] = traffic
+
+    cpu = None
+    if rank == 0 and ws == 1:
+        zc = build_inputs(args.workload, 0, 1, min(K, 40))[:, 0]
+        r = reference_time(args.workload, model, zc)
+        if r is not None:
+            sec, n, label, cores, _ = r
+            cpu = {"value": (emit / SR) / sec, "unit": "audio-s/s", "cores": cores, "kind": "reference",
+                   "sample": f"{n} stream-steps of one stream, {label}, {cores} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": "decoded audio-sec/sec (emitted; streams x 640-sample tail per step)"
+            if WORKLOADS[args.workload][3] == 640 else "decoded audio-sec/sec",
+            "value": value, "unit": "audio-s/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded weights and latents)", "config": cfg,
+            "latency_ms": {"p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
+                           "e2e_p50": float(np.percentile(e2e_ms, 50))},
+            "full_output_audio_s_per_s": value * (T * HOP) / emit,
+            "e2e": {"value": e2e_value, "unit": "audio-s/s", "clock": "host (blocking call)",
+                    "h2d_bytes_per_step": int(z_host[0].nbytes), "d2h_bytes_per_step": int(out_pin.nbytes)},
+            "gpu_launches": K * nops,
+            "wall_s_timed_region": wall,
+            "roofline": roof,
+            "per_op_ms": {op["name"]: round(ms, 5) for op, ms in zip(ops, op_ms)},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line))
+    d.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

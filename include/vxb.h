@@ -1,0 +1,167 @@
+/*
+ * vxb.h -- C ABI of the B200 AudioVAE decoder (libvxb.so).
+ *
+ * This is the drop-in seam for the reference's decode path
+ * (nowang6/voxcpm-inference): plain pointers, sizes and int status codes; no
+ * C++ types and no exceptions cross it.  Each entry point names the reference
+ * interface it replaces (reference file:line).  Device pointers are CUDA
+ * global-memory addresses on the context's device; host pointers are
+ * ordinary (preferably pinned) host memory.
+ *
+ * Threading: one vxb_ctx per GPU per host thread; calls on one context are
+ * not thread-safe.  Every function returns VXB_OK (0) or a VXB_ERR_* code;
+ * vxb_last_error() gives the calling thread's last message.
+ */
+#ifndef VXB_H
+#define VXB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VXB_API __attribute__((visibility("default")))
+#else
+#define VXB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes; the non-zero ones map onto voxcpm::ErrorCode
+ * (reference include/voxcpm/common.h:69-79). */
+#define VXB_OK 0
+#define VXB_ERR_INVALID_ARGUMENT 1
+#define VXB_ERR_OUT_OF_MEMORY 2
+#define VXB_ERR_FILE_NOT_FOUND 3
+#define VXB_ERR_INVALID_FORMAT 4
+#define VXB_ERR_BACKEND 5        /* CUDA error */
+#define VXB_ERR_NOT_READY 6      /* weights / plan missing (reference asserts instead) */
+#define VXB_ERR_TIMEOUT 7        /* bounded host wait expired */
+#define VXB_ERR_DEVICE_STATUS 8  /* a kernel's bounded device wait gave up */
+#define VXB_ERR_MISSING_TENSOR 9 /* required tensor absent (load_from_store -> false) */
+
+/* ggml tensor types accepted by vxb_upload_tensor (ggml.h enum values). */
+#define VXB_TYPE_F32 0
+#define VXB_TYPE_F16 1
+#define VXB_TYPE_Q4_0 2
+
+typedef struct vxb_ctx vxb_ctx;
+
+/* Last error message of the calling thread ("" if none). */
+VXB_API const char* vxb_last_error(void);
+
+/* Creates a context on CUDA device `device` with its own stream.
+ * Replaces VoxCPMBackend::VoxCPMBackend(BackendType, int) (include/voxcpm/backend.h:53,
+ * src/backend.cpp:91-121), which throws voxcpm::Error on init failure. */
+VXB_API int vxb_open(int device, vxb_ctx** out);
+
+/* Frees every device and host resource of the context (weights, plan, graph).
+ * Replaces ~VoxCPMBackend / ~VoxCPMWeightStore / ~AudioVAE
+ * (src/weight-store.cpp:55-76, src/audio-vae.cpp:295-329). */
+VXB_API int vxb_close(vxb_ctx* ctx);
+
+/* Decoder hyper-parameters, as AudioVAE::load_from_store reads them from the
+ * GGUF KV voxcpm_audio_vae_config_{latent_dim,decoder_dim,decoder_rates}
+ * (src/audio-vae.cpp:421-463, include/voxcpm/config.h:34-133). */
+VXB_API int vxb_set_config(vxb_ctx* ctx, int latent_dim, int decoder_dim, const int* rates, int n_rates);
+
+/* Uploads one tensor's bytes unchanged (F32, F16 or Q4_0 blocks) to HBM under
+ * its GGUF name; ne/n_dims are ggml's (ne[0] fastest).  Replaces the per-tensor
+ * fread into the backend buffer in VoxCPMWeightStore::load_from_file
+ * (src/weight-store.cpp:13-51, :78-225). */
+VXB_API int vxb_upload_tensor(vxb_ctx* ctx, const char* name, int ggml_type, const int64_t* ne, int n_dims,
+                      const void* host_data, size_t nbytes);
+
+/* Parses a GGUF file, applies its decoder config and uploads every tensor.
+ * Replaces VoxCPMWeightStore::load_from_file + the KV part of
+ * AudioVAE::load_from_store (src/weight-store.cpp:78-225, src/audio-vae.cpp:421-463).
+ * Missing required KV keys -> VXB_ERR_INVALID_FORMAT. */
+VXB_API int vxb_load_gguf(vxb_ctx* ctx, const char* path);
+
+/* Binds the decoder tensors by name, checks their shapes and builds the
+ * derived fp32 vectors (bias, Snake alpha, inv = 1/(alpha+1e-9), depthwise
+ * taps) on the device.  Idempotent.  Replaces load_decoder_weights +
+ * AudioVAE::ensure_derived_weights (src/audio-vae.cpp:365-419, :839-1003);
+ * a missing tensor gives VXB_ERR_MISSING_TENSOR, as load_from_store returns
+ * false.  Unlike the reference (which asserts Q4_0 convT weights at :739),
+ * F16 (2-D folded or 3-D) and Q4_0 are both accepted. */
+VXB_API int vxb_prepare(vxb_ctx* ctx);
+
+/* Allocates the activation arena for `batch` independent latents of `T` frames
+ * and captures the whole decode as one CUDA graph (use_graph != 0) or keeps
+ * it as a launch list.  Replaces the per-step graph build + gallocr reserve
+ * in AudioVAE::decode / VoxCPMBackend::reserve_compute_memory / alloc_graph
+ * (src/audio-vae.cpp:666-700, src/backend.cpp:241-287). */
+VXB_API int vxb_build_plan(vxb_ctx* ctx, int batch, int T, int use_graph);
+
+/* Samples per latent frame (product of the decoder rates, 640 for VoxCPM). */
+VXB_API int vxb_hop(const vxb_ctx* ctx);
+
+/* One decode of the planned shape: z [batch][latent_dim][T] (t fastest, each
+ * one the reference's ne=[T,latent_dim]) -> out [batch][hop*T], both HOST
+ * pointers; includes the host->device and device->host copies and waits for
+ * completion (bounded, VXB_ERR_TIMEOUT after 60 s).  Replaces
+ * tensor_set(latent) + VoxCPMBackend::compute + tensor_get(audio)
+ * (src/backend.cpp:293-339, vae_decode_mock.cpp:1186-1202). */
+VXB_API int vxb_decode(vxb_ctx* ctx, const float* z_host, float* out_host);
+
+/* Same with DEVICE pointers, enqueued on `stream` (NULL = the context's
+ * stream) without waiting.  Check completion with vxb_sync. */
+VXB_API int vxb_decode_device(vxb_ctx* ctx, const float* z_dev, float* out_dev, void* stream);
+
+/* Waits for the context's stream (and `stream` if given) up to timeout_ms;
+ * VXB_ERR_TIMEOUT if it has not finished, VXB_ERR_DEVICE_STATUS if a kernel
+ * reported a failed bounded wait. */
+VXB_API int vxb_sync(vxb_ctx* ctx, int timeout_ms);
+
+/* Copies the fp32 activation after plan stage `stage` (2+4b: transposed conv
+ * of block b; 3+4b, 4+4b: residual units 0 and 1 of block b) of the last
+ * decode to host memory [batch*frames][channels]; n = capacity in floats.
+ * Other stages are fused away and return VXB_ERR_INVALID_ARGUMENT. */
+VXB_API int vxb_debug_stage(vxb_ctx* ctx, int stage, float* host_out, size_t n);
+
+/* Number of kernel launches in the current plan (one decode). */
+VXB_API int vxb_plan_num_ops(const vxb_ctx* ctx);
+
+/* Name and algorithmic work of plan op `idx`: flops = 2*M*K*N for the convs
+ * (elementwise work counted roughly), bytes = minimal HBM traffic (weights
+ * once, each activation read/written once). */
+VXB_API int vxb_plan_op_info(const vxb_ctx* ctx, int idx, char* name, int name_cap, double* flops, double* bytes);
+
+/* Runs the plan's launch list `reps` times on the last decoded latent with a
+ * CUDA event between consecutive launches and writes each op's mean device
+ * time (ms) to ms_out[vxb_plan_num_ops]; if flush is given, flush_bytes of it
+ * are overwritten before every rep to evict L2. */
+VXB_API int vxb_time_ops(vxb_ctx* ctx, int reps, void* flush, size_t flush_bytes, float* ms_out);
+
+/* ---- single-kernel entry points (device pointers, enqueued on `stream`) ---- */
+
+/* Q4_0 blocks -> fp32 ((q - 8) * d), bit-exact with ggml's
+ * dequantize_row_q4_0 (ggml-quants.c:459-477). n = element count (multiple of 32). */
+VXB_API int vxb_q4_0_dequant(const void* blocks, int64_t n, float* out, void* stream);
+
+/* y[n][c] = x + sin(alpha*x)^2 / (alpha + 1e-9) over fp32 [N][C]
+ * (snake_fused_l2_custom, src/audio-vae.cpp:1443-1479). */
+VXB_API int vxb_snake(const float* x, const float* alpha, int C, int64_t N, float* y, void* stream);
+
+/* Pointwise conv as ggml mul_mat + bias (+ residual) (+ Snake) on the tensor
+ * cores: y[n][m] = sum_k W[m][k] x[n][k] + bias[m] (+ res[n][m]), then
+ * optionally Snake(alpha) and fp16 output.  W is the GGUF [K, M] weight (F16
+ * or Q4_0 bytes), x fp16 [N][K].  Replaces pointwise_l2 (src/audio-vae.cpp:1421-1435). */
+VXB_API int vxb_pointwise(const void* w, int w_type, int K, int M, const void* x_f16, int64_t N, const float* bias,
+                  const float* res, const float* snake_alpha, int out_f16, void* y, void* stream);
+
+/* Causal transposed conv (kernel 2s, stride s, cropped to T*s) as one
+ * implicit GEMM with a col2im epilogue: x fp16 [B*T][Cin] -> y fp32
+ * [B*T*s][Cout]; W is the folded GGUF [2s*Cout, Cin] weight (F16 or Q4_0).
+ * Replaces causal_transpose_conv1d_l2 / causal_transpose_conv1d
+ * (src/audio-vae.cpp:1642-1673, :512-534). */
+VXB_API int vxb_convt(const void* w, int w_type, int Cin, int Cout, int s, const void* x_f16, int B, int T,
+              const float* bias, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VXB_H */

@@ -1,0 +1,135 @@
+"""Single-kernel parity on the GPU, through the C ABI, against the C oracle.
+
+Tolerances: Q4_0 dequantisation is bit-exact; Snake within 1e-5 abs (the
+reference's own gate for its polynomial sin vs libm); tensor-core convs are
+compared with the oracle's GPU-numerics mode (same fp16 operand rounding)
+within 2e-4 relative to the output scale -- only the fp32 accumulation order
+differs.
+"""
+import numpy as np
+import pytest
+
+import oracle_lib as O
+import vxb_synth as S
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def vxb():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import vxb as V
+
+    V.lib()
+    return V
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def test_q4_0_dequant_bit_exact(vxb):
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(32 * 4096) * 0.1).astype(np.float32)
+    q = S.quantize_q4_0(x)
+    ref = np.zeros(x.size, np.float32)
+    O.lib().vo_dequant_q4_0(O.P(q), x.size, O.P(ref))
+    out = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    vxb.q4_0_dequant(dev(q.reshape(-1)), x.size, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_snake_matches_oracle(vxb):
+    rng = np.random.default_rng(1)
+    N, C = 333, 96
+    x = (rng.standard_normal((N, C)) * 4).astype(np.float32)
+    x[0, :4] = [0.0, 1500.0, -3000.0, 1e-20]
+    alpha = rng.uniform(0.5, 1.5, C).astype(np.float16).astype(np.float32)
+    ref = np.zeros_like(x)
+    O.lib().vo_snake(O.P(x), O.P(alpha), C, N, O.P(ref))
+    y = torch.empty((N, C), dtype=torch.float32, device="cuda")
+    vxb.snake(dev(x), dev(alpha), C, N, y)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(y.cpu().numpy(), ref, rtol=1e-6, atol=1e-5)
+
+
+def _pw_case(vxb, K, M, N, wt, res, snk, out16, seed):
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((M, K)) * (0.5 / np.sqrt(K))).astype(np.float32)
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    x16 = x.astype(np.float16)
+    b = (rng.standard_normal(M) * 0.01).astype(np.float32)
+    r = rng.standard_normal((N, M)).astype(np.float32) if res else None
+    alpha = rng.uniform(0.5, 1.5, M).astype(np.float32) if snk else None
+    if wt == "f16":
+        raw = W.astype(np.float16)
+        Wf, typ = raw.astype(np.float32), vxb.TYPE_F16
+        raw_bytes = raw.view(np.uint8).reshape(-1)
+    else:
+        raw_bytes = S.quantize_q4_0(W).reshape(-1)
+        Wf, typ = S.dequantize_q4_0(raw_bytes).reshape(M, K), vxb.TYPE_Q4_0
+    ref = np.zeros((N, M), np.float32)
+    O.lib().vo_pointwise(O.P(np.ascontiguousarray(Wf)), O.P(raw_bytes), 1 if wt == "f16" else 2, O.P(b),
+                         O.P(r) if res else None, O.P(x16.astype(np.float32)), N, K, M, O.MODE_GPU, O.P(ref))
+    if snk:
+        tmp = ref.copy()
+        O.lib().vo_snake(O.P(tmp), O.P(alpha), M, N, O.P(ref))
+    y = torch.empty((N, M), dtype=torch.float16 if out16 else torch.float32, device="cuda")
+    vxb.pointwise(dev(raw_bytes), typ, K, M, dev(x16), N, dev(b), y, res=dev(r) if res else None,
+                  snake_alpha=dev(alpha) if snk else None, out_f16=out16)
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    scale = max(1.0, float(np.abs(ref).max()))
+    tol = (2e-3 if out16 else 2e-4) * scale
+    err = float(np.abs(got - ref).max())
+    assert err <= tol, f"K={K} M={M} N={N} {wt}: max|d| {err:.3e} > {tol:.3e}"
+
+
+@pytest.mark.parametrize("wt", ["f16", "q4"])
+@pytest.mark.parametrize("K,M,N", [(64, 1536, 6), (1536, 128, 16), (768, 768, 48), (384, 384, 384),
+                                   (192, 192, 1920), (96, 96, 3840), (96, 96, 77), (384, 192, 5000),
+                                   (768, 384, 700)])
+def test_pointwise_matches_oracle(vxb, K, M, N, wt):
+    _pw_case(vxb, K, M, N, wt, res=False, snk=False, out16=False, seed=K + M + N)
+
+
+@pytest.mark.parametrize("wt", ["f16", "q4"])
+@pytest.mark.parametrize("res,snk,out16", [(True, False, False), (True, True, True), (False, True, True),
+                                           (True, True, False)])
+def test_pointwise_epilogues(vxb, wt, res, snk, out16):
+    _pw_case(vxb, 384, 192, 300, wt, res, snk, out16, seed=7)
+
+
+@pytest.mark.parametrize("wt", ["f16", "q4"])
+@pytest.mark.parametrize("Cin,Cout,s,B,T", [(1536, 768, 8, 1, 6), (768, 384, 8, 1, 48), (384, 192, 5, 1, 384),
+                                            (192, 96, 2, 1, 1920), (384, 192, 5, 3, 7), (192, 96, 2, 2, 300),
+                                            (64, 32, 3, 2, 50), (128, 64, 4, 1, 1)])
+def test_convt_matches_oracle(vxb, Cin, Cout, s, B, T, wt):
+    rng = np.random.default_rng(Cin + s + T)
+    K = 2 * s
+    Wfold = (rng.standard_normal((Cin, K * Cout)) * (0.5 / np.sqrt(Cin))).astype(np.float32)  # [ci][co*K+k]
+    x = rng.standard_normal((B * T, Cin)).astype(np.float32)
+    x16 = x.astype(np.float16)
+    b = (rng.standard_normal(Cout) * 0.01).astype(np.float32)
+    if wt == "f16":
+        raw = Wfold.astype(np.float16)
+        deq = raw.astype(np.float32)
+        raw_bytes, typ = raw.view(np.uint8).reshape(-1), vxb.TYPE_F16
+    else:
+        raw_bytes = S.quantize_q4_0(Wfold).reshape(-1)
+        deq = S.dequantize_q4_0(raw_bytes).reshape(Cin, K * Cout)
+        typ = vxb.TYPE_Q4_0
+    Wg = np.ascontiguousarray(deq.T)  # [co*K + k][ci]
+    ref = np.zeros((B * T * s, Cout), np.float32)
+    O.lib().vo_convt(O.P(Wg), 1, 2, O.P(b), O.P(x16.astype(np.float32)), T, B, Cin, Cout, s, O.MODE_GPU, O.P(ref))
+    y = torch.empty((B * T * s, Cout), dtype=torch.float32, device="cuda")
+    vxb.convt(dev(raw_bytes), typ, Cin, Cout, s, dev(x16), B, T, dev(b), y)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    err = float(np.abs(got - ref).max())
+    tol = 2e-4 * max(1.0, float(np.abs(ref).max()))
+    assert err <= tol, f"convt {Cin}->{Cout} s={s} B={B} T={T} {wt}: max|d| {err:.3e} > {tol:.3e}"

@@ -1,0 +1,929 @@
+// libvxb: the C ABI of include/vxb.h.  Weight store (unchanged F16 / Q4_0
+// bytes in HBM), derived vectors, the fixed launch plan of one decode and its
+// CUDA graph, and the single-kernel entry points.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "gguf_reader.h"
+#include "vxb.h"
+
+using namespace vxb;
+
+// ------------------------------------------------------------------ errors --
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                              \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess)                                                                      \
+            return fail(e_ == cudaErrorMemoryAllocation ? VXB_ERR_OUT_OF_MEMORY : VXB_ERR_BACKEND, \
+                        std::string(#expr) + ": " + cudaGetErrorString(e_));                       \
+    } while (0)
+
+// --------------------------------------------------------------- tensor maps --
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 tensor [outer][inner] (inner contiguous) with a {box_inner, box_outer}
+// box and the 128-byte swizzle; out-of-range elements read as zero.
+int make_tmap_f16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                  uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "TMA operand needs 16-byte aligned base and row pitch");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+    return VXB_OK;
+}
+
+// --------------------------------------------------------------- launching --
+
+int pick_bn(int64_t n) {
+    if (n > 4096) return 256;
+    if (n > 512) return 128;
+    if (n > 48) return 64;
+    if (n > 16) return 32;
+    return 16;
+}
+
+template <int AK, int BN, int EPI>
+int launch_gemm_t(dim3 grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+    constexpr int smem = GemmCfg<BN>::kSmemBytes;
+    constexpr int threads = AK >= kAQ4K ? 256 : 128;
+    static bool attr[64] = {};  // per device
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
+    if (!attr[dev]) {
+        CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<AK, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr[dev] = true;
+    }
+    gemm_kernel<AK, BN, EPI><<<grid, threads, smem, st>>>(ta, tb, a);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+template <int AK, int EPI>
+int launch_gemm_bn(int bn, dim3 grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                   cudaStream_t st) {
+    switch (bn) {
+        case 16: return launch_gemm_t<AK, 16, EPI>(grid, ta, tb, a, st);
+        case 32: return launch_gemm_t<AK, 32, EPI>(grid, ta, tb, a, st);
+        case 64: return launch_gemm_t<AK, 64, EPI>(grid, ta, tb, a, st);
+        case 128: return launch_gemm_t<AK, 128, EPI>(grid, ta, tb, a, st);
+        case 256: return launch_gemm_t<AK, 256, EPI>(grid, ta, tb, a, st);
+        default: return fail(VXB_ERR_INVALID_ARGUMENT, "bad BN");
+    }
+}
+
+// A prepared GEMM launch (tensor maps and arguments fixed at plan time).
+struct GemmOp {
+    int akind = 0, epi = 0, bn = 16;
+    dim3 grid;
+    CUtensorMap ta{}, tb{};
+    GemmArgs args{};
+    int launch(cudaStream_t st) const {
+        switch (akind * 2 + epi) {
+            case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, grid, ta, tb, args, st);
+            case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, grid, ta, tb, args, st);
+            case kAF16MN * 2 + kEpiConvT: return launch_gemm_bn<kAF16MN, kEpiConvT>(bn, grid, ta, tb, args, st);
+            case kAQ4MN * 2 + kEpiConvT: return launch_gemm_bn<kAQ4MN, kEpiConvT>(bn, grid, ta, tb, args, st);
+            default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported GEMM kind");
+        }
+    }
+};
+
+// Pointwise conv GEMM: W [M rows][K] (F16 or Q4_0), x fp16 [N][K].
+int setup_pointwise(GemmOp* op, const void* w, int w_type, int K, int M, const void* x16, int64_t N,
+                    const float* bias, const float* res, const float* alpha, const float* inv, int out_f16,
+                    void* out, int* status) {
+    if (K <= 0 || M <= 0 || N <= 0 || N > (int64_t(1) << 31) - 1)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: bad extents");
+    if (K % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: K must be a multiple of 8");
+    op->epi = kEpiPW;
+    op->bn = pick_bn(N);
+    op->grid = dim3((M + 127) / 128, static_cast<unsigned>((N + op->bn - 1) / op->bn));
+    int rc = make_tmap_f16(&op->tb, x16, K, N, uint64_t(K) * 2, 64, op->bn);
+    if (rc) return rc;
+    GemmArgs& a = op->args;
+    a = GemmArgs{};
+    a.M = M;
+    a.K = K;
+    a.N = static_cast<int>(N);
+    a.bias = bias;
+    a.res = res;
+    a.snake_alpha = alpha;
+    a.snake_inv = inv;
+    a.out = out;
+    a.out_f16 = out_f16;
+    a.status = status;
+    if (w_type == VXB_TYPE_F16) {
+        op->akind = kAF16K;
+        rc = make_tmap_f16(&op->ta, w, K, M, uint64_t(K) * 2, 64, 128);
+        if (rc) return rc;
+    } else if (w_type == VXB_TYPE_Q4_0) {
+        if (K % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 pointwise needs K % 32 == 0");
+        op->akind = kAQ4K;
+        op->ta = op->tb;  // unused by the Q4_0 kernels
+        a.a_q4 = static_cast<const uint8_t*>(w);
+        a.a_row_bytes = K / 32 * 18;
+    } else {
+        return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: weight type must be F16 or Q4_0");
+    }
+    return VXB_OK;
+}
+
+// Couts per transposed-conv tile: 2s*cpt rows <= 128 and a multiple of 8
+// (so that every A tile starts on a 16-byte boundary).
+int convt_cpt(int s) {
+    for (int c = 128 / (2 * s); c > 0; --c)
+        if ((2 * s * c) % 8 == 0) return c;
+    return 0;
+}
+
+// Transposed conv GEMM: W folded [Cin rows][2s*Cout] (F16 or Q4_0), x fp16 [B*T][Cin].
+int setup_convt(GemmOp* op, const void* w, int w_type, int Cin, int Cout, int s, const void* x16, int B, int T,
+                const float* bias, float* y, int* status) {
+    const int64_t N = int64_t(B) * T;
+    if (Cin <= 0 || Cout <= 0 || s <= 0 || s > 32 || N <= 0 || N * s > (int64_t(1) << 31) - 1)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad extents");
+    if (Cin % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: Cin must be a multiple of 8");
+    const int M = 2 * s * Cout;
+    const int cpt = convt_cpt(s);
+    if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");
+    op->epi = kEpiConvT;
+    op->bn = pick_bn(N + 1);
+    op->grid = dim3((Cout + cpt - 1) / cpt, static_cast<unsigned>((N + op->bn - 2) / (op->bn - 1)));
+    int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, op->bn);
+    if (rc) return rc;
+    GemmArgs& a = op->args;
+    a = GemmArgs{};
+    a.M = M;
+    a.K = Cin;
+    a.N = static_cast<int>(N);
+    a.bias = bias;
+    a.out = y;
+    a.s = s;
+    a.cout = Cout;
+    a.cpt = cpt;
+    a.seq_len = T;
+    a.status = status;
+    if (w_type == VXB_TYPE_F16) {
+        if ((uint64_t(M) * 2) % 16) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: 2s*Cout must be a multiple of 8");
+        op->akind = kAF16MN;
+        rc = make_tmap_f16(&op->ta, w, M, Cin, uint64_t(M) * 2, 64, 64);
+        if (rc) return rc;
+    } else if (w_type == VXB_TYPE_Q4_0) {
+        if (M % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 convt needs 2s*Cout % 32 == 0");
+        op->akind = kAQ4MN;
+        op->ta = op->tb;
+        a.a_q4 = static_cast<const uint8_t*>(w);
+        a.a_row_bytes = M / 32 * 18;
+    } else {
+        return fail(VXB_ERR_INVALID_ARGUMENT, "convt: weight type must be F16 or Q4_0");
+    }
+    return VXB_OK;
+}
+
+int grid_1d(int64_t work, int threads) {
+    const int64_t b = (work + threads - 1) / threads;
+    return static_cast<int>(std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 32));
+}
+
+// Converts an F32/F16 vector on the device to fp32 (and 1/(x+eps) if inv).
+__global__ void vec_to_f32_kernel(const void* src, int type, int64_t n, float* dst, float* inv) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const float v = type == VXB_TYPE_F32 ? static_cast<const float*>(src)[i]
+                                             : __half2float(static_cast<const __half*>(src)[i]);
+        dst[i] = v;
+        if (inv) inv[i] = 1.0f / (v + 1e-9f);
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ context --
+
+struct DevTensor {
+    std::string name;
+    int type = 0;
+    int n_dims = 0;
+    int64_t ne[4] = {1, 1, 1, 1};
+    void* dev = nullptr;
+    size_t nbytes = 0;
+    int64_t nelem() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+};
+
+struct Vec {  // derived fp32 vector (+ inverse for Snake alphas)
+    float* v = nullptr;
+    float* inv = nullptr;
+};
+
+struct ResUnit {
+    Vec a1, db, a2, pb;
+    float* dw = nullptr;  // [C][7] fp32
+    const DevTensor* pw = nullptr;
+};
+
+struct Block {
+    int cin = 0, cout = 0, s = 0;
+    Vec alpha, bias;
+    const DevTensor* convt = nullptr;
+    ResUnit ru[3];
+};
+
+struct Plan {
+    int B = 0, T = 0;
+    bool use_graph = false;
+    float* z = nullptr;     // [B][L][T]
+    float* out = nullptr;   // [B][hop*T]
+    float* xa = nullptr;    // fp32 activations (ping)
+    float* xb = nullptr;    // fp32 activations (pong)
+    __half* h16 = nullptr;  // pointwise B operand
+    __half* s16 = nullptr;  // transposed-conv B operand
+    size_t bytes = 0;
+    std::vector<std::function<int(cudaStream_t)>> ops;
+    struct OpInfo {
+        std::string name;
+        double flops = 0, bytes = 0;  // algorithmic work: 2*M*K*N, minimal HBM traffic
+    };
+    std::vector<OpInfo> info;   // one per op
+    std::vector<GemmOp> gemms;  // stable storage referenced by ops
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    struct StageRef {
+        float* buf;
+        size_t floats;
+        size_t last_op;  // index of the op that writes it
+    };
+    std::map<int, StageRef> stage_buf;  // debug stages
+};
+
+struct vxb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int latent_dim = 64, decoder_dim = 1536;
+    std::vector<int> rates{8, 8, 5, 2};
+    bool config_set = false;
+    std::map<std::string, DevTensor> tensors;
+    bool prepared = false;
+    std::vector<void*> derived_allocs;
+    // bound decoder
+    float* dw0 = nullptr;
+    Vec b0, b1;
+    const DevTensor* pw1 = nullptr;
+    std::vector<Block> blocks;
+    Vec final_alpha;
+    float* final_w = nullptr;
+    float final_bias = 0.f;
+    std::unique_ptr<Plan> plan;
+    int* status = nullptr;         // device status word
+    int* status_host = nullptr;    // pinned mirror
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+void free_plan(Plan* p) {
+    if (!p) return;
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    cudaFree(p->z);
+    cudaFree(p->out);
+    cudaFree(p->xa);
+    cudaFree(p->xb);
+    cudaFree(p->h16);
+    cudaFree(p->s16);
+}
+
+const DevTensor* get(vxb_ctx* c, const std::string& name) {
+    auto it = c->tensors.find(name);
+    return it == c->tensors.end() ? nullptr : &it->second;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* vxb_last_error(void) { return g_last_error.c_str(); }
+
+int vxb_open(int device, vxb_ctx** out) {
+    if (!out) return fail(VXB_ERR_INVALID_ARGUMENT, "null out");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(VXB_ERR_BACKEND, "no CUDA device");
+    if (device < 0 || device >= n) return fail(VXB_ERR_INVALID_ARGUMENT, "bad device index");
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(VXB_ERR_BACKEND, "libvxb needs an sm_100 (B200) device");
+    DeviceGuard g(device);
+    auto c = std::make_unique<vxb_ctx>();
+    c->device = device;
+    CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CUDA_TRY(cudaMalloc(&c->status, sizeof(int)));
+    CUDA_TRY(cudaMemset(c->status, 0, sizeof(int)));
+    CUDA_TRY(cudaMallocHost(&c->status_host, sizeof(int)));
+    *c->status_host = 0;
+    *out = c.release();
+    return VXB_OK;
+}
+
+int vxb_close(vxb_ctx* c) {
+    if (!c) return VXB_OK;
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->plan) free_plan(c->plan.get());
+    for (auto& kv : c->tensors) cudaFree(kv.second.dev);
+    for (void* p : c->derived_allocs) cudaFree(p);
+    cudaFree(c->status);
+    cudaFreeHost(c->status_host);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return VXB_OK;
+}
+
+int vxb_set_config(vxb_ctx* c, int latent_dim, int decoder_dim, const int* rates, int n_rates) {
+    if (!c || latent_dim <= 0 || decoder_dim <= 0 || !rates || n_rates <= 0 || n_rates > 8)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "bad decoder config");
+    int ch = decoder_dim;
+    for (int i = 0; i < n_rates; ++i) {
+        if (rates[i] <= 0 || rates[i] > 32 || ch % 2) return fail(VXB_ERR_INVALID_ARGUMENT, "bad decoder rates");
+        ch /= 2;
+    }
+    c->latent_dim = latent_dim;
+    c->decoder_dim = decoder_dim;
+    c->rates.assign(rates, rates + n_rates);
+    c->config_set = true;
+    c->prepared = false;
+    return VXB_OK;
+}
+
+int vxb_upload_tensor(vxb_ctx* c, const char* name, int type, const int64_t* ne, int n_dims, const void* host,
+                      size_t nbytes) {
+    if (!c || !name || !ne || n_dims < 1 || n_dims > 4 || (!host && nbytes))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "bad tensor upload arguments");
+    DevTensor t;
+    t.name = name;
+    t.type = type;
+    t.n_dims = n_dims;
+    for (int d = 0; d < n_dims; ++d) {
+        if (ne[d] <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, std::string("bad shape for ") + name);
+        t.ne[d] = ne[d];
+    }
+    const size_t want = ggml_type_nbytes(type, t.nelem());
+    if (want == 0 || want != nbytes)
+        return fail(VXB_ERR_INVALID_FORMAT, std::string("type/size mismatch for ") + name);
+    DeviceGuard g(c->device);
+    t.nbytes = nbytes;
+    CUDA_TRY(cudaMalloc(&t.dev, nbytes));
+    CUDA_TRY(cudaMemcpy(t.dev, host, nbytes, cudaMemcpyHostToDevice));
+    auto it = c->tensors.find(t.name);
+    if (it != c->tensors.end()) cudaFree(it->second.dev);
+    c->tensors[t.name] = t;
+    c->prepared = false;
+    return VXB_OK;
+}
+
+int vxb_load_gguf(vxb_ctx* c, const char* path) {
+    if (!c || !path) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    GgufFile f;
+    std::string err;
+    if (!f.open(path, &err)) {
+        FILE* probe = std::fopen(path, "rb");
+        if (!probe) return fail(VXB_ERR_FILE_NOT_FOUND, err);
+        std::fclose(probe);
+        return fail(VXB_ERR_INVALID_FORMAT, err);
+    }
+    auto u32 = [&](const char* k, int* v) {
+        const GgufValue* x = f.kv(k);
+        if (!x || (x->type != 4 && x->type != 5)) return false;  // u32 / i32
+        *v = static_cast<int>(x->i);
+        return true;
+    };
+    int latent = 0, dec = 0;
+    const GgufValue* r = f.kv("voxcpm_audio_vae_config_decoder_rates");
+    if (!u32("voxcpm_audio_vae_config_latent_dim", &latent) || !u32("voxcpm_audio_vae_config_decoder_dim", &dec) ||
+        !r || r->arr_i.empty())
+        return fail(VXB_ERR_INVALID_FORMAT, "GGUF lacks the required voxcpm_audio_vae_config_* keys");
+    std::vector<int> rates(r->arr_i.begin(), r->arr_i.end());
+    int rc = vxb_set_config(c, latent, dec, rates.data(), static_cast<int>(rates.size()));
+    if (rc) return rc;
+    std::vector<uint8_t> buf;
+    for (const auto& t : f.tensors) {
+        if (t.nbytes == 0) continue;  // types this path never reads (encoder-only extras)
+        buf.resize(t.nbytes);
+        if (!f.read_tensor(t, buf.data(), &err)) return fail(VXB_ERR_INVALID_FORMAT, err);
+        rc = vxb_upload_tensor(c, t.name.c_str(), t.type, t.ne, t.n_dims, buf.data(), t.nbytes);
+        if (rc) return rc;
+    }
+    return VXB_OK;
+}
+
+int vxb_hop(const vxb_ctx* c) {
+    if (!c) return 0;
+    int h = 1;
+    for (int r : c->rates) h *= r;
+    return h;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Derived fp32 vector of tensor `name` with `n` elements.
+int derive_vec(vxb_ctx* c, const std::string& name, int64_t n, bool with_inv, Vec* out) {
+    const DevTensor* t = get(c, name);
+    if (!t) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
+    if ((t->type != VXB_TYPE_F32 && t->type != VXB_TYPE_F16) || t->nelem() != n)
+        return fail(VXB_ERR_INVALID_FORMAT, "unexpected type/shape for " + name);
+    CUDA_TRY(cudaMalloc(&out->v, n * sizeof(float)));
+    c->derived_allocs.push_back(out->v);
+    if (with_inv) {
+        CUDA_TRY(cudaMalloc(&out->inv, n * sizeof(float)));
+        c->derived_allocs.push_back(out->inv);
+    }
+    vec_to_f32_kernel<<<grid_1d(n, 256), 256, 0, c->stream>>>(t->dev, t->type, n, out->v, out->inv);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+// Depthwise taps: GGUF [7, 1, C] (or [7, C, 1] for the final conv) is [c][k] in memory.
+int derive_taps(vxb_ctx* c, const std::string& name, int C, float** out) {
+    Vec v;
+    const DevTensor* t = get(c, name);
+    if (!t) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
+    if (t->ne[0] != 7 || t->nelem() != int64_t(7) * C)
+        return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
+    int rc = derive_vec(c, name, int64_t(7) * C, false, &v);
+    *out = v.v;
+    return rc;
+}
+
+int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t outer, const DevTensor** out) {
+    const DevTensor* t = get(c, name);
+    if (!t) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
+    if (t->type != VXB_TYPE_F16 && t->type != VXB_TYPE_Q4_0)
+        return fail(VXB_ERR_INVALID_FORMAT, name + ": conv weights must be F16 or Q4_0");
+    if (t->nelem() != inner * outer) return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
+    *out = t;
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_prepare(vxb_ctx* c) {
+    if (!c) return fail(VXB_ERR_INVALID_ARGUMENT, "null ctx");
+    if (c->prepared) return VXB_OK;
+    DeviceGuard g(c->device);
+    for (void* p : c->derived_allocs) cudaFree(p);
+    c->derived_allocs.clear();
+    c->blocks.clear();
+    // The reference refuses a store whose encoder tensors are absent
+    // (load_encoder_weights, src/audio-vae.cpp:331-363); the decoder never
+    // reads them, so only their presence is checked.
+    static const char* kEnc[] = {"audio_vae.encoder.block.0.weight", "audio_vae.encoder.block.0.bias",
+                                 "audio_vae.encoder.fc_mu.weight", "audio_vae.encoder.fc_mu.bias"};
+    for (const char* n : kEnc)
+        if (!get(c, n)) return fail(VXB_ERR_MISSING_TENSOR, std::string("missing tensor ") + n);
+    const std::string p = "audio_vae.decoder.model.";
+    const int L = c->latent_dim, D = c->decoder_dim;
+    int rc;
+    if ((rc = derive_taps(c, p + "0.weight", L, &c->dw0))) return rc;
+    if ((rc = derive_vec(c, p + "0.bias", L, false, &c->b0))) return rc;
+    if ((rc = check_matrix(c, p + "1.weight", L, D, &c->pw1))) return rc;
+    if (!(c->pw1->ne[0] == L || (c->pw1->ne[0] == 1 && c->pw1->ne[1] == L)))
+        return fail(VXB_ERR_INVALID_FORMAT, "model.1.weight must be [latent, decoder_dim] or [1, latent, decoder_dim]");
+    if ((rc = derive_vec(c, p + "1.bias", D, false, &c->b1))) return rc;
+    int C = D;
+    for (size_t bi = 0; bi < c->rates.size(); ++bi) {
+        Block b;
+        b.cin = C;
+        b.cout = C / 2;
+        b.s = c->rates[bi];
+        const std::string bp = p + std::to_string(bi + 2) + ".block.";
+        if ((rc = derive_vec(c, bp + "0.alpha", C, true, &b.alpha))) return rc;
+        if ((rc = check_matrix(c, bp + "1.weight", int64_t(2) * b.s * b.cout, C, &b.convt))) return rc;
+        if (b.convt->ne[0] != (b.convt->n_dims == 3 ? 2 * b.s : 2 * b.s * b.cout))
+            return fail(VXB_ERR_INVALID_FORMAT, bp + "1.weight: expected [2s*Cout, Cin] or [2s, Cout, Cin]");
+        if ((rc = derive_vec(c, bp + "1.bias", b.cout, false, &b.bias))) return rc;
+        for (int r = 0; r < 3; ++r) {
+            const std::string rp = bp + std::to_string(r + 2) + ".block.";
+            ResUnit& u = b.ru[r];
+            if ((rc = derive_vec(c, rp + "0.alpha", b.cout, true, &u.a1))) return rc;
+            if ((rc = derive_taps(c, rp + "1.weight", b.cout, &u.dw))) return rc;
+            if ((rc = derive_vec(c, rp + "1.bias", b.cout, false, &u.db))) return rc;
+            if ((rc = derive_vec(c, rp + "2.alpha", b.cout, true, &u.a2))) return rc;
+            if ((rc = check_matrix(c, rp + "3.weight", b.cout, b.cout, &u.pw))) return rc;
+            if ((rc = derive_vec(c, rp + "3.bias", b.cout, false, &u.pb))) return rc;
+        }
+        c->blocks.push_back(b);
+        C /= 2;
+    }
+    const int nb = static_cast<int>(c->rates.size());
+    if ((rc = derive_vec(c, p + std::to_string(nb + 2) + ".alpha", C, true, &c->final_alpha))) return rc;
+    if ((rc = derive_taps(c, p + std::to_string(nb + 3) + ".weight", C, &c->final_w))) return rc;
+    const DevTensor* fb = get(c, p + std::to_string(nb + 3) + ".bias");
+    if (!fb || fb->nelem() != 1) return fail(VXB_ERR_MISSING_TENSOR, "missing final conv bias");
+    Vec fbv;
+    if ((rc = derive_vec(c, fb->name, 1, false, &fbv))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(&c->final_bias, fbv.v, sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    c->prepared = true;
+    return VXB_OK;
+}
+
+extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
+    if (!c || B <= 0 || T <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad plan shape");
+    if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare before vxb_build_plan");
+    DeviceGuard g(c->device);
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (c->plan) free_plan(c->plan.get());
+    c->plan = std::make_unique<Plan>();
+    Plan& P = *c->plan;
+    P.B = B;
+    P.T = T;
+    P.use_graph = use_graph != 0;
+    const int L = c->latent_dim, D = c->decoder_dim, hop = vxb_hop(c);
+    // arena sizes
+    int64_t max_x = int64_t(B) * T * D, max_s = int64_t(B) * T * D;
+    {
+        int64_t n = int64_t(B) * T;
+        int C = D;
+        for (const Block& b : c->blocks) {
+            max_s = std::max(max_s, n * C);
+            n *= b.s;
+            C = b.cout;
+            max_x = std::max(max_x, n * C);
+        }
+    }
+    CUDA_TRY(cudaMalloc(&P.z, sizeof(float) * B * L * T));
+    CUDA_TRY(cudaMalloc(&P.out, sizeof(float) * int64_t(B) * T * hop));
+    CUDA_TRY(cudaMalloc(&P.xa, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&P.xb, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&P.h16, sizeof(__half) * max_x));
+    CUDA_TRY(cudaMalloc(&P.s16, sizeof(__half) * max_s));
+    P.bytes = sizeof(float) * (B * L * T + int64_t(B) * T * hop + 2 * max_x) + sizeof(__half) * (max_x + max_s);
+
+    int* st = c->status;
+    P.gemms.reserve(2 + 4 * c->blocks.size());
+    int rc;
+    // model.0 (head dw) -> h16 [N][L]
+    {
+        const float *z = P.z, *w = c->dw0, *bb = c->b0.v;
+        __half* o = P.h16;
+        P.ops.push_back([=](cudaStream_t s) {
+            head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z, w, bb, o, B, L, T);
+            return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
+        });
+        const double n0 = double(B) * T;
+        P.info.push_back({"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4});
+    }
+    // model.1 pointwise (+ block 0 snake) -> s16 [N][D]
+    {
+        P.gemms.emplace_back();
+        GemmOp& op = P.gemms.back();
+        const Block& b0 = c->blocks[0];
+        rc = setup_pointwise(&op, c->pw1->dev, c->pw1->type, L, D, P.h16, int64_t(B) * T, c->b1.v, nullptr,
+                             b0.alpha.v, b0.alpha.inv, 1, P.s16, st);
+        if (rc) return rc;
+    }
+    P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
+    auto wbytes = [](const DevTensor* t) { return double(t->nbytes); };
+    {
+        const double n0 = double(B) * T;
+        P.info.push_back({"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2});
+    }
+    int64_t n = int64_t(B) * T;
+    int Tb = T;
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& b = c->blocks[bi];
+        // transposed conv: s16 [n][cin] -> xa [n*s][cout]
+        P.gemms.emplace_back();
+        rc = setup_convt(&P.gemms.back(), b.convt->dev, b.convt->type, b.cin, b.cout, b.s, P.s16, B, Tb, b.bias.v,
+                         P.xa, st);
+        if (rc) return rc;
+        P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
+        P.info.push_back({"convt_b" + std::to_string(bi),
+                          2.0 * (2.0 * b.s * b.cout) * b.cin * double(n),
+                          wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4});
+        n *= b.s;
+        Tb *= b.s;
+        const int C = b.cout;
+        const int stage0 = 2 + 4 * static_cast<int>(bi);
+        P.stage_buf[stage0] = {P.xa, size_t(n) * C, P.ops.size() - 1};
+        float* cur = P.xa;
+        float* nxt = P.xb;
+        static const int kDil[3] = {1, 3, 9};
+        for (int r = 0; r < 3; ++r) {
+            const ResUnit& u = b.ru[r];
+            const int d = kDil[r];
+            {
+                const float* x = cur;
+                __half* h = P.h16;
+                const int Bq = B, Tq = Tb;
+                P.ops.push_back([=](cudaStream_t s) {
+                    dim3 grid((C + 31) / 32, (Tq + kPreTT - 1) / kPreTT, Bq);
+                    const size_t sm = sizeof(float) * (kPreTT + 6 * d) * 32;
+                    res_pre_kernel<<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C,
+                                                         Tq, d);
+                    return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
+                });
+                P.info.push_back({"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r),
+                                  double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4});
+            }
+            P.gemms.emplace_back();
+            GemmOp& op = P.gemms.back();
+            const bool last_unit = r == 2;
+            const bool last_block = bi + 1 == c->blocks.size();
+            if (!last_unit) {
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, nullptr, nullptr, 0,
+                                     nxt, st);
+                P.stage_buf[stage0 + 1 + r] = {nxt, size_t(n) * C, P.ops.size()};
+            } else if (!last_block) {
+                const Block& nb = c->blocks[bi + 1];
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, nb.alpha.v,
+                                     nb.alpha.inv, 1, P.s16, st);
+            } else {
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, c->final_alpha.v,
+                                     c->final_alpha.inv, 0, nxt, st);
+            }
+            if (rc) return rc;
+            P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
+            P.info.push_back({"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
+                              wbytes(u.pw) + double(n) * C * (2 + 4) +
+                                  double(n) * C * (last_unit && !last_block ? 2 : 4)});
+            std::swap(cur, nxt);
+        }
+        if (bi + 1 == c->blocks.size()) {
+            // final conv over snake(x) (held in `cur` after the swap)
+            const float* sx = cur;
+            float* o = P.out;
+            const float* w = c->final_w;
+            const float fb = c->final_bias;
+            const int Tq = Tb;
+            const int64_t total = n;
+            P.ops.push_back([=](cudaStream_t s) {
+                final_kernel<<<grid_1d(total * 32, 256), 256, 0, s>>>(sx, w, fb, o, C, Tq, total);
+                return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
+            });
+            P.info.push_back({"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4});
+        }
+    }
+    // prologue smem for d = 9 exceeds the default only for kPreTT + 54 rows; stays < 48 KB.
+    if (P.use_graph) {
+        CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        int orc = VXB_OK;
+        cudaMemsetAsync(st, 0, sizeof(int), c->stream);
+        for (auto& op : P.ops)
+            if ((orc = op(c->stream))) break;
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        if (orc) {
+            if (graph) cudaGraphDestroy(graph);
+            return orc;
+        }
+        if (e != cudaSuccess) return fail(VXB_ERR_BACKEND, std::string("graph capture: ") + cudaGetErrorString(e));
+        P.graph = graph;
+        CUDA_TRY(cudaGraphInstantiate(&P.exec, P.graph, 0));
+    }
+    return VXB_OK;
+}
+
+namespace {
+
+int run_plan(vxb_ctx* c, cudaStream_t s) {
+    Plan& P = *c->plan;
+    if (P.use_graph) {
+        CUDA_TRY(cudaGraphLaunch(P.exec, s));
+    } else {
+        CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), s));
+        for (auto& op : P.ops) {
+            int rc = op(s);
+            if (rc) return rc;
+        }
+    }
+    return VXB_OK;
+}
+
+int wait_stream(cudaStream_t s, int timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return VXB_OK;
+        if (e != cudaErrorNotReady) return fail(VXB_ERR_BACKEND, std::string("stream: ") + cudaGetErrorString(e));
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+            return fail(VXB_ERR_TIMEOUT, "timed out waiting for the device");
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+int check_status(vxb_ctx* c) {
+    if (*c->status_host != 0)
+        return fail(VXB_ERR_DEVICE_STATUS, "kernel bounded wait failed (code " + std::to_string(*c->status_host) + ")");
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_decode(vxb_ctx* c, const float* z_host, float* out_host) {
+    if (!c || !z_host || !out_host) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!c->plan) return fail(VXB_ERR_NOT_READY, "no plan: call vxb_build_plan");
+    DeviceGuard g(c->device);
+    Plan& P = *c->plan;
+    const size_t zin = sizeof(float) * P.B * c->latent_dim * P.T;
+    const size_t zout = sizeof(float) * int64_t(P.B) * P.T * vxb_hop(c);
+    CUDA_TRY(cudaMemcpyAsync(P.z, z_host, zin, cudaMemcpyHostToDevice, c->stream));
+    int rc = run_plan(c, c->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out_host, P.out, zout, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = wait_stream(c->stream, 60000))) return rc;
+    return check_status(c);
+}
+
+extern "C" int vxb_decode_device(vxb_ctx* c, const float* z_dev, float* out_dev, void* stream) {
+    if (!c || !z_dev || !out_dev) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!c->plan) return fail(VXB_ERR_NOT_READY, "no plan: call vxb_build_plan");
+    DeviceGuard g(c->device);
+    Plan& P = *c->plan;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    const size_t zin = sizeof(float) * P.B * c->latent_dim * P.T;
+    const size_t zout = sizeof(float) * int64_t(P.B) * P.T * vxb_hop(c);
+    if (z_dev != P.z) CUDA_TRY(cudaMemcpyAsync(P.z, z_dev, zin, cudaMemcpyDeviceToDevice, s));
+    int rc = run_plan(c, s);
+    if (rc) return rc;
+    if (out_dev != P.out) CUDA_TRY(cudaMemcpyAsync(out_dev, P.out, zout, cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return VXB_OK;
+}
+
+extern "C" int vxb_sync(vxb_ctx* c, int timeout_ms) {
+    if (!c) return fail(VXB_ERR_INVALID_ARGUMENT, "null ctx");
+    DeviceGuard g(c->device);
+    int rc = wait_stream(c->stream, timeout_ms);
+    if (rc) return rc;
+    CUDA_TRY(cudaDeviceSynchronize());
+    return check_status(c);
+}
+
+extern "C" int vxb_debug_stage(vxb_ctx* c, int stage, float* host_out, size_t n) {
+    if (!c || !c->plan || !host_out) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+    auto it = c->plan->stage_buf.find(stage);
+    if (it == c->plan->stage_buf.end()) return fail(VXB_ERR_INVALID_ARGUMENT, "stage not materialised");
+    const Plan::StageRef& ref = it->second;
+    if (n < ref.floats) return fail(VXB_ERR_INVALID_ARGUMENT, "host buffer too small");
+    DeviceGuard g(c->device);
+    // Later stages reuse the buffer, so re-run the launch list up to the op
+    // that writes this stage (on the latent still resident from the last decode).
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), c->stream));
+    for (size_t i = 0; i <= ref.last_op && i < c->plan->ops.size(); ++i) {
+        int rc = c->plan->ops[i](c->stream);
+        if (rc) return rc;
+    }
+    CUDA_TRY(cudaMemcpyAsync(host_out, ref.buf, ref.floats * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    int rc = wait_stream(c->stream, 60000);
+    if (rc) return rc;
+    return check_status(c);
+}
+
+// ------------------------------------------------------ single-kernel APIs --
+
+extern "C" int vxb_q4_0_dequant(const void* blocks, int64_t n, float* out, void* stream) {
+    if (!blocks || !out || n <= 0 || n % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "bad dequant arguments");
+    q4_0_dequant_kernel<<<grid_1d(n / 32, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t*>(blocks), out, n / 32);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+extern "C" int vxb_snake(const float* x, const float* alpha, int C, int64_t N, float* y, void* stream) {
+    if (!x || !alpha || !y || C <= 0 || N <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad snake arguments");
+    snake_kernel<<<grid_1d(N * C, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, alpha, nullptr, y, C,
+                                                                                       N * C);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+extern "C" int vxb_pointwise(const void* w, int w_type, int K, int M, const void* x_f16, int64_t N,
+                             const float* bias, const float* res, const float* snake_alpha, int out_f16, void* y,
+                             void* stream) {
+    if (!w || !x_f16 || !bias || !y) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    GemmOp op;
+    int rc = setup_pointwise(&op, w, w_type, K, M, x_f16, N, bias, res, snake_alpha, nullptr, out_f16, y, nullptr);
+    if (rc) return rc;
+    return op.launch(static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vxb_convt(const void* w, int w_type, int Cin, int Cout, int s, const void* x_f16, int B, int T,
+                         const float* bias, float* y, void* stream) {
+    if (!w || !x_f16 || !bias || !y) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    GemmOp op;
+    int rc = setup_convt(&op, w, w_type, Cin, Cout, s, x_f16, B, T, bias, y, nullptr);
+    if (rc) return rc;
+    return op.launch(static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------ introspection --
+
+extern "C" int vxb_plan_num_ops(const vxb_ctx* c) {
+    return (c && c->plan) ? static_cast<int>(c->plan->ops.size()) : 0;
+}
+
+extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, double* flops, double* bytes) {
+    if (!c || !c->plan || idx < 0 || idx >= static_cast<int>(c->plan->info.size()))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "bad op index");
+    const auto& in = c->plan->info[idx];
+    if (name && name_cap > 0) {
+        std::snprintf(name, name_cap, "%s", in.name.c_str());
+    }
+    if (flops) *flops = in.flops;
+    if (bytes) *bytes = in.bytes;
+    return VXB_OK;
+}
+
+extern "C" int vxb_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_bytes, float* ms_out) {
+    if (!c || !c->plan || reps <= 0 || !ms_out) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+    DeviceGuard g(c->device);
+    Plan& P = *c->plan;
+    const size_t nops = P.ops.size();
+    std::vector<cudaEvent_t> ev(nops + 1);
+    for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
+    std::vector<double> acc(nops, 0.0);
+    int rc = VXB_OK;
+    for (int r = 0; r < reps && rc == VXB_OK; ++r) {
+        if (flush && flush_bytes) CUDA_TRY(cudaMemsetAsync(flush, r & 0xff, flush_bytes, c->stream));
+        CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), c->stream));
+        CUDA_TRY(cudaEventRecord(ev[0], c->stream));
+        for (size_t i = 0; i < nops && rc == VXB_OK; ++i) {
+            rc = P.ops[i](c->stream);
+            CUDA_TRY(cudaEventRecord(ev[i + 1], c->stream));
+        }
+        CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        if (rc == VXB_OK) rc = wait_stream(c->stream, 60000);
+        for (size_t i = 0; i < nops && rc == VXB_OK; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            acc[i] += ms;
+        }
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    if (rc) return rc;
+    for (size_t i = 0; i < nops; ++i) ms_out[i] = static_cast<float>(acc[i] / reps);
+    return check_status(c);
+}

@@ -1,0 +1,220 @@
+"""Python binding of libvxb (include/vxb.h) over ctypes.
+
+The decode path is the CUDA library; there is no CPU fallback.  Loading the
+library or opening a context without a B200 raises VxbError.
+
+Device buffers are passed as raw pointers (ints) or torch CUDA tensors; torch
+is only used for device memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "lib", "libvxb.so")
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_OUT_OF_MEMORY = 2
+ERR_FILE_NOT_FOUND = 3
+ERR_INVALID_FORMAT = 4
+ERR_BACKEND = 5
+ERR_NOT_READY = 6
+ERR_TIMEOUT = 7
+ERR_DEVICE_STATUS = 8
+ERR_MISSING_TENSOR = 9
+
+TYPE_F32, TYPE_F16, TYPE_Q4_0 = 0, 1, 2
+
+# Every exported symbol of include/vxb.h with its ctypes signature.
+_vp, _i, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+SIGNATURES = {
+    "vxb_last_error": (ctypes.c_char_p, []),
+    "vxb_open": (_i, [_i, ctypes.POINTER(_vp)]),
+    "vxb_close": (_i, [_vp]),
+    "vxb_set_config": (_i, [_vp, _i, _i, ctypes.POINTER(_i), _i]),
+    "vxb_upload_tensor": (_i, [_vp, ctypes.c_char_p, _i, ctypes.POINTER(_i64), _i, _vp, _sz]),
+    "vxb_load_gguf": (_i, [_vp, ctypes.c_char_p]),
+    "vxb_prepare": (_i, [_vp]),
+    "vxb_build_plan": (_i, [_vp, _i, _i, _i]),
+    "vxb_hop": (_i, [_vp]),
+    "vxb_decode": (_i, [_vp, _vp, _vp]),
+    "vxb_decode_device": (_i, [_vp, _vp, _vp, _vp]),
+    "vxb_sync": (_i, [_vp, _i]),
+    "vxb_debug_stage": (_i, [_vp, _i, _vp, _sz]),
+    "vxb_plan_num_ops": (_i, [_vp]),
+    "vxb_plan_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
+                              ctypes.POINTER(ctypes.c_double)]),
+    "vxb_time_ops": (_i, [_vp, _i, _vp, _sz, ctypes.POINTER(ctypes.c_float)]),
+    "vxb_q4_0_dequant": (_i, [_vp, _i64, _vp, _vp]),
+    "vxb_snake": (_i, [_vp, _vp, _i, _i64, _vp, _vp]),
+    "vxb_pointwise": (_i, [_vp, _i, _i, _i, _vp, _i64, _vp, _vp, _vp, _i, _vp, _vp]),
+    "vxb_convt": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
+}
+
+
+class VxbError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"vxb error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """Loads libvxb.so (fails loudly when it is missing)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise VxbError(ERR_BACKEND, f"{LIB_PATH} not built (run voxcpm-inference_b200/build.py)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != OK:
+        raise VxbError(rc, lib().vxb_last_error().decode())
+
+
+def ptr(x) -> int | None:
+    """Device/host pointer of a torch tensor, numpy array or int (None -> NULL)."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    return x.data_ptr()
+
+
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream, named explicitly
+
+
+def _stream(stream) -> int:
+    """CUDA stream handle for a launch: the given torch stream / raw handle, or
+    torch's current stream.  Handle 0 (torch's legacy default stream) is passed
+    as cudaStreamLegacy, because NULL means "the context's own stream" in the
+    C ABI."""
+    if stream is None:
+        import torch
+
+        stream = torch.cuda.current_stream()
+    h = stream if isinstance(stream, int) else stream.cuda_stream
+    return h if h else CUDA_STREAM_LEGACY
+
+
+class Decoder:
+    """One decoder context on one GPU (mirrors VoxCPMBackend + AudioVAE)."""
+
+    def __init__(self, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().vxb_open(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+        self.B = self.T = 0
+
+    def close(self):
+        if self.h:
+            lib().vxb_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_gguf(self, path: str):
+        check(lib().vxb_load_gguf(self.h, path.encode()))
+
+    def set_config(self, latent_dim: int, decoder_dim: int, rates):
+        arr = (ctypes.c_int * len(rates))(*rates)
+        check(lib().vxb_set_config(self.h, latent_dim, decoder_dim, arr, len(rates)))
+
+    def upload(self, name: str, gtype: int, ne, data: bytes):
+        ne_arr = (ctypes.c_int64 * len(ne))(*ne)
+        buf = ctypes.create_string_buffer(data, len(data))
+        check(lib().vxb_upload_tensor(self.h, name.encode(), gtype, ne_arr, len(ne), buf, len(data)))
+
+    def prepare(self):
+        check(lib().vxb_prepare(self.h))
+
+    def build_plan(self, batch: int, T: int, graph: bool = True):
+        check(lib().vxb_build_plan(self.h, batch, T, 1 if graph else 0))
+        self.B, self.T = batch, T
+
+    @property
+    def hop(self) -> int:
+        return lib().vxb_hop(self.h)
+
+    def decode(self, z: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Host latents [B, latent, T] -> host waveform [B, hop*T] (copies included)."""
+        z = np.ascontiguousarray(z, dtype=np.float32)
+        if z.ndim == 2:
+            z = z[None]
+        B, _, T = z.shape
+        if (B, T) != (self.B, self.T):
+            self.build_plan(B, T)
+        if out is None:
+            out = np.empty((B, self.hop * T), np.float32)
+        check(lib().vxb_decode(self.h, ptr(z), ptr(out)))
+        return out
+
+    def decode_host_ptrs(self, z_ptr: int, out_ptr: int):
+        check(lib().vxb_decode(self.h, z_ptr, out_ptr))
+
+    def decode_device(self, z_dev, out_dev, stream=None):
+        check(lib().vxb_decode_device(self.h, ptr(z_dev), ptr(out_dev), _stream(stream)))
+
+    def sync(self, timeout_ms: int = 60000):
+        check(lib().vxb_sync(self.h, timeout_ms))
+
+    def ops(self) -> list[dict]:
+        """[{name, flops, bytes}] for every launch of the current plan."""
+        out = []
+        for i in range(lib().vxb_plan_num_ops(self.h)):
+            name = ctypes.create_string_buffer(64)
+            fl, by = ctypes.c_double(), ctypes.c_double()
+            check(lib().vxb_plan_op_info(self.h, i, name, 64, ctypes.byref(fl), ctypes.byref(by)))
+            out.append({"name": name.value.decode(), "flops": fl.value, "bytes": by.value})
+        return out
+
+    def time_ops(self, reps: int = 10, flush=None, flush_bytes: int = 0) -> list[float]:
+        n = lib().vxb_plan_num_ops(self.h)
+        ms = (ctypes.c_float * n)()
+        check(lib().vxb_time_ops(self.h, reps, ptr(flush), flush_bytes, ms))
+        return list(ms)
+
+    def debug_stage(self, stage: int, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        check(lib().vxb_debug_stage(self.h, stage, ptr(out), n))
+        return out
+
+
+# ---------------------------------------------------------- single kernels --
+
+def q4_0_dequant(blocks, n: int, out, stream=None):
+    check(lib().vxb_q4_0_dequant(ptr(blocks), n, ptr(out), _stream(stream)))
+
+
+def snake(x, alpha, C: int, N: int, y, stream=None):
+    check(lib().vxb_snake(ptr(x), ptr(alpha), C, N, ptr(y), _stream(stream)))
+
+
+def pointwise(w, w_type: int, K: int, M: int, x16, N: int, bias, y, res=None, snake_alpha=None,
+              out_f16: bool = False, stream=None):
+    check(lib().vxb_pointwise(ptr(w), w_type, K, M, ptr(x16), N, ptr(bias), ptr(res), ptr(snake_alpha),
+                              1 if out_f16 else 0, ptr(y), _stream(stream)))
+
+
+def convt(w, w_type: int, Cin: int, Cout: int, s: int, x16, B: int, T: int, bias, y, stream=None):
+    check(lib().vxb_convt(ptr(w), w_type, Cin, Cout, s, ptr(x16), B, T, ptr(bias), ptr(y), _stream(stream)))

@@ -176,55 +176,86 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 256 : 128, 1)
             uint8_t* a_dst = smem + st * Cfg::kStageBytes;
             const int k0 = kb * Cfg::kBK;
             if (AK == kAQ4K) {
-                // thread t -> row m0 + t, two 32-element blocks along k
+                // thread t -> row m0 + t, two 32-element blocks along k; all
+                // loads of both blocks are issued before any is used.
                 const int m = m0 + t;
+                uint32_t q4[2][4];
+                float dd[2];
 #pragma unroll
                 for (int hb = 0; hb < 2; ++hb) {
                     const int kx = k0 + hb * 32;
-                    __align__(16) __half v[32];
+                    dd[hb] = 0.f;
+                    q4[hb][0] = q4[hb][1] = q4[hb][2] = q4[hb][3] = 0u;
                     if (m < args.M && kx < args.K) {
-                        const uint8_t* blk = args.a_q4 + static_cast<size_t>(m) * args.a_row_bytes + (kx >> 5) * 18;
-                        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
+                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(
+                            args.a_q4 + static_cast<size_t>(m) * args.a_row_bytes + (kx >> 5) * 18);
+                        dd[hb] = half_bits_to_float(__ldg(b16));
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const uint32_t q = __ldg(blk + 2 + j);
-                            v[j] = __float2half_rn(static_cast<float>(static_cast<int>(q & 15u) - 8) * d);
-                            v[j + 16] = __float2half_rn(static_cast<float>(static_cast<int>(q >> 4) - 8) * d);
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = __float2half_rn(0.f);
+                        for (int j = 0; j < 4; ++j)
+                            q4[hb][j] = static_cast<uint32_t>(__ldg(b16 + 1 + 2 * j)) |
+                                        (static_cast<uint32_t>(__ldg(b16 + 2 + 2 * j)) << 16);
                     }
+                }
+#pragma unroll
+                for (int hb = 0; hb < 2; ++hb) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
+                        __align__(16) __half v[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const int j = (c & 1) * 8 + e;
+                            const uint32_t byte = (q4[hb][j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+                            const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
+                            v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * dd[hb]);
+                        }
                         *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
-                            *reinterpret_cast<const uint4*>(&v[c * 8]);
+                            *reinterpret_cast<const uint4*>(v);
                     }
                 }
             } else {
-                // thread t -> k row k0 + t/2, 64 consecutive m of half t&1
-                const int kl = t >> 1, half = t & 1;
-                const int k = k0 + kl;
-                const uint8_t* row = args.a_q4 + static_cast<size_t>(k) * args.a_row_bytes;
+                // Work item = one Q4_0 block (32 consecutive m at one k row)
+                // that intersects the tile's m range [m0, m0 + 128).  m0 is a
+                // multiple of 8, so a block lands on four aligned 16-byte
+                // chunks of the MN-major swizzled tile.
+                const int b_first = m0 >> 5;
+                const int nblk = ((m0 + 127) >> 5) - b_first + 1;  // <= 5
+                const int items = 64 * nblk;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    __align__(16) __half v[8];
+                for (int it = 0; it < 3; ++it) {
+                    const int item = t + it * 128;
+                    if (item >= items) break;
+                    const int kl = item / nblk;
+                    const int blk = b_first + item % nblk;
+                    const int k = k0 + kl;
+                    uint32_t q4[4] = {0u, 0u, 0u, 0u};  // 16 nibble bytes
+                    float d = 0.f;
+                    const bool valid = k < args.K && blk * 32 < args.M;
+                    if (valid) {
+                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(
+                            args.a_q4 + static_cast<size_t>(k) * args.a_row_bytes + static_cast<size_t>(blk) * 18);
+                        d = half_bits_to_float(__ldg(b16));
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int m = m0 + half * 64 + c * 8 + e;
-                        float val = 0.f;
-                        if (k < args.K && m < args.M) {
-                            const uint8_t* blk = row + (m >> 5) * 18;
-                            const int j = m & 31;
-                            const uint32_t q = __ldg(blk + 2 + (j & 15));
-                            const uint32_t nib = j < 16 ? (q & 15u) : (q >> 4);
-                            val = static_cast<float>(static_cast<int>(nib) - 8) *
-                                  half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
-                        }
-                        v[e] = __float2half_rn(val);
+                        for (int j = 0; j < 4; ++j)
+                            q4[j] = static_cast<uint32_t>(__ldg(b16 + 1 + 2 * j)) |
+                                    (static_cast<uint32_t>(__ldg(b16 + 2 + 2 * j)) << 16);
                     }
-                    const uint32_t off = half * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((c ^ kl) & 7) << 4);
-                    *reinterpret_cast<uint4*>(a_dst + off) = *reinterpret_cast<const uint4*>(v);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        // elements 8c..8c+7 of the block: low nibbles for c < 2
+                        const int ml = blk * 32 + c * 8 - m0;
+                        if (ml < 0 || ml >= 128) continue;
+                        __align__(16) __half v[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const int j = (c & 1) * 8 + e;  // byte index 0..15
+                            const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+                            const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
+                            v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
+                        }
+                        const int h = ml >> 6, mc = (ml & 63) >> 3;
+                        const uint32_t off = h * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
+                        *reinterpret_cast<uint4*>(a_dst + off) = *reinterpret_cast<const uint4*>(v);
+                    }
                 }
             }
             fence_proxy_async_smem();
@@ -249,18 +280,23 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 256 : 128, 1)
             const float iv = (mv && args.snake_alpha)
                                  ? (args.snake_inv ? args.snake_inv[m] : 1.0f / (al + 1e-9f))
                                  : 0.f;
+            const float* __restrict__ res = args.res;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
                 if (ok) tmem_ld16(t_row + c0, v);  // .sync.aligned: whole warp
-                if (!mv) continue;
+                const int nb = n_start + c0;
+                if (!mv || nb >= args.N) continue;
+                const int cnt = min(16, args.N - nb);
+                float r[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)  // issue every residual load first
+                    r[i] = (res && i < cnt) ? __ldg(res + static_cast<size_t>(nb + i) * args.M + m) : 0.f;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int n = n_start + c0 + i;
-                    if (n >= args.N) break;
-                    const size_t o = static_cast<size_t>(n) * args.M + m;
-                    float y = v[i] + b;
-                    if (args.res) y += args.res[o];
+                    if (i >= cnt) break;
+                    const size_t o = static_cast<size_t>(nb + i) * args.M + m;
+                    float y = v[i] + b + r[i];
                     if (args.snake_alpha) y = snake(y, al, iv);
                     if (args.out_f16) {
                         static_cast<__half*>(args.out)[o] = __float2half_rn(y);

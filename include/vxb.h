@@ -135,6 +135,25 @@ VXB_API int vxb_plan_op_info(const vxb_ctx* ctx, int idx, char* name, int name_c
  * are overwritten before every rep to evict L2. */
 VXB_API int vxb_time_ops(vxb_ctx* ctx, int reps, void* flush, size_t flush_bytes, float* ms_out);
 
+/* Allocation-free decode, for callers that must not allocate device memory
+ * once they are running: a real-time audio thread (cudaMalloc can stall and
+ * synchronise the device) or a host whose device memory is all owned by
+ * another allocator.  It runs the same kernels as vxb_decode_device, with
+ * z_dev [batch][latent_dim][T] and out_dev [batch][hop*T] in device memory,
+ * but keeps every intermediate activation in one fixed array compiled into
+ * libvxb (5.63 MiB, present on every GPU that loads the library until the
+ * process exits) instead of a plan arena, and calls no allocating routine.
+ * Limit: batch*T <= 8 latent frames for the VoxCPM decoder (1536 channels,
+ * rates 8,8,5,2); larger shapes return VXB_ERR_INVALID_ARGUMENT.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture.  All calls share the
+ * array: calls whose work overlaps on the GPU (other streams, other contexts
+ * on the same device) race and corrupt each other; serialise them.  Enqueued
+ * on `stream` (NULL = the context's stream); completion via vxb_sync or the
+ * stream.  This entry point has no counterpart in the reference, which
+ * always allocates its compute arena (src/backend.cpp:241-287). */
+VXB_API int vxb_decode_static(vxb_ctx* ctx, const float* z_dev, float* out_dev, int batch, int T, void* stream);
+
 /* ---- single-kernel entry points (device pointers, enqueued on `stream`) ---- */
 
 /* Q4_0 blocks -> fp32 ((q - 8) * d), bit-exact with ggml's

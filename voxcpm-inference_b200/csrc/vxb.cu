@@ -927,3 +927,119 @@ extern "C" int vxb_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_byte
     for (size_t i = 0; i < nops; ++i) ms_out[i] = static_cast<float>(acc[i] / reps);
     return check_status(c);
 }
+
+// ------------------------------------------------ allocation-free decode --
+//
+// vxb_decode_static runs the same kernels as a planned decode, but every
+// intermediate activation lives in the fixed device array below instead of
+// a plan arena, so the call itself allocates nothing.
+
+namespace {
+
+// Scratch for vxb_decode_static: two fp32 activation buffers, two fp16
+// GEMM-operand buffers and the device status word.  kStaticFrames latent
+// frames (B*T) of the VoxCPM decoder (1536 channels, rates 8,8,5,2) need
+// 720 KiB each, so the array is 5.63 MiB.  It lives as long as the library
+// is loaded, on every GPU that loads it.
+constexpr int kStaticFrames = 8;
+constexpr size_t kStaticActFloats = size_t(61440) * kStaticFrames;  // largest stage, floats
+constexpr size_t kStaticBytes = 2 * kStaticActFloats * sizeof(float) + 2 * kStaticActFloats * sizeof(__half) + 256;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticBytes];
+
+// Device address of g_static_scratch per device, looked up once.  In host
+// code the symbol is only a host-side stand-in, never a device pointer.
+uint8_t* g_static_ptr[64] = {};
+
+int static_scratch(int dev, uint8_t** out) {
+    if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));
+        g_static_ptr[dev] = static_cast<uint8_t*>(p);
+    }
+    *out = g_static_ptr[dev];
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev, int B, int T, void* stream) {
+    if (!c || !z_dev || !out_dev || B <= 0 || T <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+    if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare first");
+    const int L = c->latent_dim, D = c->decoder_dim;
+    int64_t max_x = int64_t(B) * T * D, max_s = int64_t(B) * T * D;
+    {
+        int64_t n = int64_t(B) * T;
+        int C = D;
+        for (const Block& b : c->blocks) {
+            max_s = std::max(max_s, n * C);
+            n *= b.s;
+            C = b.cout;
+            max_x = std::max(max_x, n * C);
+        }
+    }
+    if (max_x > int64_t(kStaticActFloats) || max_s > int64_t(kStaticActFloats))
+        return fail(VXB_ERR_INVALID_ARGUMENT,
+                    "vxb_decode_static: shape needs " + std::to_string(std::max(max_x, max_s)) +
+                        " activation elements, the static scratch holds " + std::to_string(kStaticActFloats) +
+                        " (B*T <= " + std::to_string(kStaticFrames) + " frames for the VoxCPM decoder)");
+    DeviceGuard g(c->device);
+    uint8_t* base = nullptr;
+    int rc = static_scratch(c->device, &base);
+    if (rc) return rc;
+    float* xa = reinterpret_cast<float*>(base);
+    float* xb = xa + kStaticActFloats;
+    __half* h16 = reinterpret_cast<__half*>(xb + kStaticActFloats);
+    __half* s16 = h16 + kStaticActFloats;
+    int* st = reinterpret_cast<int*>(s16 + kStaticActFloats);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+
+    CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(int), s));  // the status word must start at zero
+    head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z_dev, c->dw0, c->b0.v, h16, B, L, T);
+    CUDA_TRY(cudaGetLastError());
+    GemmOp op;
+    rc = setup_pointwise(&op, c->pw1->dev, c->pw1->type, L, D, h16, int64_t(B) * T, c->b1.v, nullptr,
+                         c->blocks[0].alpha.v, c->blocks[0].alpha.inv, 1, s16, st);
+    if (rc || (rc = op.launch(s))) return rc;
+    int64_t n = int64_t(B) * T;
+    int Tb = T;
+    static const int kDil[3] = {1, 3, 9};
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& b = c->blocks[bi];
+        rc = setup_convt(&op, b.convt->dev, b.convt->type, b.cin, b.cout, b.s, s16, B, Tb, b.bias.v, xa, st);
+        if (rc || (rc = op.launch(s))) return rc;
+        n *= b.s;
+        Tb *= b.s;
+        const int C = b.cout;
+        float* cur = xa;
+        float* nxt = xb;
+        for (int r = 0; r < 3; ++r) {
+            const ResUnit& u = b.ru[r];
+            const int d = kDil[r];
+            dim3 grid((C + 31) / 32, (Tb + kPreTT - 1) / kPreTT, B);
+            res_pre_kernel<<<grid, 256, sizeof(float) * (kPreTT + 6 * d) * 32, s>>>(
+                cur, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h16, C, Tb, d);
+            CUDA_TRY(cudaGetLastError());
+            const bool last_block = bi + 1 == c->blocks.size();
+            if (r < 2) {
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur, nullptr, nullptr, 0,
+                                     nxt, st);
+            } else if (!last_block) {
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur,
+                                     c->blocks[bi + 1].alpha.v, c->blocks[bi + 1].alpha.inv, 1, s16, st);
+            } else {
+                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur, c->final_alpha.v,
+                                     c->final_alpha.inv, 0, nxt, st);
+            }
+            if (rc || (rc = op.launch(s))) return rc;
+            std::swap(cur, nxt);
+        }
+        if (bi + 1 == c->blocks.size()) {
+            final_kernel<<<grid_1d(n * 32, 256), 256, 0, s>>>(cur, c->final_w, c->final_bias, out_dev, C, Tb, n);
+            CUDA_TRY(cudaGetLastError());
+        }
+    }
+    // report a failed bounded wait through vxb_sync (pinned word made at vxb_open)
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, st, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return VXB_OK;
+}

@@ -45,6 +45,7 @@ SIGNATURES = {
     "vxb_decode_device": (_i, [_vp, _vp, _vp, _vp]),
     "vxb_sync": (_i, [_vp, _i]),
     "vxb_debug_stage": (_i, [_vp, _i, _vp, _sz]),
+    "vxb_decode_static": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "vxb_plan_num_ops": (_i, [_vp]),
     "vxb_plan_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_double)]),
@@ -174,6 +175,10 @@ class Decoder:
 
     def decode_device(self, z_dev, out_dev, stream=None):
         check(lib().vxb_decode_device(self.h, ptr(z_dev), ptr(out_dev), _stream(stream)))
+
+    def decode_static(self, z_dev, out_dev, batch: int, T: int, stream=None):
+        """Allocation-free decode (device buffers, static scratch, batch*T <= 8)."""
+        check(lib().vxb_decode_static(self.h, ptr(z_dev), ptr(out_dev), batch, T, _stream(stream)))
 
     def sync(self, timeout_ms: int = 60000):
         check(lib().vxb_sync(self.h, timeout_ms))

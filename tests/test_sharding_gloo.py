@@ -1,0 +1,62 @@
+"""Host-side multi-rank logic of bench.py, on CPU with world_size-2 gloo ranks.
+
+The decode path has no data-path collective: each rank takes its own share of
+the streams (strong scaling) or its own streams (weak scaling), seeded by rank;
+the only collective is the max over ranks of the timed region.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ws, r, local = bench.dist_env()
+    out = {}
+    for w in ("c2", "c4", "c5q"):
+        quant, streams, T, emit, scaling, ar = bench.WORKLOADS[w]
+        per = streams if scaling == "weak" else max(1, streams // ws)
+        z = bench.build_inputs(w, r, per, 2) if T <= 750 else None
+        out[w] = (per, None if z is None else z[0, :, 0, :4].copy())
+    t = torch.tensor([float(rank + 1) * 10.0])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the bench's max-over-ranks of the timed region
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((rank, ws, out, float(t.item())))
+
+
+@pytest.mark.timeout(300)
+def test_two_gloo_ranks_partition_streams_without_exchange():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        rank, ws, out, tmax = q.get(timeout=240)
+        res[rank] = (ws, out, tmax)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][0] == res[1][0] == 2
+    # strong scaling: 256 streams -> 128 per rank; weak: 1 stream per rank
+    assert res[0][1]["c4"][0] == res[1][1]["c4"][0] == 128
+    assert res[0][1]["c2"][0] == 1 and res[0][1]["c5q"][0] == 32
+    # each rank's latents differ (seeded by rank): no rank duplicates another's work
+    assert not np.array_equal(res[0][1]["c2"][1], res[1][1]["c2"][1])
+    # every rank reports the max of the per-rank timings
+    assert res[0][2] == res[1][2] == 20.0

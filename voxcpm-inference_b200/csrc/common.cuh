@@ -99,6 +99,24 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         : "memory");
 }
 
+// Shared -> global tile store (bulk-group completion), and its waits.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(tmap), "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every committed bulk group has completed (writes visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -107,6 +125,22 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
 // (tcgen05.mma reads operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier `id` over one 128-thread epilogue warpgroup.
+__device__ __forceinline__ void epi_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// The same barrier, also OR-ing a predicate: true on every thread if any
+// thread passed true (a uniform bail-out).
+__device__ __forceinline__ bool epi_bar_any(int id, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %2, 0;\n barrier.red.or.pred q, %1, 128, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"(id), "r"(static_cast<uint32_t>(p))
+        : "memory");
+    return r != 0;
 }
 
 // ------------------------------------------------------------------- TMEM --
@@ -195,11 +229,44 @@ __device__ __forceinline__ uint32_t sw128_kmajor_off(uint32_t row, uint32_t k) {
 
 // ------------------------------------------------------------------ math --
 
+// sin(a)^2 by Cody-Waite reduction and a Taylor polynomial (the method the
+// reference's own fused Snake uses, audio-vae.cpp:1216-1247; constants below
+// are derived here from pi and the factorials).  a = q*(pi/2) + r with
+// |r| <= pi/4; sin^2(a) = sin^2(r) for even q and 1 - sin^2(r) for odd q, so
+// only the sine polynomial is needed.  pi/2 is split in three parts, the
+// first with 9 significant bits so that q*hi is exact for |q| < 2^15; beyond
+// |a| = 8192 the library sinf is used.
+constexpr double kHalfPi = 1.57079632679489661923;
+constexpr float kPi2Hi = 1.5703125f;  // 201/128
+constexpr float kPi2Mid = static_cast<float>(kHalfPi - 1.5703125);
+constexpr float kPi2Lo = static_cast<float>(kHalfPi - 1.5703125 - static_cast<double>(kPi2Mid));
+constexpr float kTwoOverPi = static_cast<float>(1.0 / kHalfPi);
+
+__device__ __forceinline__ float sin_sq(float a) {
+    if (fabsf(a) > 8192.f) {
+        const float s = sinf(a);
+        return s * s;
+    }
+    const float q = rintf(a * kTwoOverPi);
+    float r = fmaf(-q, kPi2Hi, a);
+    r = fmaf(-q, kPi2Mid, r);
+    r = fmaf(-q, kPi2Lo, r);
+    const float r2 = r * r;
+    // sin(r) = r (1 - r^2/3! + r^4/5! - ... - r^10/11!), |r| <= pi/4: truncation < 1e-11
+    float p = -1.0f / 39916800.0f;
+    p = fmaf(p, r2, 1.0f / 362880.0f);
+    p = fmaf(p, r2, -1.0f / 5040.0f);
+    p = fmaf(p, r2, 1.0f / 120.0f);
+    p = fmaf(p, r2, -1.0f / 6.0f);
+    const float sr = fmaf(r * r2, p, r);
+    const float s2 = sr * sr;
+    return (static_cast<int>(q) & 1) ? 1.0f - s2 : s2;
+}
+
 // Snake activation (reference audio-vae.cpp:278-289 / :1443-1479):
 // x + sin(alpha*x)^2 * inv, inv = 1 / (alpha + 1e-9).
 __device__ __forceinline__ float snake(float x, float alpha, float inv) {
-    const float s = sinf(alpha * x);
-    return fmaf(s * s, inv, x);
+    return fmaf(sin_sq(alpha * x), inv, x);
 }
 
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) {

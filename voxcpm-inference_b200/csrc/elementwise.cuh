@@ -39,12 +39,16 @@ __global__ void head_kernel(const float* __restrict__ z, const float* __restrict
     }
 }
 
-// Residual-unit prologue.  Block = 32 channels x 8 thread rows; it covers
-// kTT consecutive time steps of one sequence.  The needed input rows
-// [t0 - 6d, t0 + kTT) are loaded once, Snake-activated (snake1) into shared
-// memory, then every output applies the dilated causal taps, bias and
-// snake2, and is stored as fp16.
-constexpr int kPreTT = 32;
+// Residual-unit prologue.  A block covers 64 channels (16 threads x float4)
+// and `tt` (<= kPreTT) time steps of one sequence.  The input rows
+// [t0 - 6d, t0 + tt) are loaded once with 16-byte loads (all of a thread's
+// loads issued before any is used) and Snake-activated (snake1) into shared
+// memory; every output then applies the 7 dilated causal taps, bias and
+// snake2 and is stored as fp16.  Requires C % 4 == 0.
+constexpr int kPreTT = 128;
+constexpr int kPreMaxRows = (kPreTT + 54 + 15) / 16;  // rows per thread for d <= 9
+
+__host__ __device__ constexpr size_t res_pre_smem(int d, int tt = kPreTT) { return sizeof(float) * (tt + 6 * d) * 64; }
 
 __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
                                                       const float* __restrict__ i1,
@@ -52,61 +56,138 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
                                                       const float* __restrict__ bias,
                                                       const float* __restrict__ a2,
                                                       const float* __restrict__ i2, __half* __restrict__ out,
-                                                      int C, int T, int d) {
-    extern __shared__ float sh[];  // [(kPreTT + 6d)][32]
-    const int cx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int c = blockIdx.x * 32 + cx;
-    const int t0 = blockIdx.y * kPreTT;
+                                                      int C, int T, int d, int tt) {
+    extern __shared__ float4 sh4[];  // [(tt + 6d)][16]
+    const int cx = threadIdx.x & 15, ry = threadIdx.x >> 4;  // 16 channel groups x 16 rows
+    const int c = blockIdx.x * 64 + cx * 4;
+    const int t0 = blockIdx.y * tt;
     const int b = blockIdx.z;
     const int halo = 6 * d;
-    const int rows = kPreTT + halo;
+    const int rows = min(tt, T - t0) + halo;
     const bool cv = c < C;
-    const float al1 = cv ? a1[c] : 0.f, iv1 = cv ? i1[c] : 0.f;
     const float* xb = x + static_cast<long long>(b) * T * C;
-    for (int r = ty; r < rows; r += 8) {
+    float4 v[kPreMaxRows];
+#pragma unroll
+    for (int i = 0; i < kPreMaxRows; ++i) {
+        const int r = ry + 16 * i;
         const int t = t0 - halo + r;
-        float v = 0.f;  // causal zero padding (of snake1's output; snake(0) == 0)
-        if (cv && t >= 0 && t < T) v = snake(xb[static_cast<long long>(t) * C + c], al1, iv1);
-        sh[r * 32 + cx] = v;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // causal zero padding (snake(0) == 0)
+        if (cv && r < rows && t >= 0) v[i] = __ldg(reinterpret_cast<const float4*>(xb + static_cast<long long>(t) * C + c));
+    }
+    if (cv) {
+        const float4 al1 = *reinterpret_cast<const float4*>(a1 + c);
+        const float4 iv1 = *reinterpret_cast<const float4*>(i1 + c);
+#pragma unroll
+        for (int i = 0; i < kPreMaxRows; ++i) {
+            const int r = ry + 16 * i;
+            if (r >= rows) break;
+            float4 u = v[i];
+            u.x = snake(u.x, al1.x, iv1.x);
+            u.y = snake(u.y, al1.y, iv1.y);
+            u.z = snake(u.z, al1.z, iv1.z);
+            u.w = snake(u.w, al1.w, iv1.w);
+            sh4[r * 16 + cx] = u;
+        }
     }
     __syncthreads();
     if (!cv) return;
-    float wk[7];
+    float4 wk[7];
 #pragma unroll
-    for (int k = 0; k < 7; ++k) wk[k] = w[c * 7 + k];
-    const float bb = bias[c], al2 = a2[c], iv2 = i2[c];
+    for (int k = 0; k < 7; ++k)
+        wk[k] = make_float4(w[(c + 0) * 7 + k], w[(c + 1) * 7 + k], w[(c + 2) * 7 + k], w[(c + 3) * 7 + k]);
+    const float4 bb = *reinterpret_cast<const float4*>(bias + c);
+    const float4 al2 = *reinterpret_cast<const float4*>(a2 + c);
+    const float4 iv2 = *reinterpret_cast<const float4*>(i2 + c);
     __half* ob = out + static_cast<long long>(b) * T * C;
-    for (int tt = ty; tt < kPreTT; tt += 8) {
-        const int t = t0 + tt;
+    for (int q = ry; q < tt; q += 16) {
+        const int t = t0 + q;
         if (t >= T) break;
-        float acc = bb;
+        float4 acc = bb;
 #pragma unroll
-        for (int k = 0; k < 7; ++k) acc = fmaf(sh[(tt + k * d) * 32 + cx], wk[k], acc);
-        ob[static_cast<long long>(t) * C + c] = __float2half_rn(snake(acc, al2, iv2));
+        for (int k = 0; k < 7; ++k) {
+            const float4 u = sh4[(q + k * d) * 16 + cx];
+            acc.x = fmaf(u.x, wk[k].x, acc.x);
+            acc.y = fmaf(u.y, wk[k].y, acc.y);
+            acc.z = fmaf(u.z, wk[k].z, acc.z);
+            acc.w = fmaf(u.w, wk[k].w, acc.w);
+        }
+        const __half2 h01 = __floats2half2_rn(snake(acc.x, al2.x, iv2.x), snake(acc.y, al2.y, iv2.y));
+        const __half2 h23 = __floats2half2_rn(snake(acc.z, al2.z, iv2.z), snake(acc.w, al2.w, iv2.w));
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&h01);
+        pk.y = *reinterpret_cast<const uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(ob + static_cast<long long>(t) * C + c) = pk;
     }
 }
 
-// Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c]).
-// One warp per output sample; lanes stride over channels.
+// Time tile of res_pre_kernel: the largest of 128/64/32 that still gives at
+// least two blocks per SM.
+inline int res_pre_tt(int C, int T, int B, int sms) {
+    const long long ct = (C + 63) / 64;
+    for (int tt = kPreTT; tt > 32; tt /= 2)
+        if (ct * ((T + tt - 1) / tt) * B >= 2LL * sms) return tt;
+    return 32;
+}
+
+// Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c])
+// over the (already Snake-activated) last stage.  A block covers kFinTT time
+// steps of one sequence: rows [t0 - 6, t0 + kFinTT) are staged in shared
+// memory with 16-byte loads; each warp then reduces one output at a time over
+// channels (lanes) and taps.  Requires C % 4 == 0 and C <= 128.
+constexpr int kFinTT = 64;
+
 __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
-                                                    float bias, float* __restrict__ y, int C, int T,
-                                                    long long total) {
-    const int lane = threadIdx.x & 31;
-    const long long warp_id = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
-    const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
-    for (long long n = warp_id; n < total; n += nwarps) {
-        const int t = static_cast<int>(n % T);
-        float acc = 0.f;
+                                                    float bias, float* __restrict__ y, int C, int T) {
+    extern __shared__ float4 fsh4[];  // [(kFinTT + 6)][C/4]
+    const int c4n = C / 4;
+    const int t0 = blockIdx.x * kFinTT;
+    const int b = blockIdx.y;
+    const int rows = min(kFinTT, T - t0) + 6;
+    const float* sb = s + static_cast<long long>(b) * T * C;
+    constexpr int kMaxLd = ((kFinTT + 6) * 32 + 255) / 256;  // float4 per thread for C <= 128
+    float4 v[kMaxLd];
 #pragma unroll
-        for (int k = 0; k < 7; ++k) {
-            const int st = t + k - 6;
-            if (st < 0) continue;
-            const float* row = s + (n + k - 6) * C;
-            for (int c = lane; c < C; c += 32) acc = fmaf(row[c], w[c * 7 + k], acc);
+    for (int j = 0; j < kMaxLd; ++j) {  // every load issued before any is stored
+        const int i = threadIdx.x + j * 256;
+        const int r = i / c4n, cq = i - r * c4n;
+        const int t = t0 - 6 + r;
+        v[j] = (i < rows * c4n && t >= 0)
+                   ? __ldg(reinterpret_cast<const float4*>(sb + static_cast<long long>(t) * C) + cq)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxLd; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < rows * c4n) fsh4[i] = v[j];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // each lane owns channel quads lane, lane + 32, ... (C <= 128: at most one)
+    float4 wk[7];
+    const bool lv = lane < c4n;
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+        const int cc = lane * 4;
+        wk[k] = lv ? make_float4(w[(cc + 0) * 7 + k], w[(cc + 1) * 7 + k], w[(cc + 2) * 7 + k], w[(cc + 3) * 7 + k])
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int tt = warp; tt < kFinTT; tt += 8) {
+        const int t = t0 + tt;
+        if (t >= T) break;
+        float acc = 0.f;
+        if (lv) {
+#pragma unroll
+            for (int k = 0; k < 7; ++k) {
+                const float4 v = fsh4[(tt + k) * c4n + lane];
+                acc = fmaf(v.x, wk[k].x, acc);
+                acc = fmaf(v.y, wk[k].y, acc);
+                acc = fmaf(v.z, wk[k].z, acc);
+                acc = fmaf(v.w, wk[k].w, acc);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) y[n] = tanhf(acc + bias);
+        if (lane == 0) y[static_cast<long long>(b) * T + t] = tanhf(acc + bias);
     }
 }
 

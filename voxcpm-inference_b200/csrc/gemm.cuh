@@ -1,21 +1,24 @@
 // Implicit-GEMM convolution kernel on the 5th-generation tensor cores.
 //
-// One CTA computes a 128 x BN tile of D = A * B^T with tcgen05.mma
-// (kind::f16, fp16 operands, fp32 accumulator in TMEM):
+// Persistent, warp-specialised: each CTA walks tiles blockIdx.x,
+// blockIdx.x + gridDim.x, ... of D = A * B^T (128 x BN tiles, K steps of 64)
+// with tcgen05.mma (kind::f16: fp16 operands, fp32 accumulator in TMEM):
 //   * A = conv weights (M = output rows, K = input channels), either fp16
-//     through TMA or Q4_0 blocks dequantised to fp16 by producer warps inside
-//     the mainloop; K-major for pointwise convs (the GGUF [Cin, Cout] layout,
-//     rows = Cout) and MN-major for the transposed convs (the folded GGUF
-//     [2s*Cout, Cin] layout, rows = Cin, j = cout*2s + k contiguous).
+//     through TMA or Q4_0 blocks whose raw bytes arrive by TMA and are
+//     dequantised to fp16 in shared memory inside the mainloop; K-major for
+//     pointwise convs (the GGUF [Cin, Cout] layout, rows = Cout) and MN-major
+//     for the transposed convs (the folded GGUF [2s*Cout, Cin] layout,
+//     rows = Cin, j = cout*2s + k contiguous).
 //   * B = activations, fp16 [N tokens][K channels] (K-major), through TMA.
-// The epilogue reads the accumulator with tcgen05.ld and fuses bias, the
-// residual add, the next layer's Snake (fp16 or fp32 output), or, for a
-// transposed conv, the col2im overlap-add of the two taps that land on each
-// output sample plus bias.
+// Two TMEM accumulators let the epilogue of tile i overlap the mainloop of
+// tile i+1.  The epilogue fuses bias, the residual add, the next layer's
+// Snake (fp16 or fp32 output), or, for a transposed conv, the col2im
+// overlap-add of the two taps that land on each output sample plus bias.
 //
 // Warp roles: warp 0 lane 0 issues TMA loads, warp 1 owns TMEM and lane 0
-// issues the MMAs, warps 4-7 (Q4_0 variants only) dequantise A; warps 0-3
-// then run the epilogue (warp w reads TMEM lanes 32w..32w+31).
+// issues the MMAs, warps 4-7 and 8-11 are two epilogue warpgroups (group g
+// drains accumulator g, i.e. every other tile; warp w reads TMEM lanes
+// 32*(w%4)...), warps 12-15 (Q4_0 variants) dequantise A.
 #pragma once
 
 #include <cuda.h>
@@ -27,8 +30,8 @@ namespace vxb {
 enum AKind : int {
     kAF16K = 0,   // fp16, K-major, TMA box {64 k, 128 m}
     kAF16MN = 1,  // fp16, MN-major, two TMA boxes {64 m, 64 k}
-    kAQ4K = 2,    // Q4_0 rows along K (pointwise [Cin, Cout]), dequantised in smem
-    kAQ4MN = 3,   // Q4_0 rows along M (transposed conv [2s*Cout, Cin]), dequantised in smem
+    kAQ4K = 2,    // Q4_0 rows along K (pointwise [Cin, Cout]), raw bytes by TMA, dequantised in smem
+    kAQ4MN = 3,   // Q4_0 rows along M (transposed conv [2s*Cout, Cin]), raw bytes by TMA, dequantised in smem
 };
 
 enum Epi : int {
@@ -38,72 +41,104 @@ enum Epi : int {
 
 struct GemmArgs {
     int M, K, N;              // GEMM extents; M counts A rows of the whole layer
-    const uint8_t* a_q4;      // Q4_0 blocks (kAQ4*), else unused
-    int a_row_bytes;          // bytes per Q4_0 row
+    int m_tiles, n_tiles;     // tile grid (tile t -> m = t % m_tiles, n = t / m_tiles)
     const float* bias;        // [M] (PW) or [Cout] (ConvT)
     const float* res;         // fp32 [N][M] residual or null (PW)
     const float* snake_alpha; // [M] or null (PW)
     const float* snake_inv;   // [M] or null (PW)
     void* out;                // fp32 or fp16 [N][M] (PW); fp32 [N*s][Cout] (ConvT)
     int out_f16;              // PW: 1 = fp16 output
-    int s, cout, cpt, seq_len;  // ConvT: stride, Cout, couts per tile, latent frames per sequence
+    int s, cout, cpt, seq_len;  // ConvT: stride, Cout, couts per tile, frames per sequence
     int* status;              // device status word (bounded-wait failures)
 };
 
-template <int BN>
+// Raw Q4_0 bytes staged per k step: K-major 128 rows x 48 B (two 18-byte
+// blocks from a 16-byte aligned start), MN-major 64 rows x 112 B (up to five
+// blocks covering a 128-wide m range from a 16-byte aligned start).
+constexpr int kRawKBox = 48;
+constexpr int kRawMNBox = 112;
+
+// Pointwise epilogue chunk: tokens per residual load / output store.  The
+// host builds the residual and output tensor maps with boxes of
+// {128 channels, kEpiChunk tokens}.
+constexpr int kEpiChunk = 16;
+constexpr int kBarrierBytes = 512;  // mbarriers + TMEM slot + abort flag
+
+template <int BN, bool Q4, int EPI>
 struct GemmCfg {
     static constexpr int kBM = 128;
     static constexpr int kBK = 64;
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : 6);
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static constexpr int kRawBytes = Q4 ? 7168 : 0;  // max(128*48, 64*112)
+    static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+    static constexpr int kEpiLD = 33;                            // ConvT: staged columns (+1 carry) per row
+    static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
+    static constexpr int kResBytes = kChunk * 128 * 4;           // PW: fp32 [16 tokens][128 channels]
+    static constexpr int kOut16Bytes = kChunk * 128 * 2;         // PW: fp16 [16 tokens][128 channels]
+    static constexpr int kGroupEpiBytes = EPI == kEpiConvT ? 128 * kEpiLD * 4 : 2 * kResBytes + 2 * kOut16Bytes;
+    static constexpr int kEpiBytes = 2 * kGroupEpiBytes;         // two epilogue warpgroups
+    static constexpr int kBudget = 220 * 1024 - kEpiBytes - 1024 - kBarrierBytes;
+    static constexpr int kStagesFit = kBudget / kStageBytes;
+    static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+    static constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);   // two accumulators
+    static constexpr int kAccStride = BN < 32 ? 32 : BN;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
+    static_assert((3 * kStages + 8) * 8 + 8 <= kBarrierBytes, "barrier area too small");
+    static constexpr int kThreads = Q4 ? 512 : 384;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
+    static_assert(kStages >= 2, "pipeline needs two stages");
 };
 
 template <int AK, int BN, int EPI>
-__global__ void __launch_bounds__((AK >= kAQ4K) ? 256 : 128, 1)
+__global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_res, const __grid_constant__ CUtensorMap tmap_out,
                 const GemmArgs args) {
-    using Cfg = GemmCfg<BN>;
-    constexpr int S = Cfg::kStages;
     constexpr bool kQ4 = AK >= kAQ4K;
     constexpr bool kMN = (AK == kAF16MN) || (AK == kAQ4MN);
-    constexpr int kNumDeqWarps = kQ4 ? 4 : 0;
+    using Cfg = GemmCfg<BN, kQ4, EPI>;
+    static_assert(EPI == kEpiConvT || (BN >= 32 && BN <= 128), "pointwise tiles are 32..128 tokens wide");
+    constexpr int S = Cfg::kStages;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-    uint64_t* empty_bar = full_bar + S;
-    uint64_t* accum_bar = empty_bar + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+    float* sE = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + Cfg::kEpiBytes);
+    uint64_t* ready_bar = full_bar + S;   // A tile dequantised (Q4 only)
+    uint64_t* empty_bar = ready_bar + S;  // stage consumed by the MMAs
+    uint64_t* tfull_bar = empty_bar + S;  // accumulator [2] complete
+    uint64_t* tempty_bar = tfull_bar + 2; // accumulator [2] drained
+    uint64_t* res_bar = tempty_bar + 2;   // PW residual chunk [group][2] landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_kb = (args.K + Cfg::kBK - 1) / Cfg::kBK;
-
-    int m0, n_start;
-    if (EPI == kEpiConvT) {
-        m0 = blockIdx.x * (2 * args.s * args.cpt);
-        n_start = blockIdx.y * (BN - 1) - 1;  // column 0 holds token n_first - 1
-    } else {
-        m0 = blockIdx.x * Cfg::kBM;
-        n_start = blockIdx.y * BN;
-    }
+    const int num_tiles = args.m_tiles * args.n_tiles;
+    const int rows_per_tile = EPI == kEpiConvT ? 2 * args.s * args.cpt : Cfg::kBM;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
-            mbar_init(&full_bar[i], 1 + kNumDeqWarps);
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&ready_bar[i], 4);
             mbar_init(&empty_bar[i], 1);
         }
-        mbar_init(accum_bar, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull_bar[i], 1);
+            mbar_init(&tempty_bar[i], 4);
+            mbar_init(&res_bar[2 * i], 1);
+            mbar_init(&res_bar[2 * i + 1], 1);
+        }
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&tmap_b);
-        if (!kQ4) prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_a);
+        if (EPI == kEpiPW) {
+            prefetch_tmap(&tmap_out);
+            if (args.res) prefetch_tmap(&tmap_res);
+        }
     }
     if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tc_fence_before();
@@ -111,235 +146,315 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 256 : 128, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    // ------------------------------------------------------------ roles --
-    if (warp == 0 && lane == 0) {
-        // TMA producer: B always, A for the fp16 kinds.
-        constexpr uint32_t kTx = kQ4 ? Cfg::kBBytes : Cfg::kStageBytes;
-        for (int kb = 0; kb < num_kb; ++kb) {
-            const int st = kb % S;
-            if (!mbar_wait(&empty_bar[st], ((kb / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) break;
-            uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-            uint8_t* b_dst = a_dst + Cfg::kABytes;
-            mbar_arrive_expect_tx(&full_bar[st], kTx);
-            const int k0 = kb * Cfg::kBK;
-            if (AK == kAF16K) {
-                tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
-            } else if (AK == kAF16MN) {
-                tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
-                tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer --
+            constexpr uint32_t kTx = (kQ4 ? 0 : Cfg::kABytes) + Cfg::kBBytes;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+                const int m0 = (tile % args.m_tiles) * rows_per_tile;
+                const int nt = tile / args.m_tiles;
+                const int n_start = EPI == kEpiConvT ? nt * (BN - 1) - 1 : nt * BN;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % S;
+                    if (!mbar_wait(&empty_bar[st], ((it / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty))
+                        break;
+                    uint8_t* a_dst = smem + st * Cfg::kStageBytes;
+                    uint8_t* b_dst = a_dst + Cfg::kABytes;
+                    uint8_t* r_dst = b_dst + Cfg::kBBytes;
+                    const int k0 = kb * Cfg::kBK;
+                    uint32_t tx = kTx;
+                    if (AK == kAQ4K) tx += 128 * kRawKBox;
+                    if (AK == kAQ4MN) tx += 64 * kRawMNBox;
+                    mbar_arrive_expect_tx(&full_bar[st], tx);
+                    if (AK == kAF16K) {
+                        tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
+                    } else if (AK == kAF16MN) {
+                        tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
+                        tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
+                    } else if (AK == kAQ4K) {
+                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], (kb * 36) & ~15, m0);
+                    } else {
+                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], ((m0 >> 5) * 18) & ~15, k0);
+                    }
+                    tma_load_2d(b_dst, &tmap_b, &full_bar[st], k0, n_start);
+                }
             }
-            tma_load_2d(b_dst, &tmap_b, &full_bar[st], k0, n_start);
+            if (*abort_flag) {
+                // Failure path only: give copies already in flight time to land.
+                const unsigned long long t0 = globaltimer_ns();
+                while (globaltimer_ns() - t0 < 1000000ull) {
+                }
+            }
         }
-        if (*abort_flag) {
-            // Failure path only: give copies already in flight time to land
-            // before the CTA's shared memory goes away.
-            const unsigned long long t0 = globaltimer_ns();
-            while (globaltimer_ns() - t0 < 1000000ull) {
-            }
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer.
-        constexpr uint32_t idesc = make_idesc_f16(128, BN, kMN ? 1 : 0);
-        bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
-            const int st = kb % S;
-            if (!mbar_wait(&full_bar[st], (kb / S) & 1, abort_flag, args.status, kErrWaitFull)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + st * Cfg::kStageBytes);
-            const uint32_t b_addr = a_addr + Cfg::kABytes;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------- MMA issuer --
+            constexpr uint32_t idesc = make_idesc_f16(128, BN, kMN ? 1 : 0);
+            int it = 0, tl = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tl) {
+                const int acc = tl & 1;
+                if (!mbar_wait(&tempty_bar[acc], ((tl >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitAccum)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
+                bool ok = true;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % S;
+                    uint64_t* bar = kQ4 ? &ready_bar[st] : &full_bar[st];
+                    if (!mbar_wait(bar, (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + st * Cfg::kStageBytes);
+                    const uint32_t b_addr = a_addr + Cfg::kABytes;
 #pragma unroll
-            for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
-                // K-major SW128: +32 B per 16 k inside the 128-B row.
-                // MN-major SW128: +2 KB per 16 k (two 8-row k groups of 1 KB);
-                // the two 64-element m halves are 8 KB apart (LBO).
-                const uint64_t adesc = kMN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
-                                           : make_sdesc(a_addr + kk * 32, 16, 1024);
-                const uint64_t bdesc = make_sdesc(b_addr + kk * 32, 16, 1024);
-                umma_f16(tmem_base, adesc, bdesc, idesc, (kb | kk) != 0);
+                    for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
+                        // K-major SW128: +32 B per 16 k inside the 128-B row.
+                        // MN-major SW128: +2 KB per 16 k (two 8-row k groups of
+                        // 1 KB); the two 64-element m halves are 8 KB apart (LBO).
+                        const uint64_t adesc = kMN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
+                                                   : make_sdesc(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bdesc = make_sdesc(b_addr + kk * 32, 16, 1024);
+                        umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+                    }
+                    umma_commit(&empty_bar[st]);
+                }
+                // Published even after a failure: the barrier completes once all
+                // issued MMAs are done, so TMEM is idle before it is freed.
+                umma_commit(&tfull_bar[acc]);
+                if (!ok) break;
             }
-            umma_commit(&empty_bar[st]);
         }
-        // Always publish: the accumulator barrier completes once every MMA
-        // issued so far has finished, so TMEM is idle before it is freed even
-        // on the failure path (the epilogue then sees the abort flag).
-        (void)ok;
-        umma_commit(accum_bar);
-    } else if (kQ4 && warp >= 4) {
-        // Q4_0 dequantisers: 128 threads fill the A tile of each stage.
-        const int t = threadIdx.x - 128;
-        for (int kb = 0; kb < num_kb; ++kb) {
-            const int st = kb % S;
-            if (!mbar_wait(&empty_bar[st], ((kb / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) break;
-            uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-            const int k0 = kb * Cfg::kBK;
-            if (AK == kAQ4K) {
-                // thread t -> row m0 + t, two 32-element blocks along k; all
-                // loads of both blocks are issued before any is used.
-                const int m = m0 + t;
-                uint32_t q4[2][4];
-                float dd[2];
+    } else if (kQ4 && warp >= 12) {
+        // ------------------------------------------- Q4_0 dequantisers ------
+        const int t = threadIdx.x - 384;  // 0..127
+        int it = 0;
+        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+            const int m0 = (tile % args.m_tiles) * rows_per_tile;
+            bool ok = true;
+            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                const int st = it % S;
+                if (!mbar_wait(&full_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* a_dst = smem + st * Cfg::kStageBytes;
+                const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
+                const int k0 = kb * Cfg::kBK;
+                if (AK == kAQ4K) {
+                    // thread t -> row m0 + t, two blocks (k0..k0+63) at byte
+                    // offset (36 kb) & 15 of its 48-byte raw row
+                    const int m = m0 + t;
+                    const int off = (kb * 36) & 15;
 #pragma unroll
-                for (int hb = 0; hb < 2; ++hb) {
-                    const int kx = k0 + hb * 32;
-                    dd[hb] = 0.f;
-                    q4[hb][0] = q4[hb][1] = q4[hb][2] = q4[hb][3] = 0u;
-                    if (m < args.M && kx < args.K) {
-                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(
-                            args.a_q4 + static_cast<size_t>(m) * args.a_row_bytes + (kx >> 5) * 18);
-                        dd[hb] = half_bits_to_float(__ldg(b16));
+                    for (int hb = 0; hb < 2; ++hb) {
+                        const bool valid = m < args.M && k0 + hb * 32 < args.K;
+                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(raw + t * kRawKBox + off + hb * 18);
+                        const float d = valid ? half_bits_to_float(b16[0]) : 0.f;
+                        uint32_t q4[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            q4[hb][j] = static_cast<uint32_t>(__ldg(b16 + 1 + 2 * j)) |
-                                        (static_cast<uint32_t>(__ldg(b16 + 2 + 2 * j)) << 16);
+                            q4[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            __align__(16) __half v[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const int j = (c & 1) * 8 + e;
+                                const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+                                const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
+                                v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
+                            }
+                            *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
+                                *reinterpret_cast<const uint4*>(v);
+                        }
+                    }
+                } else {
+                    // work item = (k row, block) of the up-to-five blocks that
+                    // intersect [m0, m0 + 128); m0 is a multiple of 8, so a block
+                    // lands on four aligned 16-byte chunks of the MN-major tile
+                    const int b_first = m0 >> 5;
+                    const int nblk = ((m0 + 127) >> 5) - b_first + 1;
+                    const int base_off = b_first * 18 - ((b_first * 18) & ~15);
+                    const int items = 64 * nblk;
+#pragma unroll
+                    for (int i3 = 0; i3 < 3; ++i3) {
+                        const int item = t + i3 * 128;
+                        if (item >= items) break;
+                        const int kl = item / nblk;
+                        const int bi = item - kl * nblk;
+                        const int blk = b_first + bi;
+                        const bool valid = k0 + kl < args.K && blk * 32 < args.M;
+                        const uint16_t* b16 =
+                            reinterpret_cast<const uint16_t*>(raw + kl * kRawMNBox + base_off + bi * 18);
+                        const float d = valid ? half_bits_to_float(b16[0]) : 0.f;
+                        uint32_t q4[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            q4[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int ml = blk * 32 + c * 8 - m0;
+                            if (ml < 0 || ml >= 128) continue;
+                            __align__(16) __half v[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const int j = (c & 1) * 8 + e;
+                                const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+                                const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
+                                v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
+                            }
+                            const int h = ml >> 6, mc = (ml & 63) >> 3;
+                            const uint32_t off = h * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
+                            *reinterpret_cast<uint4*>(a_dst + off) = *reinterpret_cast<const uint4*>(v);
+                        }
                     }
                 }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready_bar[st]);
+            }
+            if (!ok) break;
+        }
+    } else if (warp >= 4 && warp < 12) {
+        // ------------------------------------------------------ epilogue --
+        const int eg = (warp - 4) >> 2;          // epilogue warpgroup == accumulator it drains
+        const int bar_id = 1 + eg;
+        const int q = warp & 3;                  // TMEM lane quadrant
+        const int row = q * 32 + lane;           // D row of this thread
+        const int et = (threadIdx.x - 128) & 127;  // 0..127 within the group
+        float* sG = sE + eg * (Cfg::kGroupEpiBytes / 4);
+        uint64_t* rbar = res_bar + 2 * eg;
+        int tl = eg;                             // local tile index (this group takes tl = eg, eg+2, ...)
+        int g_chunk = 0;                         // PW chunks processed by this group (buffer parity)
+        for (int tile = blockIdx.x + eg * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, tl += 2) {
+            const int acc = eg;
+            bool ok = mbar_wait(&tfull_bar[acc], (tl >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
+            ok = !epi_bar_any(bar_id, !ok || *abort_flag != 0);  // uniform over the group
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + acc * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
+            const int mt = tile % args.m_tiles;
+            const int nt = tile / args.m_tiles;
+            if (EPI == kEpiPW) {
+                // Chunks of 16 tokens: the residual chunk arrives by TMA into
+                // one of two buffers (the next chunk's load is issued before
+                // this one is processed), the result is written in place
+                // (fp32) or to the fp16 buffer, and a TMA store sends it out.
+                const int m0 = mt * Cfg::kBM;
+                const int m = m0 + row;
+                const int n_start = nt * BN;
+                const bool mv = m < args.M;
+                const float b = mv ? args.bias[m] : 0.f;
+                const float al = (mv && args.snake_alpha) ? args.snake_alpha[m] : 0.f;
+                const float iv = (mv && args.snake_alpha)
+                                     ? (args.snake_inv ? args.snake_inv[m] : 1.0f / (al + 1e-9f))
+                                     : 0.f;
+                const bool has_res = args.res != nullptr;
+                const int nch = min(BN / Cfg::kChunk, (args.N - n_start + Cfg::kChunk - 1) / Cfg::kChunk);
+                auto issue_res = [&](int ch, int gidx) {
+                    const int j = gidx & 1;
+                    bulk_wait_read<0>();  // no store may still read the buffer being refilled
+                    mbar_arrive_expect_tx(&rbar[j], Cfg::kResBytes);
+                    tma_load_2d(sG + j * (Cfg::kResBytes / 4), &tmap_res, &rbar[j], m0, n_start + ch * Cfg::kChunk);
+                };
+                if (has_res && et == 0 && nch > 0) issue_res(0, g_chunk);
+#pragma unroll 1
+                for (int ch = 0; ch < nch; ++ch, ++g_chunk) {
+                    const int j = g_chunk & 1;
+                    if (has_res && et == 0 && ch + 1 < nch) issue_res(ch + 1, g_chunk + 1);
+                    float v[16];
+                    tmem_ld16(t_row + ch * Cfg::kChunk, v);
+                    float* rbuf = sG + j * (Cfg::kResBytes / 4);
+                    __half* obuf = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sG) + 2 * Cfg::kResBytes +
+                                                             j * Cfg::kOut16Bytes);
+                    bool w_ok = true;
+                    if (has_res) {
+                        w_ok = mbar_wait(&rbar[j], (g_chunk >> 1) & 1, abort_flag, args.status, kErrWaitFull);
+                    } else {
+                        if (et == 0) bulk_wait_read<1>();  // the store that last used buffer j has read it
+                        epi_bar(bar_id);
+                    }
+                    if (w_ok) {
+                        float r[16];
 #pragma unroll
-                for (int hb = 0; hb < 2; ++hb) {
+                        for (int i = 0; i < 16; ++i) r[i] = has_res ? rbuf[i * 128 + row] : 0.f;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        __align__(16) __half v[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const int j = (c & 1) * 8 + e;
-                            const uint32_t byte = (q4[hb][j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-                            const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
-                            v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * dd[hb]);
+                        for (int i = 0; i < 16; ++i) {
+                            float y = v[i] + b + r[i];
+                            if (args.snake_alpha) y = snake(y, al, iv);
+                            if (args.out_f16) {
+                                obuf[i * 128 + row] = __float2half_rn(y);
+                            } else {
+                                rbuf[i * 128 + row] = y;
+                            }
                         }
-                        *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
-                            *reinterpret_cast<const uint4*>(v);
+                    }
+                    fence_proxy_async_smem();
+                    if (epi_bar_any(bar_id, !w_ok)) {  // uniform: some thread's residual never landed
+                        ok = false;
+                        break;
+                    }
+                    if (et == 0) {
+                        tma_store_2d(&tmap_out, args.out_f16 ? static_cast<const void*>(obuf) : rbuf, m0,
+                                     n_start + ch * Cfg::kChunk);
+                        bulk_commit();
                     }
                 }
             } else {
-                // Work item = one Q4_0 block (32 consecutive m at one k row)
-                // that intersects the tile's m range [m0, m0 + 128).  m0 is a
-                // multiple of 8, so a block lands on four aligned 16-byte
-                // chunks of the MN-major swizzled tile.
-                const int b_first = m0 >> 5;
-                const int nblk = ((m0 + 127) >> 5) - b_first + 1;  // <= 5
-                const int items = 64 * nblk;
-#pragma unroll
-                for (int it = 0; it < 3; ++it) {
-                    const int item = t + it * 128;
-                    if (item >= items) break;
-                    const int kl = item / nblk;
-                    const int blk = b_first + item % nblk;
-                    const int k = k0 + kl;
-                    uint32_t q4[4] = {0u, 0u, 0u, 0u};  // 16 nibble bytes
-                    float d = 0.f;
-                    const bool valid = k < args.K && blk * 32 < args.M;
-                    if (valid) {
-                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(
-                            args.a_q4 + static_cast<size_t>(k) * args.a_row_bytes + static_cast<size_t>(blk) * 18);
-                        d = half_bits_to_float(__ldg(b16));
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            q4[j] = static_cast<uint32_t>(__ldg(b16 + 1 + 2 * j)) |
-                                    (static_cast<uint32_t>(__ldg(b16 + 2 + 2 * j)) << 16);
-                    }
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        // elements 8c..8c+7 of the block: low nibbles for c < 2
-                        const int ml = blk * 32 + c * 8 - m0;
-                        if (ml < 0 || ml >= 128) continue;
-                        __align__(16) __half v[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const int j = (c & 1) * 8 + e;  // byte index 0..15
-                            const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-                            const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
-                            v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
-                        }
-                        const int h = ml >> 6, mc = (ml & 63) >> 3;
-                        const uint32_t off = h * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
-                        *reinterpret_cast<uint4*>(a_dst + off) = *reinterpret_cast<const uint4*>(v);
-                    }
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full_bar[st]);
-        }
-    }
-
-    // ----------------------------------------------------------- epilogue --
-    if (warp < 4) {
-        __syncwarp();
-        bool ok = mbar_wait(accum_bar, 0, abort_flag, args.status, kErrWaitAccum);
-        ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);  // tcgen05.ld needs a uniform warp
-        tc_fence_after();
-        const int row = warp * 32 + lane;  // D row == TMEM lane
-        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-        if (EPI == kEpiPW) {
-            const int m = m0 + row;
-            const bool mv = ok && m < args.M;
-            const float b = mv ? args.bias[m] : 0.f;
-            const float al = (mv && args.snake_alpha) ? args.snake_alpha[m] : 0.f;
-            const float iv = (mv && args.snake_alpha)
-                                 ? (args.snake_inv ? args.snake_inv[m] : 1.0f / (al + 1e-9f))
-                                 : 0.f;
-            const float* __restrict__ res = args.res;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float v[16];
-                if (ok) tmem_ld16(t_row + c0, v);  // .sync.aligned: whole warp
-                const int nb = n_start + c0;
-                if (!mv || nb >= args.N) continue;
-                const int cnt = min(16, args.N - nb);
-                float r[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i)  // issue every residual load first
-                    r[i] = (res && i < cnt) ? __ldg(res + static_cast<size_t>(nb + i) * args.M + m) : 0.f;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (i >= cnt) break;
-                    const size_t o = static_cast<size_t>(nb + i) * args.M + m;
-                    float y = v[i] + b + r[i];
-                    if (args.snake_alpha) y = snake(y, al, iv);
-                    if (args.out_f16) {
-                        static_cast<__half*>(args.out)[o] = __float2half_rn(y);
-                    } else {
-                        static_cast<float*>(args.out)[o] = y;
-                    }
-                }
-            }
-        } else {
-            // ConvT: stage D (fp32) in the now idle pipeline smem, then
-            // overlap-add the two taps of every output sample.
-            constexpr int LD = BN + 1;
-            float* sD = reinterpret_cast<float*>(smem);
-            if (ok) {
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(t_row + c0, v);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) sD[row * LD + c0 + i] = v[i];
-                }
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (ok) {
+                // ConvT: 32-column chunks staged in smem with one carried
+                // column (the previous token), then each thread emits the
+                // outputs of one (phase r, cout) pair for every group-th token.
                 const int s = args.s;
-                const int co_lo = blockIdx.x * args.cpt;
+                const int co_lo = mt * args.cpt;
                 const int cpt = min(args.cpt, args.cout - co_lo);
-                const int n_first = n_start + 1;
-                const int n_tok = min(BN - 1, args.N - n_first);
-                const int total = n_tok * s * cpt;
+                const int n_start = nt * (BN - 1) - 1;  // token of D column 0
+                const int npairs = s * args.cpt;        // <= 128
+                const int groups = 128 / npairs;
+                const int pair = et % npairs, grp = et / npairs;
+                const int r = pair / args.cpt, co_l = pair - (pair / args.cpt) * args.cpt;
+                const bool active = grp < groups && co_l < cpt;
+                const float bias = active ? args.bias[co_lo + co_l] : 0.f;
+                const int rowA = (co_l * 2 * s + r) * Cfg::kEpiLD;
+                const int rowB = rowA + s * Cfg::kEpiLD;
                 float* out = static_cast<float*>(args.out);
-                for (int idx = threadIdx.x; idx < total; idx += 128) {
-                    const int co_l = idx % cpt;
-                    const int rest = idx / cpt;
-                    const int r = rest % s;
-                    const int nn = rest / s;
-                    const int n = n_first + nn;
-                    float y = sD[(co_l * 2 * s + r) * LD + nn + 1] + args.bias[co_lo + co_l];
-                    if (n % args.seq_len != 0) y += sD[(co_l * 2 * s + s + r) * LD + nn];
-                    out[(static_cast<size_t>(n) * s + r) * args.cout + co_lo + co_l] = y;
+                float carry = 0.f;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld16(t_row + c0, v);
+                    tmem_ld16(t_row + c0 + 16, v + 16);
+                    sG[row * Cfg::kEpiLD] = carry;  // column c0 - 1
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sG[row * Cfg::kEpiLD + 1 + j] = v[j];
+                    carry = v[31];
+                    epi_bar(bar_id);
+                    if (active) {
+                        // output columns c in [c0, min(c0+32, BN)) with c >= 1; token n = n_start + c
+                        const int c_end = min(c0 + 32, BN);
+                        int c = c0 + grp;
+                        int n = n_start + c;
+                        int tpos = (n % args.seq_len + args.seq_len) % args.seq_len;
+                        for (; c < c_end; c += groups, n += groups) {
+                            if (c >= 1 && n < args.N) {
+                                float y = sG[rowA + (c - c0) + 1] + bias;
+                                if (tpos != 0) y += sG[rowB + (c - c0)];
+                                out[(static_cast<size_t>(n) * s + r) * args.cout + co_lo + co_l] = y;
+                            }
+                            tpos += groups;
+                            while (tpos >= args.seq_len) tpos -= args.seq_len;
+                        }
+                    }
+                    epi_bar(bar_id);
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (!ok) break;
         }
+        if (EPI == kEpiPW && et == 0) bulk_wait_all();  // stores done before the CTA's smem goes away
     }
 
     tc_fence_before();

@@ -80,6 +80,62 @@ int make_tmap_f16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t out
     return VXB_OK;
 }
 
+// 2-D fp32 / fp16 tensor [outer][inner] without swizzle (epilogue tiles).
+int make_tmap_plain(CUtensorMap* m, const void* base, bool f16, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                    uint32_t box_outer) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    const uint64_t row_bytes = inner * (f16 ? 2 : 4);
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "epilogue tensor needs 16-byte aligned base and rows");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (plain) failed: " + std::to_string(r));
+    return VXB_OK;
+}
+
+// 2-D byte tensor [rows][pitch] (no swizzle), for the raw Q4_0 blocks.
+int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t pitch, uint64_t rows, uint32_t box_inner,
+                 uint32_t box_outer) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch & 15))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 rows must be padded to 16 bytes for TMA");
+    const cuuint64_t dims[2] = {pitch, rows};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (u8) failed: " + std::to_string(r));
+    return VXB_OK;
+}
+
+int num_sms(int dev) {
+    static int cache[64] = {};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// A conv weight as a GEMM operand: fp16 bytes, or Q4_0 blocks in rows padded
+// to `pitch` bytes (a multiple of 16, for TMA).
+struct WView {
+    const void* p = nullptr;
+    int type = 0;
+    int pitch = 0;
+};
+
 // --------------------------------------------------------------- launching --
 
 int pick_bn(int64_t n) {
@@ -91,9 +147,10 @@ int pick_bn(int64_t n) {
 }
 
 template <int AK, int BN, int EPI>
-int launch_gemm_t(dim3 grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
-    constexpr int smem = GemmCfg<BN>::kSmemBytes;
-    constexpr int threads = AK >= kAQ4K ? 256 : 128;
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const CUtensorMap& to,
+                  const GemmArgs& a, cudaStream_t st) {
+    constexpr int smem = GemmCfg<BN, (AK >= kAQ4K), EPI>::kSmemBytes;
+    constexpr int threads = GemmCfg<BN, (AK >= kAQ4K), EPI>::kThreads;
     static bool attr[64] = {};  // per device
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev));
@@ -102,20 +159,26 @@ int launch_gemm_t(dim3 grid, const CUtensorMap& ta, const CUtensorMap& tb, const
         CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<AK, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr[dev] = true;
     }
-    gemm_kernel<AK, BN, EPI><<<grid, threads, smem, st>>>(ta, tb, a);
+    const int tiles = a.m_tiles * a.n_tiles;
+    dim3 g(std::max(1, std::min(tiles, num_sms(dev))));
+    gemm_kernel<AK, BN, EPI><<<g, threads, smem, st>>>(ta, tb, tr, to, a);
     CUDA_TRY(cudaGetLastError());
     return VXB_OK;
 }
 
 template <int AK, int EPI>
-int launch_gemm_bn(int bn, dim3 grid, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                   cudaStream_t st) {
+int launch_gemm_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr,
+                   const CUtensorMap& to, const GemmArgs& a, cudaStream_t st) {
     switch (bn) {
-        case 16: return launch_gemm_t<AK, 16, EPI>(grid, ta, tb, a, st);
-        case 32: return launch_gemm_t<AK, 32, EPI>(grid, ta, tb, a, st);
-        case 64: return launch_gemm_t<AK, 64, EPI>(grid, ta, tb, a, st);
-        case 128: return launch_gemm_t<AK, 128, EPI>(grid, ta, tb, a, st);
-        case 256: return launch_gemm_t<AK, 256, EPI>(grid, ta, tb, a, st);
+        case 16:
+            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 16, EPI>(ta, tb, tr, to, a, st);
+            return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise tiles are at least 32 wide");
+        case 32: return launch_gemm_t<AK, 32, EPI>(ta, tb, tr, to, a, st);
+        case 64: return launch_gemm_t<AK, 64, EPI>(ta, tb, tr, to, a, st);
+        case 128: return launch_gemm_t<AK, 128, EPI>(ta, tb, tr, to, a, st);
+        case 256:
+            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 256, EPI>(ta, tb, tr, to, a, st);
+            return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise tiles are at most 128 wide");
         default: return fail(VXB_ERR_INVALID_ARGUMENT, "bad BN");
     }
 }
@@ -124,36 +187,44 @@ int launch_gemm_bn(int bn, dim3 grid, const CUtensorMap& ta, const CUtensorMap& 
 struct GemmOp {
     int akind = 0, epi = 0, bn = 16;
     dim3 grid;
-    CUtensorMap ta{}, tb{};
+    CUtensorMap ta{}, tb{}, tr{}, to{};
     GemmArgs args{};
     int launch(cudaStream_t st) const {
         switch (akind * 2 + epi) {
-            case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, grid, ta, tb, args, st);
-            case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, grid, ta, tb, args, st);
-            case kAF16MN * 2 + kEpiConvT: return launch_gemm_bn<kAF16MN, kEpiConvT>(bn, grid, ta, tb, args, st);
-            case kAQ4MN * 2 + kEpiConvT: return launch_gemm_bn<kAQ4MN, kEpiConvT>(bn, grid, ta, tb, args, st);
+            case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, ta, tb, tr, to, args, st);
+            case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, ta, tb, tr, to, args, st);
+            case kAF16MN * 2 + kEpiConvT: return launch_gemm_bn<kAF16MN, kEpiConvT>(bn, ta, tb, tr, to, args, st);
+            case kAQ4MN * 2 + kEpiConvT: return launch_gemm_bn<kAQ4MN, kEpiConvT>(bn, ta, tb, tr, to, args, st);
             default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported GEMM kind");
         }
     }
 };
 
-// Pointwise conv GEMM: W [M rows][K] (F16 or Q4_0), x fp16 [N][K].
-int setup_pointwise(GemmOp* op, const void* w, int w_type, int K, int M, const void* x16, int64_t N,
-                    const float* bias, const float* res, const float* alpha, const float* inv, int out_f16,
-                    void* out, int* status) {
+// Pointwise conv GEMM: W [M rows][K] (F16, or Q4_0 rows padded to w.pitch), x fp16 [N][K].
+int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t N, const float* bias,
+                    const float* res, const float* alpha, const float* inv, int out_f16, void* out, int* status) {
     if (K <= 0 || M <= 0 || N <= 0 || N > (int64_t(1) << 31) - 1)
         return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: bad extents");
     if (K % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: K must be a multiple of 8");
     op->epi = kEpiPW;
-    op->bn = pick_bn(N);
-    op->grid = dim3((M + 127) / 128, static_cast<unsigned>((N + op->bn - 1) / op->bn));
+    op->bn = std::max(32, std::min(128, pick_bn(N)));
+    op->grid = dim3(1);
     int rc = make_tmap_f16(&op->tb, x16, K, N, uint64_t(K) * 2, 64, op->bn);
     if (rc) return rc;
+    // epilogue tiles: [kEpiChunk tokens][128 channels] of the residual (fp32) and output
+    if ((rc = make_tmap_plain(&op->to, out, out_f16 != 0, M, N, 128, kEpiChunk))) return rc;
+    if (res) {
+        if ((rc = make_tmap_plain(&op->tr, res, false, M, N, 128, kEpiChunk))) return rc;
+    } else {
+        op->tr = op->to;
+    }
     GemmArgs& a = op->args;
     a = GemmArgs{};
     a.M = M;
     a.K = K;
     a.N = static_cast<int>(N);
+    a.m_tiles = (M + 127) / 128;
+    a.n_tiles = static_cast<int>((N + op->bn - 1) / op->bn);
     a.bias = bias;
     a.res = res;
     a.snake_alpha = alpha;
@@ -161,20 +232,17 @@ int setup_pointwise(GemmOp* op, const void* w, int w_type, int K, int M, const v
     a.out = out;
     a.out_f16 = out_f16;
     a.status = status;
-    if (w_type == VXB_TYPE_F16) {
+    if (w.type == VXB_TYPE_F16) {
         op->akind = kAF16K;
-        rc = make_tmap_f16(&op->ta, w, K, M, uint64_t(K) * 2, 64, 128);
-        if (rc) return rc;
-    } else if (w_type == VXB_TYPE_Q4_0) {
+        rc = make_tmap_f16(&op->ta, w.p, K, M, uint64_t(K) * 2, 64, 128);
+    } else if (w.type == VXB_TYPE_Q4_0) {
         if (K % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 pointwise needs K % 32 == 0");
         op->akind = kAQ4K;
-        op->ta = op->tb;  // unused by the Q4_0 kernels
-        a.a_q4 = static_cast<const uint8_t*>(w);
-        a.a_row_bytes = K / 32 * 18;
+        rc = make_tmap_u8(&op->ta, w.p, w.pitch, M, kRawKBox, 128);
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: weight type must be F16 or Q4_0");
     }
-    return VXB_OK;
+    return rc;
 }
 
 // Couts per transposed-conv tile: 2s*cpt rows <= 128 and a multiple of 8
@@ -185,9 +253,10 @@ int convt_cpt(int s) {
     return 0;
 }
 
-// Transposed conv GEMM: W folded [Cin rows][2s*Cout] (F16 or Q4_0), x fp16 [B*T][Cin].
-int setup_convt(GemmOp* op, const void* w, int w_type, int Cin, int Cout, int s, const void* x16, int B, int T,
-                const float* bias, float* y, int* status) {
+// Transposed conv GEMM: W folded [Cin rows][2s*Cout] (F16, or Q4_0 rows padded
+// to w.pitch), x fp16 [B*T][Cin].
+int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, int B, int T, const float* bias,
+                float* y, int* status) {
     const int64_t N = int64_t(B) * T;
     if (Cin <= 0 || Cout <= 0 || s <= 0 || s > 32 || N <= 0 || N * s > (int64_t(1) << 31) - 1)
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad extents");
@@ -197,14 +266,17 @@ int setup_convt(GemmOp* op, const void* w, int w_type, int Cin, int Cout, int s,
     if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");
     op->epi = kEpiConvT;
     op->bn = pick_bn(N + 1);
-    op->grid = dim3((Cout + cpt - 1) / cpt, static_cast<unsigned>((N + op->bn - 2) / (op->bn - 1)));
+    op->grid = dim3(1);
     int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, op->bn);
     if (rc) return rc;
+    op->tr = op->to = op->tb;  // unused by the transposed-conv epilogue
     GemmArgs& a = op->args;
     a = GemmArgs{};
     a.M = M;
     a.K = Cin;
     a.N = static_cast<int>(N);
+    a.m_tiles = (Cout + cpt - 1) / cpt;
+    a.n_tiles = static_cast<int>((N + op->bn - 2) / (op->bn - 1));
     a.bias = bias;
     a.out = y;
     a.s = s;
@@ -212,21 +284,18 @@ int setup_convt(GemmOp* op, const void* w, int w_type, int Cin, int Cout, int s,
     a.cpt = cpt;
     a.seq_len = T;
     a.status = status;
-    if (w_type == VXB_TYPE_F16) {
+    if (w.type == VXB_TYPE_F16) {
         if ((uint64_t(M) * 2) % 16) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: 2s*Cout must be a multiple of 8");
         op->akind = kAF16MN;
-        rc = make_tmap_f16(&op->ta, w, M, Cin, uint64_t(M) * 2, 64, 64);
-        if (rc) return rc;
-    } else if (w_type == VXB_TYPE_Q4_0) {
+        rc = make_tmap_f16(&op->ta, w.p, M, Cin, uint64_t(M) * 2, 64, 64);
+    } else if (w.type == VXB_TYPE_Q4_0) {
         if (M % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 convt needs 2s*Cout % 32 == 0");
         op->akind = kAQ4MN;
-        op->ta = op->tb;
-        a.a_q4 = static_cast<const uint8_t*>(w);
-        a.a_row_bytes = M / 32 * 18;
+        rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kRawMNBox, 64);
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: weight type must be F16 or Q4_0");
     }
-    return VXB_OK;
+    return rc;
 }
 
 int grid_1d(int64_t work, int threads) {
@@ -253,9 +322,12 @@ struct DevTensor {
     int type = 0;
     int n_dims = 0;
     int64_t ne[4] = {1, 1, 1, 1};
-    void* dev = nullptr;
+    void* dev = nullptr;     // the GGUF bytes, unchanged
     size_t nbytes = 0;
+    void* q4pad = nullptr;   // Q4_0 GEMM weights: same blocks, rows padded to 16 B (made by vxb_prepare)
+    int q4pitch = 0;
     int64_t nelem() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
+    WView view() const { return type == VXB_TYPE_Q4_0 ? WView{q4pad, type, q4pitch} : WView{dev, type, 0}; }
 };
 
 struct Vec {  // derived fp32 vector (+ inverse for Snake alphas)
@@ -387,7 +459,10 @@ int vxb_close(vxb_ctx* c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
     if (c->plan) free_plan(c->plan.get());
-    for (auto& kv : c->tensors) cudaFree(kv.second.dev);
+    for (auto& kv : c->tensors) {
+        cudaFree(kv.second.dev);
+        cudaFree(kv.second.q4pad);
+    }
     for (void* p : c->derived_allocs) cudaFree(p);
     cudaFree(c->status);
     cudaFreeHost(c->status_host);
@@ -432,7 +507,10 @@ int vxb_upload_tensor(vxb_ctx* c, const char* name, int type, const int64_t* ne,
     CUDA_TRY(cudaMalloc(&t.dev, nbytes));
     CUDA_TRY(cudaMemcpy(t.dev, host, nbytes, cudaMemcpyHostToDevice));
     auto it = c->tensors.find(t.name);
-    if (it != c->tensors.end()) cudaFree(it->second.dev);
+    if (it != c->tensors.end()) {
+        cudaFree(it->second.dev);
+        cudaFree(it->second.q4pad);
+    }
     c->tensors[t.name] = t;
     c->prepared = false;
     return VXB_OK;
@@ -513,12 +591,26 @@ int derive_taps(vxb_ctx* c, const std::string& name, int C, float** out) {
     return rc;
 }
 
+// Binds a conv weight used as a GEMM operand ([outer rows][inner]); for Q4_0
+// it also makes the TMA-friendly copy: the same 18-byte blocks, every row
+// padded with zeros to a multiple of 16 bytes.
 int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t outer, const DevTensor** out) {
-    const DevTensor* t = get(c, name);
-    if (!t) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
+    auto it = c->tensors.find(name);
+    if (it == c->tensors.end()) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
+    DevTensor* t = &it->second;
     if (t->type != VXB_TYPE_F16 && t->type != VXB_TYPE_Q4_0)
         return fail(VXB_ERR_INVALID_FORMAT, name + ": conv weights must be F16 or Q4_0");
     if (t->nelem() != inner * outer) return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
+    if (t->type == VXB_TYPE_Q4_0) {
+        if (inner % 32) return fail(VXB_ERR_INVALID_FORMAT, name + ": Q4_0 rows must hold whole blocks");
+        const size_t row = size_t(inner) / 32 * 18, pitch = (row + 15) / 16 * 16;
+        cudaFree(t->q4pad);
+        t->q4pad = nullptr;
+        CUDA_TRY(cudaMalloc(&t->q4pad, pitch * outer));
+        CUDA_TRY(cudaMemsetAsync(t->q4pad, 0, pitch * outer, c->stream));
+        CUDA_TRY(cudaMemcpy2DAsync(t->q4pad, pitch, t->dev, row, row, outer, cudaMemcpyDeviceToDevice, c->stream));
+        t->q4pitch = static_cast<int>(pitch);
+    }
     *out = t;
     return VXB_OK;
 }
@@ -573,6 +665,9 @@ extern "C" int vxb_prepare(vxb_ctx* c) {
         c->blocks.push_back(b);
         C /= 2;
     }
+    // channel counts: 16-byte vectors in the elementwise kernels, TMA rows in the GEMMs
+    if (C % 8 || C > 128 || L % 8)
+        return fail(VXB_ERR_INVALID_FORMAT, "decoder channels must be multiples of 8 and the last stage <= 128");
     const int nb = static_cast<int>(c->rates.size());
     if ((rc = derive_vec(c, p + std::to_string(nb + 2) + ".alpha", C, true, &c->final_alpha))) return rc;
     if ((rc = derive_taps(c, p + std::to_string(nb + 3) + ".weight", C, &c->final_w))) return rc;
@@ -637,7 +732,7 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
         P.gemms.emplace_back();
         GemmOp& op = P.gemms.back();
         const Block& b0 = c->blocks[0];
-        rc = setup_pointwise(&op, c->pw1->dev, c->pw1->type, L, D, P.h16, int64_t(B) * T, c->b1.v, nullptr,
+        rc = setup_pointwise(&op, c->pw1->view(), L, D, P.h16, int64_t(B) * T, c->b1.v, nullptr,
                              b0.alpha.v, b0.alpha.inv, 1, P.s16, st);
         if (rc) return rc;
     }
@@ -653,7 +748,7 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
         const Block& b = c->blocks[bi];
         // transposed conv: s16 [n][cin] -> xa [n*s][cout]
         P.gemms.emplace_back();
-        rc = setup_convt(&P.gemms.back(), b.convt->dev, b.convt->type, b.cin, b.cout, b.s, P.s16, B, Tb, b.bias.v,
+        rc = setup_convt(&P.gemms.back(), b.convt->view(), b.cin, b.cout, b.s, P.s16, B, Tb, b.bias.v,
                          P.xa, st);
         if (rc) return rc;
         P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
@@ -675,11 +770,11 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
                 const float* x = cur;
                 __half* h = P.h16;
                 const int Bq = B, Tq = Tb;
+                const int tt = res_pre_tt(C, Tq, Bq, num_sms(c->device));
                 P.ops.push_back([=](cudaStream_t s) {
-                    dim3 grid((C + 31) / 32, (Tq + kPreTT - 1) / kPreTT, Bq);
-                    const size_t sm = sizeof(float) * (kPreTT + 6 * d) * 32;
-                    res_pre_kernel<<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C,
-                                                         Tq, d);
+                    dim3 grid((C + 63) / 64, (Tq + tt - 1) / tt, Bq);
+                    res_pre_kernel<<<grid, 256, res_pre_smem(d, tt), s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
+                                                                          u.a2.inv, h, C, Tq, d, tt);
                     return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
                 });
                 P.info.push_back({"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r),
@@ -690,15 +785,15 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
             const bool last_unit = r == 2;
             const bool last_block = bi + 1 == c->blocks.size();
             if (!last_unit) {
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, nullptr, nullptr, 0,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, nullptr, nullptr, 0,
                                      nxt, st);
                 P.stage_buf[stage0 + 1 + r] = {nxt, size_t(n) * C, P.ops.size()};
             } else if (!last_block) {
                 const Block& nb = c->blocks[bi + 1];
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, nb.alpha.v,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, nb.alpha.v,
                                      nb.alpha.inv, 1, P.s16, st);
             } else {
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, P.h16, n, u.pb.v, cur, c->final_alpha.v,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, c->final_alpha.v,
                                      c->final_alpha.inv, 0, nxt, st);
             }
             if (rc) return rc;
@@ -714,10 +809,10 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
             float* o = P.out;
             const float* w = c->final_w;
             const float fb = c->final_bias;
-            const int Tq = Tb;
-            const int64_t total = n;
+            const int Tq = Tb, Bq = B;
             P.ops.push_back([=](cudaStream_t s) {
-                final_kernel<<<grid_1d(total * 32, 256), 256, 0, s>>>(sx, w, fb, o, C, Tq, total);
+                dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
+                final_kernel<<<grid, 256, sizeof(float) * (kFinTT + 6) * C, s>>>(sx, w, fb, o, C, Tq);
                 return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
             });
             P.info.push_back({"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4});
@@ -860,23 +955,63 @@ extern "C" int vxb_snake(const float* x, const float* alpha, int C, int64_t N, f
     return VXB_OK;
 }
 
+namespace {
+
+// Unit entry points receive the GGUF bytes as they are; a Q4_0 weight whose
+// rows are not a multiple of 16 bytes gets a stream-ordered padded copy.
+struct PaddedQ4 {
+    void* p = nullptr;
+    cudaStream_t s = nullptr;
+    ~PaddedQ4() {
+        if (p) cudaFreeAsync(p, s);
+    }
+};
+
+int view_for(const void* w, int w_type, int64_t inner, int64_t rows, cudaStream_t st, PaddedQ4* tmp, WView* out) {
+    *out = WView{w, w_type, 0};
+    if (w_type != VXB_TYPE_Q4_0) return VXB_OK;
+    if (inner % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 rows must hold whole blocks");
+    const size_t row = size_t(inner) / 32 * 18, pitch = (row + 15) / 16 * 16;
+    out->pitch = static_cast<int>(pitch);
+    if (pitch == row && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return VXB_OK;
+    tmp->s = st;
+    CUDA_TRY(cudaMallocAsync(&tmp->p, pitch * rows, st));
+    CUDA_TRY(cudaMemsetAsync(tmp->p, 0, pitch * rows, st));
+    CUDA_TRY(cudaMemcpy2DAsync(tmp->p, pitch, w, row, row, rows, cudaMemcpyDeviceToDevice, st));
+    out->p = tmp->p;
+    return VXB_OK;
+}
+
+}  // namespace
+
 extern "C" int vxb_pointwise(const void* w, int w_type, int K, int M, const void* x_f16, int64_t N,
                              const float* bias, const float* res, const float* snake_alpha, int out_f16, void* y,
                              void* stream) {
     if (!w || !x_f16 || !bias || !y) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
-    GemmOp op;
-    int rc = setup_pointwise(&op, w, w_type, K, M, x_f16, N, bias, res, snake_alpha, nullptr, out_f16, y, nullptr);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    PaddedQ4 tmp;
+    WView wv;
+    int rc = view_for(w, w_type, K, M, st, &tmp, &wv);
     if (rc) return rc;
-    return op.launch(static_cast<cudaStream_t>(stream));
+    GemmOp op;
+    rc = setup_pointwise(&op, wv, K, M, x_f16, N, bias, res, snake_alpha, nullptr, out_f16, y, nullptr);
+    if (rc) return rc;
+    return op.launch(st);
 }
 
 extern "C" int vxb_convt(const void* w, int w_type, int Cin, int Cout, int s, const void* x_f16, int B, int T,
                          const float* bias, float* y, void* stream) {
     if (!w || !x_f16 || !bias || !y) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
-    GemmOp op;
-    int rc = setup_convt(&op, w, w_type, Cin, Cout, s, x_f16, B, T, bias, y, nullptr);
+    if (s <= 0 || Cout <= 0 || Cin <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad extents");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    PaddedQ4 tmp;
+    WView wv;
+    int rc = view_for(w, w_type, int64_t(2) * s * Cout, Cin, st, &tmp, &wv);
     if (rc) return rc;
-    return op.launch(static_cast<cudaStream_t>(stream));
+    GemmOp op;
+    rc = setup_convt(&op, wv, Cin, Cout, s, x_f16, B, T, bias, y, nullptr);
+    if (rc) return rc;
+    return op.launch(st);
 }
 
 // ------------------------------------------------------------ introspection --
@@ -998,7 +1133,7 @@ extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev,
     head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z_dev, c->dw0, c->b0.v, h16, B, L, T);
     CUDA_TRY(cudaGetLastError());
     GemmOp op;
-    rc = setup_pointwise(&op, c->pw1->dev, c->pw1->type, L, D, h16, int64_t(B) * T, c->b1.v, nullptr,
+    rc = setup_pointwise(&op, c->pw1->view(), L, D, h16, int64_t(B) * T, c->b1.v, nullptr,
                          c->blocks[0].alpha.v, c->blocks[0].alpha.inv, 1, s16, st);
     if (rc || (rc = op.launch(s))) return rc;
     int64_t n = int64_t(B) * T;
@@ -1006,7 +1141,7 @@ extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev,
     static const int kDil[3] = {1, 3, 9};
     for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
         const Block& b = c->blocks[bi];
-        rc = setup_convt(&op, b.convt->dev, b.convt->type, b.cin, b.cout, b.s, s16, B, Tb, b.bias.v, xa, st);
+        rc = setup_convt(&op, b.convt->view(), b.cin, b.cout, b.s, s16, B, Tb, b.bias.v, xa, st);
         if (rc || (rc = op.launch(s))) return rc;
         n *= b.s;
         Tb *= b.s;
@@ -1016,26 +1151,28 @@ extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev,
         for (int r = 0; r < 3; ++r) {
             const ResUnit& u = b.ru[r];
             const int d = kDil[r];
-            dim3 grid((C + 31) / 32, (Tb + kPreTT - 1) / kPreTT, B);
-            res_pre_kernel<<<grid, 256, sizeof(float) * (kPreTT + 6 * d) * 32, s>>>(
-                cur, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h16, C, Tb, d);
+            const int tt = res_pre_tt(C, Tb, B, num_sms(c->device));
+            dim3 grid((C + 63) / 64, (Tb + tt - 1) / tt, B);
+            res_pre_kernel<<<grid, 256, res_pre_smem(d, tt), s>>>(
+                cur, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h16, C, Tb, d, tt);
             CUDA_TRY(cudaGetLastError());
             const bool last_block = bi + 1 == c->blocks.size();
             if (r < 2) {
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur, nullptr, nullptr, 0,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur, nullptr, nullptr, 0,
                                      nxt, st);
             } else if (!last_block) {
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur,
                                      c->blocks[bi + 1].alpha.v, c->blocks[bi + 1].alpha.inv, 1, s16, st);
             } else {
-                rc = setup_pointwise(&op, u.pw->dev, u.pw->type, C, C, h16, n, u.pb.v, cur, c->final_alpha.v,
+                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur, c->final_alpha.v,
                                      c->final_alpha.inv, 0, nxt, st);
             }
             if (rc || (rc = op.launch(s))) return rc;
             std::swap(cur, nxt);
         }
         if (bi + 1 == c->blocks.size()) {
-            final_kernel<<<grid_1d(n * 32, 256), 256, 0, s>>>(cur, c->final_w, c->final_bias, out_dev, C, Tb, n);
+            final_kernel<<<dim3((Tb + kFinTT - 1) / kFinTT, B), 256, sizeof(float) * (kFinTT + 6) * C, s>>>(
+                cur, c->final_w, c->final_bias, out_dev, C, Tb);
             CUDA_TRY(cudaGetLastError());
         }
     }

@@ -124,10 +124,12 @@ VXB_API int vxb_debug_stage(vxb_ctx* ctx, int stage, float* host_out, size_t n);
 /* Number of kernel launches in the current plan (one decode). */
 VXB_API int vxb_plan_num_ops(const vxb_ctx* ctx);
 
-/* Name and algorithmic work of plan op `idx`: flops = 2*M*K*N for the convs
- * (elementwise work counted roughly), bytes = minimal HBM traffic (weights
- * once, each activation read/written once). */
-VXB_API int vxb_plan_op_info(const vxb_ctx* ctx, int idx, char* name, int name_cap, double* flops, double* bytes);
+/* Name, kernel (template instance as a profiler shows it) and algorithmic
+ * work of plan op `idx`: flops = 2*M*K*N for the convs (elementwise work
+ * counted roughly), bytes = minimal HBM traffic (weights once, each
+ * activation read/written once). */
+VXB_API int vxb_plan_op_info(const vxb_ctx* ctx, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
+                             double* flops, double* bytes);
 
 /* Runs the plan's launch list `reps` times on the last decoded latent with a
  * CUDA event between consecutive launches and writes each op's mean device

@@ -184,6 +184,9 @@ int launch_gemm_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const C
 }
 
 // A prepared GEMM launch (tensor maps and arguments fixed at plan time).
+struct GemmOp;
+std::string gemm_kernel_name(const GemmOp& op);
+
 struct GemmOp {
     int akind = 0, epi = 0, bn = 16;
     dim3 grid;
@@ -199,6 +202,10 @@ struct GemmOp {
         }
     }
 };
+
+std::string gemm_kernel_name(const GemmOp& op) {
+    return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(op.epi) + ">";
+}
 
 // Pointwise conv GEMM: W [M rows][K] (F16, or Q4_0 rows padded to w.pitch), x fp16 [N][K].
 int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t N, const float* bias,
@@ -362,6 +369,7 @@ struct Plan {
     struct OpInfo {
         std::string name;
         double flops = 0, bytes = 0;  // algorithmic work: 2*M*K*N, minimal HBM traffic
+        std::string kernel;           // kernel (template instance) the op launches
     };
     std::vector<OpInfo> info;   // one per op
     std::vector<GemmOp> gemms;  // stable storage referenced by ops
@@ -725,7 +733,7 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
             return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
         });
         const double n0 = double(B) * T;
-        P.info.push_back({"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4});
+        P.info.push_back({"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4, "head_kernel"});
     }
     // model.1 pointwise (+ block 0 snake) -> s16 [N][D]
     {
@@ -740,7 +748,8 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
     auto wbytes = [](const DevTensor* t) { return double(t->nbytes); };
     {
         const double n0 = double(B) * T;
-        P.info.push_back({"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2});
+        P.info.push_back({"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2,
+                          gemm_kernel_name(P.gemms.back())});
     }
     int64_t n = int64_t(B) * T;
     int Tb = T;
@@ -754,7 +763,8 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
         P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
         P.info.push_back({"convt_b" + std::to_string(bi),
                           2.0 * (2.0 * b.s * b.cout) * b.cin * double(n),
-                          wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4});
+                          wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4,
+                          gemm_kernel_name(P.gemms.back())});
         n *= b.s;
         Tb *= b.s;
         const int C = b.cout;
@@ -778,7 +788,7 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
                     return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
                 });
                 P.info.push_back({"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r),
-                                  double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4});
+                                  double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
             }
             P.gemms.emplace_back();
             GemmOp& op = P.gemms.back();
@@ -800,7 +810,8 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
             P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
             P.info.push_back({"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
                               wbytes(u.pw) + double(n) * C * (2 + 4) +
-                                  double(n) * C * (last_unit && !last_block ? 2 : 4)});
+                                  double(n) * C * (last_unit && !last_block ? 2 : 4),
+                              gemm_kernel_name(P.gemms.back())});
             std::swap(cur, nxt);
         }
         if (bi + 1 == c->blocks.size()) {
@@ -815,7 +826,7 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
                 final_kernel<<<grid, 256, sizeof(float) * (kFinTT + 6) * C, s>>>(sx, w, fb, o, C, Tq);
                 return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
             });
-            P.info.push_back({"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4});
+            P.info.push_back({"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4, "final_kernel"});
         }
     }
     // prologue smem for d = 9 exceeds the default only for kPreTT + 54 rows; stays < 48 KB.
@@ -1020,13 +1031,13 @@ extern "C" int vxb_plan_num_ops(const vxb_ctx* c) {
     return (c && c->plan) ? static_cast<int>(c->plan->ops.size()) : 0;
 }
 
-extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, double* flops, double* bytes) {
+extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
+                                double* flops, double* bytes) {
     if (!c || !c->plan || idx < 0 || idx >= static_cast<int>(c->plan->info.size()))
         return fail(VXB_ERR_INVALID_ARGUMENT, "bad op index");
     const auto& in = c->plan->info[idx];
-    if (name && name_cap > 0) {
-        std::snprintf(name, name_cap, "%s", in.name.c_str());
-    }
+    if (name && name_cap > 0) std::snprintf(name, name_cap, "%s", in.name.c_str());
+    if (kernel && kernel_cap > 0) std::snprintf(kernel, kernel_cap, "%s", in.kernel.c_str());
     if (flops) *flops = in.flops;
     if (bytes) *bytes = in.bytes;
     return VXB_OK;

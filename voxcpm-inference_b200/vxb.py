@@ -47,7 +47,7 @@ SIGNATURES = {
     "vxb_debug_stage": (_i, [_vp, _i, _vp, _sz]),
     "vxb_decode_static": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "vxb_plan_num_ops": (_i, [_vp]),
-    "vxb_plan_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
+    "vxb_plan_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
                               ctypes.POINTER(ctypes.c_double)]),
     "vxb_time_ops": (_i, [_vp, _i, _vp, _sz, ctypes.POINTER(ctypes.c_float)]),
     "vxb_q4_0_dequant": (_i, [_vp, _i64, _vp, _vp]),
@@ -184,13 +184,14 @@ class Decoder:
         check(lib().vxb_sync(self.h, timeout_ms))
 
     def ops(self) -> list[dict]:
-        """[{name, flops, bytes}] for every launch of the current plan."""
+        """[{name, kernel, flops, bytes}] for every launch of the current plan."""
         out = []
         for i in range(lib().vxb_plan_num_ops(self.h)):
-            name = ctypes.create_string_buffer(64)
+            name, kern = ctypes.create_string_buffer(64), ctypes.create_string_buffer(64)
             fl, by = ctypes.c_double(), ctypes.c_double()
-            check(lib().vxb_plan_op_info(self.h, i, name, 64, ctypes.byref(fl), ctypes.byref(by)))
-            out.append({"name": name.value.decode(), "flops": fl.value, "bytes": by.value})
+            check(lib().vxb_plan_op_info(self.h, i, name, 64, kern, 64, ctypes.byref(fl), ctypes.byref(by)))
+            out.append({"name": name.value.decode(), "kernel": kern.value.decode(), "flops": fl.value,
+                        "bytes": by.value})
         return out
 
     def time_ops(self, reps: int = 10, flush=None, flush_bytes: int = 0) -> list[float]:

@@ -233,13 +233,13 @@ __device__ __forceinline__ uint32_t sw128_kmajor_off(uint32_t row, uint32_t k) {
 // reference's own fused Snake uses, audio-vae.cpp:1216-1247; constants below
 // are derived here from pi and the factorials).  a = q*(pi/2) + r with
 // |r| <= pi/4; sin^2(a) = sin^2(r) for even q and 1 - sin^2(r) for odd q, so
-// only the sine polynomial is needed.  pi/2 is split in three parts, the
-// first with 9 significant bits so that q*hi is exact for |q| < 2^15; beyond
-// |a| = 8192 the library sinf is used.
+// only the sine polynomial is needed.  pi/2 = hi + lo with hi = 201/128
+// (8 significant bits: q*hi is exact for |q| < 2^16); for |a| <= 8192 the
+// reduction error is below 2e-7; beyond that the library sinf is used.  The
+// degree-9 Taylor polynomial truncates below 2e-9 on |r| <= pi/4.
 constexpr double kHalfPi = 1.57079632679489661923;
 constexpr float kPi2Hi = 1.5703125f;  // 201/128
-constexpr float kPi2Mid = static_cast<float>(kHalfPi - 1.5703125);
-constexpr float kPi2Lo = static_cast<float>(kHalfPi - 1.5703125 - static_cast<double>(kPi2Mid));
+constexpr float kPi2Lo = static_cast<float>(kHalfPi - 1.5703125);
 constexpr float kTwoOverPi = static_cast<float>(1.0 / kHalfPi);
 
 __device__ __forceinline__ float sin_sq(float a) {
@@ -249,18 +249,44 @@ __device__ __forceinline__ float sin_sq(float a) {
     }
     const float q = rintf(a * kTwoOverPi);
     float r = fmaf(-q, kPi2Hi, a);
-    r = fmaf(-q, kPi2Mid, r);
     r = fmaf(-q, kPi2Lo, r);
     const float r2 = r * r;
-    // sin(r) = r (1 - r^2/3! + r^4/5! - ... - r^10/11!), |r| <= pi/4: truncation < 1e-11
-    float p = -1.0f / 39916800.0f;
-    p = fmaf(p, r2, 1.0f / 362880.0f);
+    // sin(r) = r (1 - r^2/3! + r^4/5! - r^6/7! + r^8/9!)
+    float p = 1.0f / 362880.0f;
     p = fmaf(p, r2, -1.0f / 5040.0f);
     p = fmaf(p, r2, 1.0f / 120.0f);
     p = fmaf(p, r2, -1.0f / 6.0f);
     const float sr = fmaf(r * r2, p, r);
     const float s2 = sr * sr;
     return (static_cast<int>(q) & 1) ? 1.0f - s2 : s2;
+}
+
+// Eight Q4_0 values -> eight fp16 (one 16-byte smem chunk), (q - 8) * d.
+// w0, w1 hold the 8 bytes whose low (hi = false) or high (hi = true)
+// nibbles are the values, in order.  Each nibble q is OR-ed into the fp16
+// pattern of 1024 (0x6400), giving 1024 + q exactly; subtracting 1032
+// gives q - 8 exactly, and one fp16 multiply by d rounds the exact product
+// (at most 15 significant bits) once -- the same result as rounding the
+// fp32 product (q - 8) * d to fp16.
+__device__ __forceinline__ uint4 q4_dequant8(uint32_t w0, uint32_t w1, bool hi, __half2 d2) {
+    const uint32_t a0 = hi ? (w0 >> 4) : w0;
+    const uint32_t a1 = hi ? (w1 >> 4) : w1;
+    uint32_t p[4];
+    p[0] = (a0 & 0x0000000Fu) | ((a0 << 8) & 0x000F0000u);
+    p[1] = ((a0 >> 16) & 0x0000000Fu) | ((a0 >> 8) & 0x000F0000u);
+    p[2] = (a1 & 0x0000000Fu) | ((a1 << 8) & 0x000F0000u);
+    p[3] = ((a1 >> 16) & 0x0000000Fu) | ((a1 >> 8) & 0x000F0000u);
+    const __half2 k1032 = __float2half2_rn(1032.0f);
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t bits = p[i] | 0x64006400u;
+        __half2 h = *reinterpret_cast<const __half2*>(&bits);
+        h = __hmul2(__hsub2(h, k1032), d2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return out;
 }
 
 // Snake activation (reference audio-vae.cpp:278-289 / :1443-1479):

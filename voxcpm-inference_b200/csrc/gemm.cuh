@@ -251,23 +251,17 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     for (int hb = 0; hb < 2; ++hb) {
                         const bool valid = m < args.M && k0 + hb * 32 < args.K;
                         const uint16_t* b16 = reinterpret_cast<const uint16_t*>(raw + t * kRawKBox + off + hb * 18);
-                        const float d = valid ? half_bits_to_float(b16[0]) : 0.f;
+                        const __half2 d2 = __half2half2(valid ? __ushort_as_half(b16[0]) : __float2half_rn(0.f));
                         uint32_t q4[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             q4[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
-                            __align__(16) __half v[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const int j = (c & 1) * 8 + e;
-                                const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-                                const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
-                                v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
-                            }
+                            // chunk c: elements 8c..8c+7 = low nibbles of bytes 0-7 / 8-15, then high nibbles
+                            const int wsel = (c & 1) * 2;
                             *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
-                                *reinterpret_cast<const uint4*>(v);
+                                q4_dequant8(q4[wsel], q4[wsel + 1], c >= 2, d2);
                         }
                     }
                 } else {
@@ -288,7 +282,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                         const bool valid = k0 + kl < args.K && blk * 32 < args.M;
                         const uint16_t* b16 =
                             reinterpret_cast<const uint16_t*>(raw + kl * kRawMNBox + base_off + bi * 18);
-                        const float d = valid ? half_bits_to_float(b16[0]) : 0.f;
+                        const __half2 d2 = __half2half2(valid ? __ushort_as_half(b16[0]) : __float2half_rn(0.f));
                         uint32_t q4[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
@@ -297,17 +291,10 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                         for (int c = 0; c < 4; ++c) {
                             const int ml = blk * 32 + c * 8 - m0;
                             if (ml < 0 || ml >= 128) continue;
-                            __align__(16) __half v[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const int j = (c & 1) * 8 + e;
-                                const uint32_t byte = (q4[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-                                const uint32_t nib = c < 2 ? (byte & 15u) : (byte >> 4);
-                                v[e] = __float2half_rn(static_cast<float>(static_cast<int>(nib) - 8) * d);
-                            }
+                            const int wsel = (c & 1) * 2;
                             const int h = ml >> 6, mc = (ml & 63) >> 3;
                             const uint32_t off = h * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
-                            *reinterpret_cast<uint4*>(a_dst + off) = *reinterpret_cast<const uint4*>(v);
+                            *reinterpret_cast<uint4*>(a_dst + off) = q4_dequant8(q4[wsel], q4[wsel + 1], c >= 2, d2);
                         }
                     }
                 }

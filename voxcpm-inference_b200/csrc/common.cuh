@@ -61,13 +61,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One try with a suspend-time hint: the thread sleeps (without issuing) until
+// the phase completes or about 20 us pass, so waiting warps do not take
+// issue slots from the working ones.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(20000)
         : "memory");
     return ok != 0;
 }
@@ -229,14 +232,15 @@ __device__ __forceinline__ uint32_t sw128_kmajor_off(uint32_t row, uint32_t k) {
 
 // ------------------------------------------------------------------ math --
 
-// sin(a)^2 by Cody-Waite reduction and a Taylor polynomial (the method the
-// reference's own fused Snake uses, audio-vae.cpp:1216-1247; constants below
-// are derived here from pi and the factorials).  a = q*(pi/2) + r with
+// sin(a)^2 by Cody-Waite reduction (the reduction the reference's own fused
+// Snake uses, audio-vae.cpp:1216-1247; the constants below are derived here
+// from pi).  a = q*(pi/2) + r with
 // |r| <= pi/4; sin^2(a) = sin^2(r) for even q and 1 - sin^2(r) for odd q, so
-// only the sine polynomial is needed.  pi/2 = hi + lo with hi = 201/128
-// (8 significant bits: q*hi is exact for |q| < 2^16); for |a| <= 8192 the
-// reduction error is below 2e-7; beyond that the library sinf is used.  The
-// degree-9 Taylor polynomial truncates below 2e-9 on |r| <= pi/4.
+// only the sine of the reduced argument is needed.  pi/2 = hi + lo with
+// hi = 201/128 (8 significant bits: q*hi is exact for |q| < 2^16); for
+// |a| <= 8192 the reduction error is below 2e-7; beyond that the library
+// sinf is used.  On |r| <= pi/4 the hardware sine (__sinf) is accurate to
+// 4e-7 absolute.
 constexpr double kHalfPi = 1.57079632679489661923;
 constexpr float kPi2Hi = 1.5703125f;  // 201/128
 constexpr float kPi2Lo = static_cast<float>(kHalfPi - 1.5703125);
@@ -250,13 +254,8 @@ __device__ __forceinline__ float sin_sq(float a) {
     const float q = rintf(a * kTwoOverPi);
     float r = fmaf(-q, kPi2Hi, a);
     r = fmaf(-q, kPi2Lo, r);
-    const float r2 = r * r;
-    // sin(r) = r (1 - r^2/3! + r^4/5! - r^6/7! + r^8/9!)
-    float p = 1.0f / 362880.0f;
-    p = fmaf(p, r2, -1.0f / 5040.0f);
-    p = fmaf(p, r2, 1.0f / 120.0f);
-    p = fmaf(p, r2, -1.0f / 6.0f);
-    const float sr = fmaf(r * r2, p, r);
+    // |r| <= pi/4, where the hardware sine's absolute error is below 4e-7
+    const float sr = __sinf(r);
     const float s2 = sr * sr;
     return (static_cast<int>(q) & 1) ? 1.0f - s2 : s2;
 }

@@ -98,6 +98,13 @@ VXB_API int vxb_build_plan(vxb_ctx* ctx, int batch, int T, int use_graph);
 /* Samples per latent frame (product of the decoder rates, 640 for VoxCPM). */
 VXB_API int vxb_hop(const vxb_ctx* ctx);
 
+/* Reads back the decoder config (as set by vxb_set_config / vxb_load_gguf):
+ * latent and decoder widths and up to max_rates upsampling rates; *n_rates
+ * receives the number of rates.  The reference reads the same fields from
+ * AudioVAEConfig (include/voxcpm/config.h:34-133). */
+VXB_API int vxb_get_config(const vxb_ctx* ctx, int* latent_dim, int* decoder_dim, int* rates, int max_rates,
+                           int* n_rates);
+
 /* One decode of the planned shape: z [batch][latent_dim][T] (t fastest, each
  * one the reference's ne=[T,latent_dim]) -> out [batch][hop*T], both HOST
  * pointers; includes the host->device and device->host copies and waits for

@@ -133,3 +133,23 @@ def test_convt_matches_oracle(vxb, Cin, Cout, s, B, T, wt):
     err = float(np.abs(got - ref).max())
     tol = 2e-4 * max(1.0, float(np.abs(ref).max()))
     assert err <= tol, f"convt {Cin}->{Cout} s={s} B={B} T={T} {wt}: max|d| {err:.3e} > {tol:.3e}"
+
+
+def test_snake_error_bound_wide_range(vxb):
+    """Snake over |alpha * x| up to 2e5 and alpha from 0.05 to 20 against fp64:
+    |y - y64| <= inv * 1.2e-6 + |x| * 2^-23 (the bound the kernel's sin^2
+    states) plus the fp32 rounding of y."""
+    mags = np.logspace(-4, 4, 2001)
+    x = np.concatenate([mags, -mags, [0.0, 1e-30, 3.0e4, -9.9e3]]).astype(np.float32)
+    alpha = np.array([0.05, 0.5, 1.0, 1.37, 5.0, 20.0], np.float32)
+    C, N = alpha.size, x.size
+    X = np.repeat(x[:, None], C, axis=1).copy()
+    y = torch.empty((N, C), dtype=torch.float32, device="cuda")
+    vxb.snake(dev(X), dev(alpha), C, N, y)
+    torch.cuda.synchronize()
+    inv = (1.0 / (alpha.astype(np.float32) + np.float32(1e-9))).astype(np.float64)
+    X64 = X.astype(np.float64)
+    y64 = X64 + inv * np.sin(alpha.astype(np.float64) * X64) ** 2
+    err = np.abs(y.cpu().numpy().astype(np.float64) - y64)
+    bound = inv * 1.2e-6 + np.abs(X64) * 2.0 ** -23 + np.abs(y64) * 2.0 ** -24
+    assert np.all(err <= bound), float(np.max(err / bound))

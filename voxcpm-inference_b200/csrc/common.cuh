@@ -120,6 +120,17 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Waits until every committed bulk group has completed (writes visible).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 16-byte global -> shared copy (cp.async, cached at L2 only); src_bytes = 0
+// writes zeros without reading src.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -232,32 +243,25 @@ __device__ __forceinline__ uint32_t sw128_kmajor_off(uint32_t row, uint32_t k) {
 
 // ------------------------------------------------------------------ math --
 
-// sin(a)^2 by Cody-Waite reduction (the reduction the reference's own fused
-// Snake uses, audio-vae.cpp:1216-1247; the constants below are derived here
-// from pi).  a = q*(pi/2) + r with
-// |r| <= pi/4; sin^2(a) = sin^2(r) for even q and 1 - sin^2(r) for odd q, so
-// only the sine of the reduced argument is needed.  pi/2 = hi + lo with
-// hi = 201/128 (8 significant bits: q*hi is exact for |q| < 2^16); for
-// |a| <= 8192 the reduction error is below 2e-7; beyond that the library
-// sinf is used.  On |r| <= pi/4 the hardware sine (__sinf) is accurate to
-// 4e-7 absolute.
-constexpr double kHalfPi = 1.57079632679489661923;
-constexpr float kPi2Hi = 1.5703125f;  // 201/128
-constexpr float kPi2Lo = static_cast<float>(kHalfPi - 1.5703125);
-constexpr float kTwoOverPi = static_cast<float>(1.0 / kHalfPi);
+// sin(a)^2.  sin^2 has period pi, so a is reduced to r = a - k*pi with
+// k = rint(a / pi), |r| <= pi/2 (Cody-Waite: pi = hi + lo, hi = 201/64;
+// fmaf keeps k*hi exact), and the hardware sine (__sinf, absolute error
+// below 2^-21.41 on [-pi, pi]) is squared.  The reduction adds less than
+// 2e-7 + 2e-11*|a| of phase error, so sin^2 is off by less than
+// 1.2e-6 + 4e-11*|a|, and Snake's y = x + inv * sin^2(alpha * x) by less than
+// inv * 1.2e-6 + |x| * 2^-23 (the last term includes rounding alpha * x).
+// No branch, no parity select.
+constexpr double kPi = 3.14159265358979323846;
+constexpr float kPiHi = 3.140625f;  // 201/64
+constexpr float kPiLo = static_cast<float>(kPi - 3.140625);
+constexpr float kInvPi = static_cast<float>(1.0 / kPi);
 
 __device__ __forceinline__ float sin_sq(float a) {
-    if (fabsf(a) > 8192.f) {
-        const float s = sinf(a);
-        return s * s;
-    }
-    const float q = rintf(a * kTwoOverPi);
-    float r = fmaf(-q, kPi2Hi, a);
-    r = fmaf(-q, kPi2Lo, r);
-    // |r| <= pi/4, where the hardware sine's absolute error is below 4e-7
-    const float sr = __sinf(r);
-    const float s2 = sr * sr;
-    return (static_cast<int>(q) & 1) ? 1.0f - s2 : s2;
+    const float k = rintf(a * kInvPi);
+    float r = fmaf(-k, kPiHi, a);
+    r = fmaf(-k, kPiLo, r);
+    const float s = __sinf(r);
+    return s * s;
 }
 
 // Eight Q4_0 values -> eight fp16 (one 16-byte smem chunk), (q - 8) * d.

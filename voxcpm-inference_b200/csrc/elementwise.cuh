@@ -39,17 +39,21 @@ __global__ void head_kernel(const float* __restrict__ z, const float* __restrict
     }
 }
 
-// Residual-unit prologue.  A block covers 64 channels (16 threads x float4)
-// and `tt` (<= kPreTT) time steps of one sequence.  The input rows
-// [t0 - 6d, t0 + tt) are loaded once with 16-byte loads (all of a thread's
-// loads issued before any is used) and Snake-activated (snake1) into shared
-// memory; every output then applies the 7 dilated causal taps, bias and
-// snake2 and is stored as fp16.  Requires C % 4 == 0.
+// Residual-unit prologue.  A block covers CT channels (CT/4 threads x
+// float4) and `tt` (<= kPreTT) time steps of one sequence.  The input rows
+// [t0 - 6d, t0 + tt) are copied into shared memory with 16-byte cp.async
+// (zero-filled before the sequence start: causal padding, snake(0) == 0) and
+// Snake-activated (snake1) in place by the thread that copied them; every
+// output then applies the 7 dilated causal taps, bias and snake2 and is
+// stored as fp16.  CT = 64 when C is a multiple of 64, else 32 (C = 96 keeps
+// every thread busy).  Requires C % 4 == 0.
 constexpr int kPreTT = 128;
-constexpr int kPreMaxRows = (kPreTT + 54 + 15) / 16;  // rows per thread for d <= 9
 
-__host__ __device__ constexpr size_t res_pre_smem(int d, int tt = kPreTT) { return sizeof(float) * (tt + 6 * d) * 64; }
+__host__ __device__ constexpr size_t res_pre_smem(int d, int tt = kPreTT, int ct = 64) {
+    return sizeof(float) * (tt + 6 * d) * ct;
+}
 
+template <int CT>
 __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
                                                       const float* __restrict__ i1,
                                                       const float* __restrict__ w /*[C][7]*/,
@@ -57,36 +61,33 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
                                                       const float* __restrict__ a2,
                                                       const float* __restrict__ i2, __half* __restrict__ out,
                                                       int C, int T, int d, int tt) {
-    extern __shared__ float4 sh4[];  // [(tt + 6d)][16]
-    const int cx = threadIdx.x & 15, ry = threadIdx.x >> 4;  // 16 channel groups x 16 rows
-    const int c = blockIdx.x * 64 + cx * 4;
+    constexpr int CG = CT / 4;    // threads across channels
+    constexpr int RG = 256 / CG;  // threads across rows
+    extern __shared__ float4 sh4[];  // [(tt + 6d)][CG]
+    const int cx = threadIdx.x % CG, ry = threadIdx.x / CG;
+    const int c = blockIdx.x * CT + cx * 4;
     const int t0 = blockIdx.y * tt;
     const int b = blockIdx.z;
     const int halo = 6 * d;
     const int rows = min(tt, T - t0) + halo;
     const bool cv = c < C;
     const float* xb = x + static_cast<long long>(b) * T * C;
-    float4 v[kPreMaxRows];
-#pragma unroll
-    for (int i = 0; i < kPreMaxRows; ++i) {
-        const int r = ry + 16 * i;
+    for (int r = ry; r < rows; r += RG) {
         const int t = t0 - halo + r;
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // causal zero padding (snake(0) == 0)
-        if (cv && r < rows && t >= 0) v[i] = __ldg(reinterpret_cast<const float4*>(xb + static_cast<long long>(t) * C + c));
+        const bool ok = cv && t >= 0;
+        cp_async16(&sh4[r * CG + cx], ok ? xb + static_cast<long long>(t) * C + c : xb, ok ? 16u : 0u);
     }
+    cp_async_wait_all();
     if (cv) {
         const float4 al1 = *reinterpret_cast<const float4*>(a1 + c);
         const float4 iv1 = *reinterpret_cast<const float4*>(i1 + c);
-#pragma unroll
-        for (int i = 0; i < kPreMaxRows; ++i) {
-            const int r = ry + 16 * i;
-            if (r >= rows) break;
-            float4 u = v[i];
+        for (int r = ry; r < rows; r += RG) {
+            float4 u = sh4[r * CG + cx];
             u.x = snake(u.x, al1.x, iv1.x);
             u.y = snake(u.y, al1.y, iv1.y);
             u.z = snake(u.z, al1.z, iv1.z);
             u.w = snake(u.w, al1.w, iv1.w);
-            sh4[r * 16 + cx] = u;
+            sh4[r * CG + cx] = u;
         }
     }
     __syncthreads();
@@ -99,13 +100,13 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     const float4 al2 = *reinterpret_cast<const float4*>(a2 + c);
     const float4 iv2 = *reinterpret_cast<const float4*>(i2 + c);
     __half* ob = out + static_cast<long long>(b) * T * C;
-    for (int q = ry; q < tt; q += 16) {
+    for (int q = ry; q < tt; q += RG) {
         const int t = t0 + q;
         if (t >= T) break;
         float4 acc = bb;
 #pragma unroll
         for (int k = 0; k < 7; ++k) {
-            const float4 u = sh4[(q + k * d) * 16 + cx];
+            const float4 u = sh4[(q + k * d) * CG + cx];
             acc.x = fmaf(u.x, wk[k].x, acc.x);
             acc.y = fmaf(u.y, wk[k].y, acc.y);
             acc.z = fmaf(u.z, wk[k].z, acc.z);
@@ -120,10 +121,13 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     }
 }
 
+// Channel tile of res_pre_kernel for C channels.
+inline int res_pre_ct(int C) { return C % 64 == 0 ? 64 : 32; }
+
 // Time tile of res_pre_kernel: the largest of 128/64/32 that still gives at
 // least two blocks per SM.
 inline int res_pre_tt(int C, int T, int B, int sms) {
-    const long long ct = (C + 63) / 64;
+    const long long ct = (C + res_pre_ct(C) - 1) / res_pre_ct(C);
     for (int tt = kPreTT; tt > 32; tt /= 2)
         if (ct * ((T + tt - 1) / tt) * B >= 2LL * sms) return tt;
     return 32;

@@ -355,22 +355,32 @@ struct Block {
     ResUnit ru[3];
 };
 
+struct OpInfo {
+    std::string name;
+    double flops = 0, bytes = 0;  // algorithmic work: 2*M*K*N, minimal HBM traffic
+    std::string kernel;           // kernel (template instance) the op launches
+};
+
+// Device buffers of one decode: the caller's latent and waveform, and the
+// activation arena (each buffer sized for the largest stage).
+struct DecodeBufs {
+    const float* z = nullptr;  // [B][L][T]
+    float* out = nullptr;      // [B][hop*T]
+    float* xa = nullptr;       // fp32 residual stream (ping)
+    float* xb = nullptr;       // fp32 residual stream (pong)
+    __half* h16 = nullptr;     // fp16 pointwise B operand (prologue output, head output)
+    __half* s16 = nullptr;     // fp16 transposed-conv B operand
+    int* status = nullptr;     // device status word
+};
+
 struct Plan {
     int B = 0, T = 0;
     bool use_graph = false;
     float* z = nullptr;     // [B][L][T]
     float* out = nullptr;   // [B][hop*T]
-    float* xa = nullptr;    // fp32 activations (ping)
-    float* xb = nullptr;    // fp32 activations (pong)
-    __half* h16 = nullptr;  // pointwise B operand
-    __half* s16 = nullptr;  // transposed-conv B operand
+    DecodeBufs bufs;
     size_t bytes = 0;
     std::vector<std::function<int(cudaStream_t)>> ops;
-    struct OpInfo {
-        std::string name;
-        double flops = 0, bytes = 0;  // algorithmic work: 2*M*K*N, minimal HBM traffic
-        std::string kernel;           // kernel (template instance) the op launches
-    };
     std::vector<OpInfo> info;   // one per op
     std::vector<GemmOp> gemms;  // stable storage referenced by ops
     cudaGraph_t graph = nullptr;
@@ -424,10 +434,10 @@ void free_plan(Plan* p) {
     if (p->graph) cudaGraphDestroy(p->graph);
     cudaFree(p->z);
     cudaFree(p->out);
-    cudaFree(p->xa);
-    cudaFree(p->xb);
-    cudaFree(p->h16);
-    cudaFree(p->s16);
+    cudaFree(p->bufs.xa);
+    cudaFree(p->bufs.xb);
+    cudaFree(p->bufs.h16);
+    cudaFree(p->bufs.s16);
 }
 
 const DevTensor* get(vxb_ctx* c, const std::string& name) {
@@ -566,6 +576,16 @@ int vxb_hop(const vxb_ctx* c) {
     return h;
 }
 
+int vxb_get_config(const vxb_ctx* c, int* latent_dim, int* decoder_dim, int* rates, int max_rates, int* n_rates) {
+    if (!c || !latent_dim || !decoder_dim || !n_rates || max_rates < 0 || (max_rates > 0 && !rates))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "vxb_get_config: null argument");
+    *latent_dim = c->latent_dim;
+    *decoder_dim = c->decoder_dim;
+    *n_rates = static_cast<int>(c->rates.size());
+    for (int i = 0; i < max_rates && i < *n_rates; ++i) rates[i] = c->rates[i];
+    return VXB_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -689,6 +709,171 @@ extern "C" int vxb_prepare(vxb_ctx* c) {
     return VXB_OK;
 }
 
+namespace {
+
+// Largest activation of any stage (floats) and largest transposed-conv input.
+void arena_sizes(const vxb_ctx* c, int B, int T, int64_t* max_x, int64_t* max_s) {
+    *max_x = *max_s = int64_t(B) * T * c->decoder_dim;
+    int64_t n = int64_t(B) * T;
+    for (const Block& b : c->blocks) {
+        *max_s = std::max(*max_s, n * b.cin);
+        n *= b.s;
+        *max_x = std::max(*max_x, n * b.cout);
+    }
+}
+
+// Receives the launches of one decode in order.
+struct OpSink {
+    virtual ~OpSink() = default;
+    virtual int gemm(const GemmOp& op, OpInfo info) = 0;
+    virtual int kernel(std::function<int(cudaStream_t)> fn, OpInfo info) = 0;
+    // the op emitted last writes debug stage `stage` into buf
+    virtual void stage(int stage, float* buf, size_t floats) {}
+};
+
+// The launch sequence of one decode of B latents of T frames:
+//   head dw -> model.1 pointwise (+ block 0 Snake, fp16)
+//   per block: transposed conv -> 3 x (prologue: snake, dilated dw, snake ->
+//              pointwise GEMM + bias + residual; the last unit also applies
+//              the next block's Snake (fp16) or the final Snake (fp32))
+//   final k7 conv + tanh.
+int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
+    const int L = c->latent_dim, D = c->decoder_dim;
+    auto wbytes = [](const DevTensor* t) { return double(t->nbytes); };
+    const double n0 = double(B) * T;
+    int rc;
+    {
+        const float *z = d.z, *w = c->dw0, *bb = c->b0.v;
+        __half* o = d.h16;
+        rc = sink.kernel(
+            [=](cudaStream_t s) {
+                head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z, w, bb, o, B, L, T);
+                return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
+            },
+            {"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4, "head_kernel"});
+        if (rc) return rc;
+    }
+    {
+        GemmOp op;
+        const Block& b0 = c->blocks[0];
+        if ((rc = setup_pointwise(&op, c->pw1->view(), L, D, d.h16, int64_t(B) * T, c->b1.v, nullptr, b0.alpha.v,
+                                  b0.alpha.inv, 1, d.s16, d.status)))
+            return rc;
+        if ((rc = sink.gemm(op, {"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2,
+                                 gemm_kernel_name(op)})))
+            return rc;
+    }
+    int64_t n = int64_t(B) * T;
+    int Tb = T;
+    static const int kDil[3] = {1, 3, 9};
+    const int sms = num_sms(c->device);
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& b = c->blocks[bi];
+        const bool last_block = bi + 1 == c->blocks.size();
+        {
+            GemmOp op;
+            if ((rc = setup_convt(&op, b.convt->view(), b.cin, b.cout, b.s, d.s16, B, Tb, b.bias.v, d.xa, d.status)))
+                return rc;
+            if ((rc = sink.gemm(op, {"convt_b" + std::to_string(bi), 2.0 * (2.0 * b.s * b.cout) * b.cin * double(n),
+                                     wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4,
+                                     gemm_kernel_name(op)})))
+                return rc;
+        }
+        n *= b.s;
+        Tb *= b.s;
+        const int C = b.cout;
+        const int stage0 = 2 + 4 * static_cast<int>(bi);
+        sink.stage(stage0, d.xa, size_t(n) * C);
+        float* cur = d.xa;
+        float* nxt = d.xb;
+        for (int r = 0; r < 3; ++r) {
+            const ResUnit& u = b.ru[r];
+            const int dl = kDil[r];
+            {
+                const float* x = cur;
+                __half* h = d.h16;
+                const int Bq = B, Tq = Tb;
+                const int tt = res_pre_tt(C, Tq, Bq, sms);
+                const int ct = res_pre_ct(C);
+                rc = sink.kernel(
+                    [=](cudaStream_t s) {
+                        dim3 grid((C + ct - 1) / ct, (Tq + tt - 1) / tt, Bq);
+                        const size_t sm = res_pre_smem(dl, tt, ct);
+                        if (ct == 64)
+                            res_pre_kernel<64><<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
+                                                                     u.a2.inv, h, C, Tq, dl, tt);
+                        else
+                            res_pre_kernel<32><<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
+                                                                     u.a2.inv, h, C, Tq, dl, tt);
+                        return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
+                    },
+                    {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
+                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
+                if (rc) return rc;
+            }
+            GemmOp op;
+            double out_bytes;
+            if (r < 2) {
+                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, nullptr, nullptr, 0, nxt,
+                                     d.status);
+                out_bytes = 4;
+            } else if (!last_block) {
+                const Block& nb = c->blocks[bi + 1];
+                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, nb.alpha.v, nb.alpha.inv, 1,
+                                     d.s16, d.status);
+                out_bytes = 2;
+            } else {
+                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, c->final_alpha.v,
+                                     c->final_alpha.inv, 0, nxt, d.status);
+                out_bytes = 4;
+            }
+            if (rc) return rc;
+            if ((rc = sink.gemm(op, {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
+                                     wbytes(u.pw) + double(n) * C * (2 + 4 + out_bytes), gemm_kernel_name(op)})))
+                return rc;
+            if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
+            std::swap(cur, nxt);
+        }
+        if (last_block) {
+            // final conv over snake(x) (held in `cur` after the swap)
+            const float* sx = cur;
+            float* o = d.out;
+            const float* w = c->final_w;
+            const float fb = c->final_bias;
+            const int Tq = Tb, Bq = B;
+            rc = sink.kernel(
+                [=](cudaStream_t s) {
+                    dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
+                    final_kernel<<<grid, 256, sizeof(float) * (kFinTT + 6) * C, s>>>(sx, w, fb, o, C, Tq);
+                    return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
+                },
+                {"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4, "final_kernel"});
+            if (rc) return rc;
+        }
+    }
+    return VXB_OK;
+}
+
+// Records the launches into a plan (replayed later, optionally as a graph).
+struct PlanSink : OpSink {
+    Plan& P;
+    explicit PlanSink(Plan& p) : P(p) {}
+    int gemm(const GemmOp& op, OpInfo info) override {
+        P.gemms.push_back(op);
+        P.ops.push_back([&P = P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
+        P.info.push_back(std::move(info));
+        return VXB_OK;
+    }
+    int kernel(std::function<int(cudaStream_t)> fn, OpInfo info) override {
+        P.ops.push_back(std::move(fn));
+        P.info.push_back(std::move(info));
+        return VXB_OK;
+    }
+    void stage(int stage, float* buf, size_t floats) override { P.stage_buf[stage] = {buf, floats, P.ops.size() - 1}; }
+};
+
+}  // namespace
+
 extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
     if (!c || B <= 0 || T <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad plan shape");
     if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare before vxb_build_plan");
@@ -700,140 +885,27 @@ extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
     P.B = B;
     P.T = T;
     P.use_graph = use_graph != 0;
-    const int L = c->latent_dim, D = c->decoder_dim, hop = vxb_hop(c);
-    // arena sizes
-    int64_t max_x = int64_t(B) * T * D, max_s = int64_t(B) * T * D;
-    {
-        int64_t n = int64_t(B) * T;
-        int C = D;
-        for (const Block& b : c->blocks) {
-            max_s = std::max(max_s, n * C);
-            n *= b.s;
-            C = b.cout;
-            max_x = std::max(max_x, n * C);
-        }
-    }
+    const int L = c->latent_dim, hop = vxb_hop(c);
+    int64_t max_x, max_s;
+    arena_sizes(c, B, T, &max_x, &max_s);
     CUDA_TRY(cudaMalloc(&P.z, sizeof(float) * B * L * T));
     CUDA_TRY(cudaMalloc(&P.out, sizeof(float) * int64_t(B) * T * hop));
-    CUDA_TRY(cudaMalloc(&P.xa, sizeof(float) * max_x));
-    CUDA_TRY(cudaMalloc(&P.xb, sizeof(float) * max_x));
-    CUDA_TRY(cudaMalloc(&P.h16, sizeof(__half) * max_x));
-    CUDA_TRY(cudaMalloc(&P.s16, sizeof(__half) * max_s));
+    DecodeBufs& d = P.bufs;
+    CUDA_TRY(cudaMalloc(&d.xa, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&d.xb, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&d.h16, sizeof(__half) * max_x));
+    CUDA_TRY(cudaMalloc(&d.s16, sizeof(__half) * max_s));
+    d.z = P.z;
+    d.out = P.out;
+    d.status = c->status;
     P.bytes = sizeof(float) * (B * L * T + int64_t(B) * T * hop + 2 * max_x) + sizeof(__half) * (max_x + max_s);
-
-    int* st = c->status;
-    P.gemms.reserve(2 + 4 * c->blocks.size());
-    int rc;
-    // model.0 (head dw) -> h16 [N][L]
-    {
-        const float *z = P.z, *w = c->dw0, *bb = c->b0.v;
-        __half* o = P.h16;
-        P.ops.push_back([=](cudaStream_t s) {
-            head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z, w, bb, o, B, L, T);
-            return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
-        });
-        const double n0 = double(B) * T;
-        P.info.push_back({"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4, "head_kernel"});
-    }
-    // model.1 pointwise (+ block 0 snake) -> s16 [N][D]
-    {
-        P.gemms.emplace_back();
-        GemmOp& op = P.gemms.back();
-        const Block& b0 = c->blocks[0];
-        rc = setup_pointwise(&op, c->pw1->view(), L, D, P.h16, int64_t(B) * T, c->b1.v, nullptr,
-                             b0.alpha.v, b0.alpha.inv, 1, P.s16, st);
-        if (rc) return rc;
-    }
-    P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
-    auto wbytes = [](const DevTensor* t) { return double(t->nbytes); };
-    {
-        const double n0 = double(B) * T;
-        P.info.push_back({"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2,
-                          gemm_kernel_name(P.gemms.back())});
-    }
-    int64_t n = int64_t(B) * T;
-    int Tb = T;
-    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
-        const Block& b = c->blocks[bi];
-        // transposed conv: s16 [n][cin] -> xa [n*s][cout]
-        P.gemms.emplace_back();
-        rc = setup_convt(&P.gemms.back(), b.convt->view(), b.cin, b.cout, b.s, P.s16, B, Tb, b.bias.v,
-                         P.xa, st);
-        if (rc) return rc;
-        P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
-        P.info.push_back({"convt_b" + std::to_string(bi),
-                          2.0 * (2.0 * b.s * b.cout) * b.cin * double(n),
-                          wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4,
-                          gemm_kernel_name(P.gemms.back())});
-        n *= b.s;
-        Tb *= b.s;
-        const int C = b.cout;
-        const int stage0 = 2 + 4 * static_cast<int>(bi);
-        P.stage_buf[stage0] = {P.xa, size_t(n) * C, P.ops.size() - 1};
-        float* cur = P.xa;
-        float* nxt = P.xb;
-        static const int kDil[3] = {1, 3, 9};
-        for (int r = 0; r < 3; ++r) {
-            const ResUnit& u = b.ru[r];
-            const int d = kDil[r];
-            {
-                const float* x = cur;
-                __half* h = P.h16;
-                const int Bq = B, Tq = Tb;
-                const int tt = res_pre_tt(C, Tq, Bq, num_sms(c->device));
-                P.ops.push_back([=](cudaStream_t s) {
-                    dim3 grid((C + 63) / 64, (Tq + tt - 1) / tt, Bq);
-                    res_pre_kernel<<<grid, 256, res_pre_smem(d, tt), s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
-                                                                          u.a2.inv, h, C, Tq, d, tt);
-                    return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
-                });
-                P.info.push_back({"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r),
-                                  double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
-            }
-            P.gemms.emplace_back();
-            GemmOp& op = P.gemms.back();
-            const bool last_unit = r == 2;
-            const bool last_block = bi + 1 == c->blocks.size();
-            if (!last_unit) {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, nullptr, nullptr, 0,
-                                     nxt, st);
-                P.stage_buf[stage0 + 1 + r] = {nxt, size_t(n) * C, P.ops.size()};
-            } else if (!last_block) {
-                const Block& nb = c->blocks[bi + 1];
-                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, nb.alpha.v,
-                                     nb.alpha.inv, 1, P.s16, st);
-            } else {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, P.h16, n, u.pb.v, cur, c->final_alpha.v,
-                                     c->final_alpha.inv, 0, nxt, st);
-            }
-            if (rc) return rc;
-            P.ops.push_back([&P, idx = P.gemms.size() - 1](cudaStream_t s) { return P.gemms[idx].launch(s); });
-            P.info.push_back({"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
-                              wbytes(u.pw) + double(n) * C * (2 + 4) +
-                                  double(n) * C * (last_unit && !last_block ? 2 : 4),
-                              gemm_kernel_name(P.gemms.back())});
-            std::swap(cur, nxt);
-        }
-        if (bi + 1 == c->blocks.size()) {
-            // final conv over snake(x) (held in `cur` after the swap)
-            const float* sx = cur;
-            float* o = P.out;
-            const float* w = c->final_w;
-            const float fb = c->final_bias;
-            const int Tq = Tb, Bq = B;
-            P.ops.push_back([=](cudaStream_t s) {
-                dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
-                final_kernel<<<grid, 256, sizeof(float) * (kFinTT + 6) * C, s>>>(sx, w, fb, o, C, Tq);
-                return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
-            });
-            P.info.push_back({"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4, "final_kernel"});
-        }
-    }
-    // prologue smem for d = 9 exceeds the default only for kPreTT + 54 rows; stays < 48 KB.
+    PlanSink sink(P);
+    int rc = emit_decode(c, d, B, T, sink);
+    if (rc) return rc;
     if (P.use_graph) {
         CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
         int orc = VXB_OK;
-        cudaMemsetAsync(st, 0, sizeof(int), c->stream);
+        cudaMemsetAsync(c->status, 0, sizeof(int), c->stream);
         for (auto& op : P.ops)
             if ((orc = op(c->stream))) break;
         cudaGraph_t graph = nullptr;
@@ -1107,23 +1179,21 @@ int static_scratch(int dev, uint8_t** out) {
     return VXB_OK;
 }
 
+// Launches every op as soon as it is emitted.
+struct LaunchSink : OpSink {
+    cudaStream_t s;
+    explicit LaunchSink(cudaStream_t st) : s(st) {}
+    int gemm(const GemmOp& op, OpInfo) override { return op.launch(s); }
+    int kernel(std::function<int(cudaStream_t)> fn, OpInfo) override { return fn(s); }
+};
+
 }  // namespace
 
 extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev, int B, int T, void* stream) {
     if (!c || !z_dev || !out_dev || B <= 0 || T <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
     if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare first");
-    const int L = c->latent_dim, D = c->decoder_dim;
-    int64_t max_x = int64_t(B) * T * D, max_s = int64_t(B) * T * D;
-    {
-        int64_t n = int64_t(B) * T;
-        int C = D;
-        for (const Block& b : c->blocks) {
-            max_s = std::max(max_s, n * C);
-            n *= b.s;
-            C = b.cout;
-            max_x = std::max(max_x, n * C);
-        }
-    }
+    int64_t max_x, max_s;
+    arena_sizes(c, B, T, &max_x, &max_s);
     if (max_x > int64_t(kStaticActFloats) || max_s > int64_t(kStaticActFloats))
         return fail(VXB_ERR_INVALID_ARGUMENT,
                     "vxb_decode_static: shape needs " + std::to_string(std::max(max_x, max_s)) +
@@ -1133,61 +1203,19 @@ extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev,
     uint8_t* base = nullptr;
     int rc = static_scratch(c->device, &base);
     if (rc) return rc;
-    float* xa = reinterpret_cast<float*>(base);
-    float* xb = xa + kStaticActFloats;
-    __half* h16 = reinterpret_cast<__half*>(xb + kStaticActFloats);
-    __half* s16 = h16 + kStaticActFloats;
-    int* st = reinterpret_cast<int*>(s16 + kStaticActFloats);
+    DecodeBufs d;
+    d.z = z_dev;
+    d.out = out_dev;
+    d.xa = reinterpret_cast<float*>(base);
+    d.xb = d.xa + kStaticActFloats;
+    d.h16 = reinterpret_cast<__half*>(d.xb + kStaticActFloats);
+    d.s16 = d.h16 + kStaticActFloats;
+    d.status = reinterpret_cast<int*>(d.s16 + kStaticActFloats);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-
-    CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(int), s));  // the status word must start at zero
-    head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z_dev, c->dw0, c->b0.v, h16, B, L, T);
-    CUDA_TRY(cudaGetLastError());
-    GemmOp op;
-    rc = setup_pointwise(&op, c->pw1->view(), L, D, h16, int64_t(B) * T, c->b1.v, nullptr,
-                         c->blocks[0].alpha.v, c->blocks[0].alpha.inv, 1, s16, st);
-    if (rc || (rc = op.launch(s))) return rc;
-    int64_t n = int64_t(B) * T;
-    int Tb = T;
-    static const int kDil[3] = {1, 3, 9};
-    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
-        const Block& b = c->blocks[bi];
-        rc = setup_convt(&op, b.convt->view(), b.cin, b.cout, b.s, s16, B, Tb, b.bias.v, xa, st);
-        if (rc || (rc = op.launch(s))) return rc;
-        n *= b.s;
-        Tb *= b.s;
-        const int C = b.cout;
-        float* cur = xa;
-        float* nxt = xb;
-        for (int r = 0; r < 3; ++r) {
-            const ResUnit& u = b.ru[r];
-            const int d = kDil[r];
-            const int tt = res_pre_tt(C, Tb, B, num_sms(c->device));
-            dim3 grid((C + 63) / 64, (Tb + tt - 1) / tt, B);
-            res_pre_kernel<<<grid, 256, res_pre_smem(d, tt), s>>>(
-                cur, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h16, C, Tb, d, tt);
-            CUDA_TRY(cudaGetLastError());
-            const bool last_block = bi + 1 == c->blocks.size();
-            if (r < 2) {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur, nullptr, nullptr, 0,
-                                     nxt, st);
-            } else if (!last_block) {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur,
-                                     c->blocks[bi + 1].alpha.v, c->blocks[bi + 1].alpha.inv, 1, s16, st);
-            } else {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, h16, n, u.pb.v, cur, c->final_alpha.v,
-                                     c->final_alpha.inv, 0, nxt, st);
-            }
-            if (rc || (rc = op.launch(s))) return rc;
-            std::swap(cur, nxt);
-        }
-        if (bi + 1 == c->blocks.size()) {
-            final_kernel<<<dim3((Tb + kFinTT - 1) / kFinTT, B), 256, sizeof(float) * (kFinTT + 6) * C, s>>>(
-                cur, c->final_w, c->final_bias, out_dev, C, Tb);
-            CUDA_TRY(cudaGetLastError());
-        }
-    }
+    CUDA_TRY(cudaMemsetAsync(d.status, 0, sizeof(int), s));  // the status word must start at zero
+    LaunchSink sink(s);
+    if ((rc = emit_decode(c, d, B, T, sink))) return rc;
     // report a failed bounded wait through vxb_sync (pinned word made at vxb_open)
-    CUDA_TRY(cudaMemcpyAsync(c->status_host, st, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, d.status, sizeof(int), cudaMemcpyDeviceToHost, s));
     return VXB_OK;
 }

@@ -41,6 +41,7 @@ SIGNATURES = {
     "vxb_prepare": (_i, [_vp]),
     "vxb_build_plan": (_i, [_vp, _i, _i, _i]),
     "vxb_hop": (_i, [_vp]),
+    "vxb_get_config": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i), _i, ctypes.POINTER(_i)]),
     "vxb_decode": (_i, [_vp, _vp, _vp]),
     "vxb_decode_device": (_i, [_vp, _vp, _vp, _vp]),
     "vxb_sync": (_i, [_vp, _i]),
@@ -157,6 +158,13 @@ class Decoder:
     def hop(self) -> int:
         return lib().vxb_hop(self.h)
 
+    def config(self) -> dict:
+        """{latent_dim, decoder_dim, rates} of the loaded decoder."""
+        lat, dec, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        rates = (ctypes.c_int * 8)()
+        check(lib().vxb_get_config(self.h, ctypes.byref(lat), ctypes.byref(dec), rates, 8, ctypes.byref(n)))
+        return {"latent_dim": lat.value, "decoder_dim": dec.value, "rates": list(rates[: n.value])}
+
     def decode(self, z: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
         """Host latents [B, latent, T] -> host waveform [B, hop*T] (copies included)."""
         z = np.ascontiguousarray(z, dtype=np.float32)
@@ -168,6 +176,34 @@ class Decoder:
         if out is None:
             out = np.empty((B, self.hop * T), np.float32)
         check(lib().vxb_decode(self.h, ptr(z), ptr(out)))
+        return out
+
+    def decode_chunked(self, z: np.ndarray, chunk: int, halo: int | None = None) -> np.ndarray:
+        """Host latents [latent, T] (or [1, latent, T]) -> waveform [hop*T],
+        decoded in windows of at most chunk + halo frames (activation memory
+        bounded by the window, not the utterance).  Equal to decode(z): every
+        window starts `halo` frames (>= the receptive field) before the frames
+        it keeps, and is zero-padded at its end to one plan size -- the decoder
+        is causal, so the padding never reaches a kept sample."""
+        import chunking
+
+        z = np.asarray(z, dtype=np.float32)
+        if z.ndim == 3:
+            if z.shape[0] != 1:
+                raise ValueError("decode_chunked decodes one utterance")
+            z = z[0]
+        L, T = z.shape
+        if halo is None:
+            halo = chunking.min_halo(self.config()["rates"])
+        W = min(T, chunk + halo)
+        win = np.zeros((1, L, W), np.float32)
+        out = np.empty(T * self.hop, np.float32)
+        hop = self.hop
+        for c in chunking.chunks_of(T, chunk, halo):
+            win[0, :, : c.frames] = z[:, c.start:c.end]
+            win[0, :, c.frames:] = 0.0
+            y = self.decode(win)
+            out[c.keep * hop:c.end * hop] = y[0, c.halo * hop:(c.halo + c.end - c.keep) * hop]
         return out
 
     def decode_host_ptrs(self, z_ptr: int, out_ptr: int):

@@ -10,6 +10,10 @@ distributed):
       independent z=[1,64,6]; the last 640 samples (40 ms) are emitted.
   c1  the same with F16 weights.
   c3  one 60 s utterance, z=[1,64,1500] (AR(1) 0.9), F16; a step = the decode.
+      Over N ranks the utterance is cut into N time chunks, each decoded
+      with a 20-frame left halo (the decoder's receptive field is 18.49
+      frames, so every kept sample equals the one-shot decode's; strong
+      scaling, no exchange).
   c4  256 independent streams per step, z=[256,64,6], Q4_0-mixed, split
       evenly over the ranks (strong scaling).
   c5f / c5q  64 utterances z=[64,64,750] (AR(1) 0.9), F16 / Q4_0-mixed, split
@@ -48,7 +52,7 @@ WORKLOADS = {
     # name: (quant, streams per step (global), T, emitted samples per stream-step, scaling, ar)
     "c2": ("q4_0", 1, 6, 640, "weak", None),
     "c1": ("f16", 1, 6, 640, "weak", None),
-    "c3": ("f16", 1, 1500, 1500 * HOP, "weak", 0.9),
+    "c3": ("f16", 1, 1500, 1500 * HOP, "strong", 0.9),
     "c4": ("q4_0", 256, 6, 640, "strong", None),
     "c5f": ("f16", 64, 750, 750 * HOP, "strong", 0.9),
     "c5q": ("q4_0", 64, 750, 750 * HOP, "strong", 0.9),
@@ -158,8 +162,14 @@ def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: 
     return statistics.median(times), len(times), label, cores, times
 
 
-def build_inputs(workload: str, rank: int, per_rank: int, steps: int):
+C3_HALO = 20  # frames of left context per time chunk (receptive field 18.49)
+
+
+def build_inputs(workload: str, rank: int, per_rank: int, steps: int, window=None):
     quant, _, T, _, _, ar = WORKLOADS[workload]
+    if window is not None:  # one utterance shared by all ranks, this rank's time window
+        z = S.make_latents(steps, T, seed=1000, ar=ar, batch=1)
+        return np.ascontiguousarray(z[..., window.start:window.end])
     z = S.make_latents(steps, T, seed=1000 + rank, ar=ar, batch=per_rank)
     return z  # [steps, per_rank, 64, T]
 
@@ -175,7 +185,16 @@ def main():
     ws, rank, local = dist_env()
     quant, streams, T, emit, scaling, ar = WORKLOADS[args.workload]
     per_rank = streams if scaling == "weak" else max(1, streams // ws)
-    emitted_s_per_step = per_rank * emit / SR  # per rank
+    window = None
+    if args.workload == "c3":  # time chunks of one utterance
+        import chunking
+
+        per_rank = 1
+        window = chunking.split(T, ws, C3_HALO)[rank] if ws > 1 else None
+    audio_per_step = (streams * emit if scaling == "strong" else ws * per_rank * emit) / SR  # whole job
+    T_full = T
+    if window is not None:
+        T = window.frames
     hbm, tfl, peak_src = peaks()
     tmpdir = tempfile.mkdtemp(prefix="vxb_bench_")
     model = os.path.join(tmpdir, f"{quant}.gguf")
@@ -184,6 +203,12 @@ def main():
            "frames": T, "emitted_samples_per_stream_step": emit, "sample_rate": SR,
            "l2": "flushed before every step (256 MiB memset outside the timed events)",
            "parallelism": f"dp{ws} (independent streams per GPU, no collective)"}
+    cfg["frames"] = T_full
+    if window is not None:
+        cfg["parallelism"] = (f"dp{ws} time chunks of one utterance ({C3_HALO}-frame left halo), no collective")
+        cfg["rank0_window"] = "frames [%d, %d), kept from %d" % (
+            chunking.split(T_full, ws, C3_HALO)[0].start, chunking.split(T_full, ws, C3_HALO)[0].end,
+            chunking.split(T_full, ws, C3_HALO)[0].keep)
 
     if args.impl == "reference":
         if rank != 0:
@@ -230,7 +255,7 @@ def main():
     d.build_plan(per_rank, T, graph=True)
     nops = len(d.ops())
     K, W = args.steps, max(3, args.warmup)
-    z_host = build_inputs(args.workload, rank, per_rank, K + W)
+    z_host = build_inputs(args.workload, rank, per_rank, K + W, window)
     z_dev = torch.from_numpy(z_host).cuda()
     out_dev = torch.empty((per_rank, T * HOP), dtype=torch.float32, device="cuda")
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
@@ -266,7 +291,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
         dist.barrier()
-    audio_total = emitted_s_per_step * K * ws
+    audio_total = audio_per_step * K
     value = audio_total / (total_ms / 1e3)
 
     # e2e: the public blocking call with pinned host buffers
@@ -341,7 +366,7 @@ def main():
             "dtype": "f16", "data": "synthetic (seeded weights and latents)", "config": cfg,
             "latency_ms": {"p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
                            "e2e_p50": float(np.percentile(e2e_ms, 50))},
-            "full_output_audio_s_per_s": value * (T * HOP) / emit,
+            "full_output_audio_s_per_s": value * (T_full * HOP) / emit,
             "e2e": {"value": e2e_value, "unit": "audio-s/s", "clock": "host (blocking call)",
                     "h2d_bytes_per_step": int(z_host[0].nbytes), "d2h_bytes_per_step": int(out_pin.nbytes)},
             "gpu_launches": K * nops,

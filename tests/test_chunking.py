@@ -1,0 +1,64 @@
+"""Time-chunked decode: receptive field, chunk arithmetic, and exactness of
+halo chunks checked on the C oracle (CPU, small-width model with the
+VoxCPM rates; the receptive field does not depend on the width)."""
+import numpy as np
+import pytest
+
+import chunking as CH
+import oracle_lib as O
+import vxb_synth as S
+from models import model_path
+
+
+def test_receptive_field_voxcpm():
+    rf = CH.receptive_field_frames((8, 8, 5, 2))
+    # 6 + (1 + 78/8) + (1/8 + 78/64) + (1/64 + 78/320) + (1/320 + 78/640) + 6/640
+    assert abs(rf - 18.4875) < 1e-12
+    assert CH.min_halo((8, 8, 5, 2)) == 19
+
+
+@pytest.mark.parametrize("T,parts,halo", [(1500, 8, 20), (1500, 3, 19), (7, 8, 20), (1, 1, 0), (64, 5, 19)])
+def test_split_covers_every_frame_once(T, parts, halo):
+    ch = CH.split(T, parts, halo)
+    assert len(ch) == min(T, parts)
+    assert ch[0].start == 0 and ch[0].keep == 0 and ch[-1].end == T
+    for a, b in zip(ch, ch[1:]):
+        assert a.end == b.keep
+    for c in ch:
+        assert c.keep - c.start == min(halo, c.keep)
+    sizes = [c.end - c.keep for c in ch]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_chunks_of_and_bad_arguments():
+    ch = CH.chunks_of(100, 32, 19)
+    assert [(c.start, c.keep, c.end) for c in ch] == [(0, 0, 32), (13, 32, 64), (45, 64, 96), (77, 96, 100)]
+    for bad in [(0, 1, 0), (5, 0, 1), (5, 1, -1)]:
+        with pytest.raises(ValueError):
+            CH.split(*bad)
+
+
+@pytest.fixture(scope="module")
+def small_model():
+    path, _ = model_path(quant="f16", seed=3, decoder_dim=128)
+    m = O.OracleModel(path)
+    yield m
+    m.close()
+
+
+def test_halo_chunks_reproduce_full_decode(small_model):
+    """Chunks with the minimal halo (19 frames) reproduce the full decode's
+    kept samples exactly; an 18-frame halo does not."""
+    m, T, hop = small_model, 72, 640
+    z = S.make_latents(1, T, latent_dim=m.latent_dim, seed=9, ar=0.9)[0, 0]
+    full = m.decode(z[None], O.MODE_EXACT)
+    for halo, exact in ((19, True), (24, True), (18, False)):
+        worst = 0.0
+        for c in CH.chunks_of(T, 25, halo):
+            part = m.decode(z[None, :, c.start:c.end], O.MODE_EXACT)
+            kept = part[0, c.halo * hop:]
+            worst = max(worst, float(np.abs(kept - full[0, c.keep * hop:c.end * hop]).max()))
+        if exact:
+            assert worst == 0.0, (halo, worst)
+        else:
+            assert worst > 0.0, halo

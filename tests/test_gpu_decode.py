@@ -113,6 +113,18 @@ def test_causal_prefix_property(vxb, quant):
         assert np.abs(part - full[:, : t * 640]).max() <= 1e-5, t
 
 
+@pytest.mark.parametrize("quant", ["f16", "q4_0"])
+def test_chunked_decode_equals_full(vxb, quant):
+    """A long utterance decoded in 64-frame windows with the minimal halo
+    (19 frames for rates 8,8,5,2) equals the one-shot decode."""
+    d = decoder_for(vxb, quant=quant, seed=0)
+    assert d.config() == {"latent_dim": 64, "decoder_dim": 1536, "rates": [8, 8, 5, 2]}
+    z = S.make_latents(1, 300, seed=25, ar=0.9)[0, 0]
+    full = d.decode(z[None])[0]
+    got = d.decode_chunked(z, chunk=64)
+    assert np.abs(got - full).max() <= 1e-5
+
+
 def test_decode_rejects_bad_shapes(vxb):
     d = decoder_for(vxb, quant="f16", seed=0)
     with pytest.raises(vxb.VxbError) as e:

@@ -60,3 +60,54 @@ def test_two_gloo_ranks_partition_streams_without_exchange():
     assert not np.array_equal(res[0][1]["c2"][1], res[1][1]["c2"][1])
     # every rank reports the max of the per-rank timings
     assert res[0][2] == res[1][2] == 20.0
+
+
+def _chunk_worker(rank, world, port, model, T, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+    import bench
+    import chunking
+    import oracle_lib as O
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ws, r, _ = bench.dist_env()
+    w = chunking.split(T, ws, bench.C3_HALO)[r]
+    z = bench.S.make_latents(1, T, seed=1000, ar=0.9)[0, 0]  # the utterance every rank shares
+    m = O.OracleModel(model)
+    y = m.decode(z[None, :, w.start:w.end], O.MODE_EXACT)[0]
+    kept = y[w.halo * 640:]
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((r, w.keep, kept))
+
+
+@pytest.mark.timeout(300)
+def test_two_gloo_ranks_time_chunks_reproduce_one_utterance():
+    """c3 over ranks: each rank decodes its time window (20-frame halo) of the
+    shared utterance with no exchange; the kept samples, placed side by side,
+    equal the one-shot decode (oracle, small-width model, CPU)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+    import oracle_lib as O
+    import vxb_synth as S
+    from models import model_path
+
+    model, _ = model_path(quant="f16", seed=3, decoder_dim=128)
+    T = 50
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + ((os.getpid() + 7) % 1000)
+    procs = [ctx.Process(target=_chunk_worker, args=(r, 2, port, model, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    parts = sorted(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    z = S.make_latents(1, T, seed=1000, ar=0.9)[0, 0]
+    full = O.OracleModel(model).decode(z[None], O.MODE_EXACT)[0]
+    got = np.concatenate([k for _, _, k in parts])
+    assert parts[1][1] == 25 and got.size == full.size
+    assert np.array_equal(got, full)

@@ -93,6 +93,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// ------------------------------------------------ programmatic launches --
+// Every decode kernel is launched with programmatic stream serialisation:
+// it may start (and run its setup) while the previous kernel finishes, and
+// waits here before touching memory the previous kernels wrote or read.
+// griddepcontrol.wait returns once every prerequisite grid has completed and
+// its memory operations are visible; launch_dependents then lets the next
+// kernel be scheduled (issued only after the wait, so at most two grids are
+// in flight).  Without a programmatic prerequisite both are no-ops.
+__device__ __forceinline__ void grid_dep_sync() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // -------------------------------------------------------------------- TMA --
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y) {
@@ -296,6 +309,49 @@ __device__ __forceinline__ uint4 q4_dequant8(uint32_t w0, uint32_t w1, bool hi, 
 // x + sin(alpha*x)^2 * inv, inv = 1 / (alpha + 1e-9).
 __device__ __forceinline__ float snake(float x, float alpha, float inv) {
     return fmaf(sin_sq(alpha * x), inv, x);
+}
+
+// ----------------------------------------------- paired fp32 arithmetic --
+// sm_100 executes two fp32 FMAs / multiplies as one instruction
+// (fma.rn.f32x2, mul.rn.f32x2; same IEEE rounding per lane as fmaf / fmul).
+__device__ __forceinline__ uint64_t f2_bits(float2 a) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+    return r;
+}
+__device__ __forceinline__ float2 f2_val(uint64_t r) {
+    float2 a;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+    return a;
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return f2_val(d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return f2_val(d);
+}
+
+// Snake on two lanes at once: the same operations and roundings as snake()
+// per lane (alpha*x, the period-pi reduction, the hardware sine, the square
+// and the final fma), paired where sm_100 has a two-lane instruction.
+__device__ __forceinline__ float2 snake2(float2 x, float2 alpha, float2 inv) {
+    const float2 a = fmul2(alpha, x);
+    const float2 q = fmul2(a, make_float2(kInvPi, kInvPi));
+    const float2 k = make_float2(-rintf(q.x), -rintf(q.y));
+    float2 r = ffma2(k, make_float2(kPiHi, kPiHi), a);
+    r = ffma2(k, make_float2(kPiLo, kPiLo), r);
+    const float2 sn = make_float2(__sinf(r.x), __sinf(r.y));
+    return ffma2(fmul2(sn, sn), inv, x);
+}
+
+__device__ __forceinline__ float4 snake4(float4 x, float4 alpha, float4 inv) {
+    const float2 lo = snake2(make_float2(x.x, x.y), make_float2(alpha.x, alpha.y), make_float2(inv.x, inv.y));
+    const float2 hi = snake2(make_float2(x.z, x.w), make_float2(alpha.z, alpha.w), make_float2(inv.z, inv.w));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) {

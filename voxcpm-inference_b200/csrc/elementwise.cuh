@@ -21,6 +21,7 @@ namespace vxb {
 // padding 3: src = t + k*d - 2*pad).
 __global__ void head_kernel(const float* __restrict__ z, const float* __restrict__ w /*[L][7]*/,
                             const float* __restrict__ bias, __half* __restrict__ out, int B, int L, int T) {
+    grid_dep_sync();
     const long long total = static_cast<long long>(B) * T * L;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -72,6 +73,7 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     const int rows = min(tt, T - t0) + halo;
     const bool cv = c < C;
     const float* xb = x + static_cast<long long>(b) * T * C;
+    grid_dep_sync();
     for (int r = ry; r < rows; r += RG) {
         const int t = t0 - halo + r;
         const bool ok = cv && t >= 0;
@@ -81,21 +83,16 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     if (cv) {
         const float4 al1 = *reinterpret_cast<const float4*>(a1 + c);
         const float4 iv1 = *reinterpret_cast<const float4*>(i1 + c);
-        for (int r = ry; r < rows; r += RG) {
-            float4 u = sh4[r * CG + cx];
-            u.x = snake(u.x, al1.x, iv1.x);
-            u.y = snake(u.y, al1.y, iv1.y);
-            u.z = snake(u.z, al1.z, iv1.z);
-            u.w = snake(u.w, al1.w, iv1.w);
-            sh4[r * CG + cx] = u;
-        }
+        for (int r = ry; r < rows; r += RG) sh4[r * CG + cx] = snake4(sh4[r * CG + cx], al1, iv1);
     }
     __syncthreads();
     if (!cv) return;
-    float4 wk[7];
+    float2 wlo[7], whi[7];
 #pragma unroll
-    for (int k = 0; k < 7; ++k)
-        wk[k] = make_float4(w[(c + 0) * 7 + k], w[(c + 1) * 7 + k], w[(c + 2) * 7 + k], w[(c + 3) * 7 + k]);
+    for (int k = 0; k < 7; ++k) {
+        wlo[k] = make_float2(w[(c + 0) * 7 + k], w[(c + 1) * 7 + k]);
+        whi[k] = make_float2(w[(c + 2) * 7 + k], w[(c + 3) * 7 + k]);
+    }
     const float4 bb = *reinterpret_cast<const float4*>(bias + c);
     const float4 al2 = *reinterpret_cast<const float4*>(a2 + c);
     const float4 iv2 = *reinterpret_cast<const float4*>(i2 + c);
@@ -103,17 +100,16 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     for (int q = ry; q < tt; q += RG) {
         const int t = t0 + q;
         if (t >= T) break;
-        float4 acc = bb;
+        float2 lo = make_float2(bb.x, bb.y), hi = make_float2(bb.z, bb.w);
 #pragma unroll
-        for (int k = 0; k < 7; ++k) {
+        for (int k = 0; k < 7; ++k) {  // taps in order, one fma per tap and lane
             const float4 u = sh4[(q + k * d) * CG + cx];
-            acc.x = fmaf(u.x, wk[k].x, acc.x);
-            acc.y = fmaf(u.y, wk[k].y, acc.y);
-            acc.z = fmaf(u.z, wk[k].z, acc.z);
-            acc.w = fmaf(u.w, wk[k].w, acc.w);
+            lo = ffma2(make_float2(u.x, u.y), wlo[k], lo);
+            hi = ffma2(make_float2(u.z, u.w), whi[k], hi);
         }
-        const __half2 h01 = __floats2half2_rn(snake(acc.x, al2.x, iv2.x), snake(acc.y, al2.y, iv2.y));
-        const __half2 h23 = __floats2half2_rn(snake(acc.z, al2.z, iv2.z), snake(acc.w, al2.w, iv2.w));
+        const float4 y = snake4(make_float4(lo.x, lo.y, hi.x, hi.y), al2, iv2);
+        const __half2 h01 = __floats2half2_rn(y.x, y.y);
+        const __half2 h23 = __floats2half2_rn(y.z, y.w);
         uint2 pk;
         pk.x = *reinterpret_cast<const uint32_t*>(&h01);
         pk.y = *reinterpret_cast<const uint32_t*>(&h23);
@@ -148,6 +144,7 @@ __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s,
     const int b = blockIdx.y;
     const int rows = min(kFinTT, T - t0) + 6;
     const float* sb = s + static_cast<long long>(b) * T * C;
+    grid_dep_sync();
     constexpr int kMaxLd = ((kFinTT + 6) * 32 + 255) / 256;  // float4 per thread for C <= 128
     float4 v[kMaxLd];
 #pragma unroll

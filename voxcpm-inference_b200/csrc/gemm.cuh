@@ -145,6 +145,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    grid_dep_sync();  // setup above overlaps the previous kernel's tail
 
     if (warp == 0) {
         if (lane == 0) {

@@ -146,6 +146,26 @@ int pick_bn(int64_t n) {
     return 16;
 }
 
+// Launches a decode kernel with programmatic stream serialisation (the
+// kernel calls grid_dep_sync before it touches activations), so its launch
+// and setup overlap the previous kernel; captured into graphs as
+// programmatic edges.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int AK, int BN, int EPI>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const CUtensorMap& to,
                   const GemmArgs& a, cudaStream_t st) {
@@ -161,8 +181,7 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     }
     const int tiles = a.m_tiles * a.n_tiles;
     dim3 g(std::max(1, std::min(tiles, num_sms(dev))));
-    gemm_kernel<AK, BN, EPI><<<g, threads, smem, st>>>(ta, tb, tr, to, a);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_pdl(gemm_kernel<AK, BN, EPI>, g, dim3(threads), smem, st, ta, tb, tr, to, a));
     return VXB_OK;
 }
 
@@ -747,8 +766,9 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
         __half* o = d.h16;
         rc = sink.kernel(
             [=](cudaStream_t s) {
-                head_kernel<<<grid_1d(int64_t(B) * T * L, 256), 256, 0, s>>>(z, w, bb, o, B, L, T);
-                return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
+                const cudaError_t e =
+                    launch_pdl(head_kernel, dim3(grid_1d(int64_t(B) * T * L, 256)), dim3(256), 0, s, z, w, bb, o, B, L, T);
+                return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
             },
             {"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4, "head_kernel"});
         if (rc) return rc;
@@ -799,13 +819,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     [=](cudaStream_t s) {
                         dim3 grid((C + ct - 1) / ct, (Tq + tt - 1) / tt, Bq);
                         const size_t sm = res_pre_smem(dl, tt, ct);
-                        if (ct == 64)
-                            res_pre_kernel<64><<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
-                                                                     u.a2.inv, h, C, Tq, dl, tt);
-                        else
-                            res_pre_kernel<32><<<grid, 256, sm, s>>>(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v,
-                                                                     u.a2.inv, h, C, Tq, dl, tt);
-                        return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
+                        const cudaError_t e =
+                            launch_pdl(ct == 64 ? res_pre_kernel<64> : res_pre_kernel<32>, grid, dim3(256), sm, s, x,
+                                       u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C, Tq, dl, tt);
+                        return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
                      double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
@@ -844,8 +861,9 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             rc = sink.kernel(
                 [=](cudaStream_t s) {
                     dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
-                    final_kernel<<<grid, 256, sizeof(float) * (kFinTT + 6) * C, s>>>(sx, w, fb, o, C, Tq);
-                    return cudaGetLastError() == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
+                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), sizeof(float) * (kFinTT + 6) * C,
+                                                     s, sx, w, fb, o, C, Tq);
+                    return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
                 {"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4, "final_kernel"});
             if (rc) return rc;

@@ -19,6 +19,7 @@
 
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "resunit.cuh"
 #include "gguf_reader.h"
 #include "vxb.h"
 
@@ -322,6 +323,110 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: weight type must be F16 or Q4_0");
     }
     return rc;
+}
+
+// ------------------------------------------------- fused residual unit --
+
+// fp32 activations [B][T][C] as a 3-D tensor (C fastest) for the fused
+// residual unit: box {32 channels, rows, 1 sequence}; rows outside [0, T)
+// read as zero and are not written.  swizzle: the 128-byte swizzle of the
+// residual / output boxes (none for the producers' slices).
+int make_tmap_x3d(CUtensorMap* m, const void* base, uint64_t C, uint64_t T, uint64_t B, uint32_t box_rows,
+                  bool swizzle) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (C * 4) % 16)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "residual-unit tensor needs 16-byte aligned base and rows");
+    const cuuint64_t dims[3] = {C, T, B};
+    const cuuint64_t strides[2] = {C * 4, C * 4 * T};
+    const cuuint32_t box[3] = {32, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (x3d) failed: " + std::to_string(r));
+    return VXB_OK;
+}
+
+template <int EPI>
+int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtensorMap& ty, const ResUnitArgs& a,
+                     int grid, cudaStream_t st) {
+    static bool attr[64] = {};  // per device
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
+    if (!attr[dev]) {
+        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRuSmemLimit));
+        attr[dev] = true;
+    }
+    const size_t smem = static_cast<size_t>(ru_layout(a.C).total);
+    CUDA_TRY(launch_pdl(resunit_kernel<EPI>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, a));
+    return VXB_OK;
+}
+
+struct ResUnitOp {
+    int epi = 0, grid = 1;
+    CUtensorMap tx{}, tr{}, ty{};
+    ResUnitArgs args{};
+    int launch(cudaStream_t st) const {
+        switch (epi) {
+            case kResPlain: return launch_resunit_t<kResPlain>(tx, tr, ty, args, grid, st);
+            case kResSnakeF16: return launch_resunit_t<kResSnakeF16>(tx, tr, ty, args, grid, st);
+            case kResSnakeF32: return launch_resunit_t<kResSnakeF32>(tx, tr, ty, args, grid, st);
+            default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported fused residual unit");
+        }
+    }
+    std::string kernel_name() const { return "resunit_kernel<" + std::to_string(epi) + ">"; }
+};
+
+// Whether a stage of C channels runs its residual units as one fused kernel
+// (the pointwise weights of the unit fit shared memory).
+bool resunit_fits(int C) { return C > 0 && C <= 128 && C % 32 == 0 && ru_layout(C).slots >= 2; }
+
+// Fused residual unit over x [B*T][C] -> y; w = the unit's pointwise weight
+// (GGUF bytes: F16 [C][C] or Q4_0 rows), dilation d <= 9.
+int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const float* x, void* y, int epi,
+                  const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
+                  const float* i2, const float* pb, const float* sa, const float* si, int B, int T, int sms,
+                  int* status) {
+    if (!resunit_fits(C) || d < 1 || d > 9 || B <= 0 || T <= 0)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: bad extents");
+    if (w_type != VXB_TYPE_F16 && w_type != VXB_TYPE_Q4_0)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: weight type must be F16 or Q4_0");
+    if (epi != kResPlain && (!sa || !si)) return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: no Snake");
+    op->epi = epi;
+    ResUnitArgs& a = op->args;
+    a = ResUnitArgs{};
+    a.x = x;
+    a.y = y;
+    a.a1 = a1;
+    a.i1 = i1;
+    a.dw = dw;
+    a.db = db;
+    a.a2 = a2;
+    a.i2 = i2;
+    a.w = static_cast<const uint8_t*>(w);
+    a.w_q4 = w_type == VXB_TYPE_Q4_0;
+    a.pb = pb;
+    a.sa = sa;
+    a.si = si;
+    a.T = T;
+    a.C = C;
+    a.d = d;
+    a.t_tiles = (T + kRuTT - 1) / kRuTT;
+    const int64_t tiles = int64_t(B) * a.t_tiles;
+    if (tiles > (int64_t(1) << 30)) return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: too many tiles");
+    a.tiles = static_cast<int>(tiles);
+    a.status = status;
+    op->grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+    int rc = make_tmap_x3d(&op->tx, x, C, T, B, kRuTT + 6 * d, false);
+    if (rc) return rc;
+    if ((rc = make_tmap_x3d(&op->tr, x, C, T, B, kRuTT, true))) return rc;
+    if (epi == kResSnakeF16) {
+        op->ty = op->tr;  // fp16 rows are stored from registers
+        return VXB_OK;
+    }
+    return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, true);
 }
 
 int grid_1d(int64_t work, int threads) {
@@ -809,6 +914,36 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
         for (int r = 0; r < 3; ++r) {
             const ResUnit& u = b.ru[r];
             const int dl = kDil[r];
+            if (resunit_fits(C)) {
+                // one fused kernel: snake1 -> dw -> snake2 -> pointwise -> + bias + x [-> Snake]
+                ResUnitOp op;
+                int epi = kResPlain;
+                const float *sa = nullptr, *si = nullptr;
+                void* y = nxt;
+                double out_bytes = 4;
+                if (r == 2 && !last_block) {
+                    epi = kResSnakeF16;
+                    sa = c->blocks[bi + 1].alpha.v;
+                    si = c->blocks[bi + 1].alpha.inv;
+                    y = d.s16;
+                    out_bytes = 2;
+                } else if (r == 2) {
+                    epi = kResSnakeF32;
+                    sa = c->final_alpha.v;
+                    si = c->final_alpha.inv;
+                }
+                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                                        u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status)))
+                    return rc;
+                rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
+                                 {"resunit_b" + std::to_string(bi) + "u" + std::to_string(r),
+                                  2.0 * C * C * double(n) + 20.0 * double(n) * C,
+                                  wbytes(u.pw) + double(n) * C * (4 + out_bytes), op.kernel_name()});
+                if (rc) return rc;
+                if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
+                std::swap(cur, nxt);
+                continue;
+            }
             {
                 const float* x = cur;
                 __half* h = d.h16;

@@ -137,7 +137,7 @@ def test_convt_matches_oracle(vxb, Cin, Cout, s, B, T, wt):
 
 def test_snake_error_bound_wide_range(vxb):
     """Snake over |alpha * x| up to 2e5 and alpha from 0.05 to 20 against fp64:
-    |y - y64| <= inv * 1.2e-6 + |x| * 2^-23 (the bound the kernel's sin^2
+    |y - y64| <= inv * 1.2e-6 + |x| * 2^-22 (the bound the kernel's sin^2
     states) plus the fp32 rounding of y."""
     mags = np.logspace(-4, 4, 2001)
     x = np.concatenate([mags, -mags, [0.0, 1e-30, 3.0e4, -9.9e3]]).astype(np.float32)
@@ -151,5 +151,5 @@ def test_snake_error_bound_wide_range(vxb):
     X64 = X.astype(np.float64)
     y64 = X64 + inv * np.sin(alpha.astype(np.float64) * X64) ** 2
     err = np.abs(y.cpu().numpy().astype(np.float64) - y64)
-    bound = inv * 1.2e-6 + np.abs(X64) * 2.0 ** -23 + np.abs(y64) * 2.0 ** -24
+    bound = inv * 1.2e-6 + np.abs(X64) * 2.0 ** -22 + np.abs(y64) * 2.0 ** -24
     assert np.all(err <= bound), float(np.max(err / bound))

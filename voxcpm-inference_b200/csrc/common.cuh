@@ -269,21 +269,25 @@ __device__ __forceinline__ uint32_t sw128_kmajor_off(uint32_t row, uint32_t k) {
 
 // ------------------------------------------------------------------ math --
 
-// sin(a)^2.  sin^2 has period pi, so a is reduced to r = a - k*pi with
-// k = rint(a / pi), |r| <= pi/2 (Cody-Waite: pi = hi + lo, hi = 201/64;
+// sin(a)^2.  sin^2 has period pi, so a is reduced to r = a - k*pi with k the
+// integer nearest a/pi, |r| <= pi/2 (Cody-Waite: pi = hi + lo, hi = 201/64;
 // fmaf keeps k*hi exact), and the hardware sine (__sinf, absolute error
-// below 2^-21.41 on [-pi, pi]) is squared.  The reduction adds less than
-// 2e-7 + 2e-11*|a| of phase error, so sin^2 is off by less than
-// 1.2e-6 + 4e-11*|a|, and Snake's y = x + inv * sin^2(alpha * x) by less than
-// inv * 1.2e-6 + |x| * 2^-23 (the last term includes rounding alpha * x).
-// No branch, no parity select.
+// below 2^-21.41 on [-pi, pi]) is squared.  k is rounded on the FMA pipe:
+// adding 1.5 * 2^23 leaves the nearest integer in the significand (exact for
+// |a/pi| < 2^22).  The reduction adds less than 2e-7 + 2e-11*|a| of phase
+// error, so sin^2 is off by less than 1.2e-6 + 4e-11*|a|, and Snake's
+// y = x + inv * sin^2(alpha * x) by less than inv * 1.2e-6 + |x| * 2^-23
+// (the last term includes rounding alpha * x).  For |a| >= 2^22 * pi any
+// value of sin^2 in [0, 1] is within inv <= |x| * 2^-22 of the true one, so
+// the bound inv * 1.2e-6 + |x| * 2^-22 holds for every x.  No branch.
 constexpr double kPi = 3.14159265358979323846;
 constexpr float kPiHi = 3.140625f;  // 201/64
 constexpr float kPiLo = static_cast<float>(kPi - 3.140625);
 constexpr float kInvPi = static_cast<float>(1.0 / kPi);
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 
 __device__ __forceinline__ float sin_sq(float a) {
-    const float k = rintf(a * kInvPi);
+    const float k = fmaf(a, kInvPi, kRoundMagic) - kRoundMagic;
     float r = fmaf(-k, kPiHi, a);
     r = fmaf(-k, kPiLo, r);
     const float s = __sinf(r);
@@ -350,11 +354,12 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
 
 // Snake on two lanes at once: the same operations and roundings as snake()
 // per lane (alpha*x, the period-pi reduction, the hardware sine, the square
-// and the final fma), paired where sm_100 has a two-lane instruction.
+// and the final fma), paired where sm_100 has a two-lane instruction
+// (-k = M - (a/pi + M) is exact, as is k = (a/pi + M) - M).
 __device__ __forceinline__ float2 snake2(float2 x, float2 alpha, float2 inv) {
     const float2 a = fmul2(alpha, x);
-    const float2 q = fmul2(a, make_float2(kInvPi, kInvPi));
-    const float2 k = make_float2(-rintf(q.x), -rintf(q.y));
+    const float2 t = ffma2(a, make_float2(kInvPi, kInvPi), make_float2(kRoundMagic, kRoundMagic));
+    const float2 k = ffma2(t, make_float2(-1.f, -1.f), make_float2(kRoundMagic, kRoundMagic));  // -nearest(a/pi)
     float2 r = ffma2(k, make_float2(kPiHi, kPiHi), a);
     r = ffma2(k, make_float2(kPiLo, kPiLo), r);
     const float2 sn = make_float2(__sinf(r.x), __sinf(r.y));

@@ -15,8 +15,8 @@
 // or copied (F16) into shared memory once per CTA; D in TMEM (two
 // accumulators of C columns, so tile i's epilogue overlaps tile i+1's work).
 //
-// Warp roles (448 threads):
-//   warp 9      loader: one TMA load per 32-channel slice of a tile, rows
+// Warp roles (480 threads):
+//   warp 9      slice loader: one TMA load per 32-channel slice of a tile, rows
 //               [t0 - 6d, t0 + 128) of the sequence (rows before its start
 //               read as zero: the causal padding), into a ring of slots that
 //               runs several slices (and tiles) ahead of the producers.
@@ -25,12 +25,13 @@
 //               computes the outputs q, q+d, q+2d, q+3d, whose 28 taps read
 //               only 10 distinct rows.
 //   warp 8      TMEM owner; lane 0 issues the MMAs (K steps of 16).
+//   warp 14     residual loader: the boxes [128 tokens][32 channels] of x
+//               that the epilogue adds, by TMA (128-byte swizzle) into a ring
+//               that runs ahead of the epilogue.
 //   warps 10-13 epilogue, one TMEM lane (= token) per thread, 32 channels at
-//               a time: the residual box [128 tokens][32 channels] arrives by
-//               TMA (128-byte swizzle, conflict-free per-row access) into a
-//               ring of boxes, y = D + b + x is written back in place and
-//               leaves by TMA; the fp16 variant stores straight from
-//               registers.
+//               a time: y = D + b + x is written back into the residual box
+//               (swizzled, conflict-free per-row access) and leaves by TMA;
+//               the fp16 variant stores straight from registers.
 // Every wait is bounded (the status word records a failure and the kernel
 // returns); the CTA always frees its TMEM.
 #pragma once
@@ -66,19 +67,21 @@ struct ResUnitArgs {
 constexpr int kRuTT = 128;                 // tokens per tile (MMA M)
 constexpr int kRuSlice = 32;               // channels per slice / residual box (one 128-byte row)
 constexpr int kRuMaxRows = kRuTT + 6 * 9;  // slice rows for dilation <= 9
-constexpr int kRuThreads = 448;
+constexpr int kRuThreads = 480;
 constexpr int kRuSlotBytes = kRuMaxRows * kRuSlice * 4;  // 182 rows x 128 B
 constexpr int kRuBoxBytes = kRuTT * kRuSlice * 4;        // 128 rows x 128 B
 constexpr int kRuNE = 3;                                 // residual boxes in flight
-constexpr int kRuMaxSlots = 6;
+constexpr int kRuNH = 2;                                 // H buffers
+constexpr int kRuMaxSlots = 4;
 constexpr int kRuBarBytes = 256;
 constexpr int kRuSmemLimit = 227 * 1024;
 
-// Shared-memory layout for C channels (all offsets 1024-byte aligned):
-//   W  KB k-blocks of [C rows][128 B]   H  KB k-blocks of [128 rows][128 B]
-//   E  kRuNE residual boxes             X  slots of [182 rows][128 B]
+// Shared-memory layout for C channels (W, H, E 1024-byte aligned):
+//   W  KB k-blocks of [C rows][128 B]   H  2 x KB k-blocks of [128 rows][128 B]
+//   E  kRuNE residual boxes             P  per-channel parameters (12 C floats)
+//   X  slots of [182 rows][128 B]
 struct RuLayout {
-    int kb, w_bytes, h_off, e_off, x_off, bar_off, slots, total;
+    int kb, w_bytes, h_off, e_off, p_off, x_off, bar_off, slots, total;
 };
 
 __host__ __device__ inline RuLayout ru_layout(int C) {
@@ -86,8 +89,9 @@ __host__ __device__ inline RuLayout ru_layout(int C) {
     L.kb = (C + 63) / 64;
     L.w_bytes = L.kb * C * 128;
     L.h_off = L.w_bytes;
-    L.e_off = L.h_off + L.kb * kRuTT * 128;
-    L.x_off = L.e_off + kRuNE * kRuBoxBytes;
+    L.e_off = L.h_off + kRuNH * L.kb * kRuTT * 128;
+    L.p_off = L.e_off + kRuNE * kRuBoxBytes;
+    L.x_off = L.p_off + (12 * C * 4 + 127) / 128 * 128;
     const int room = kRuSmemLimit - 1024 - kRuBarBytes - L.x_off;
     L.slots = room / kRuSlotBytes;
     if (L.slots > kRuMaxSlots) L.slots = kRuMaxSlots;
@@ -139,12 +143,22 @@ __global__ void __launch_bounds__(kRuThreads, 1)
     uint8_t* sH = smem + L.h_off;
     uint8_t* sE = smem + L.e_off;
     uint8_t* sX = smem + L.x_off;
+    // parameters: taps [7][C] (tap-major: one float4 per tap and channel quad),
+    // then snake1 alpha / inv, dw bias, snake2 alpha / inv, [C] each
+    float* sP = reinterpret_cast<float*>(smem + L.p_off);
+    float* sTap = sP;
+    float* sA1 = sP + 7 * C;
+    float* sI1 = sA1 + C;
+    float* sDB = sI1 + C;
+    float* sA2 = sDB + C;
+    float* sI2 = sA2 + C;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [NS] slice landed (TMA bytes)
     uint64_t* empty = full + kRuMaxSlots;                            // [NS] slice consumed (8 producer warps)
     uint64_t* efull = empty + kRuMaxSlots;                           // [NE] residual box landed
-    uint64_t* hfull = efull + kRuNE;                                 // H written (8 producer warps)
-    uint64_t* hempty = hfull + 1;                                    // H read by the MMAs
-    uint64_t* afull = hempty + 1;                                    // [2] accumulator complete
+    uint64_t* eempty = efull + kRuNE;                                // [NE] residual box released
+    uint64_t* hfull = eempty + kRuNE;                                // [NH] H written (8 producer warps)
+    uint64_t* hempty = hfull + kRuNH;                                // [NH] H read by the MMAs
+    uint64_t* afull = hempty + kRuNH;                                // [2] accumulator complete
     uint64_t* aempty = afull + 2;                                    // [2] accumulator drained (4 warps)
     uint64_t* done_bar = aempty + 2;                                 // all MMAs of the CTA complete
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -161,9 +175,14 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
-        for (int i = 0; i < kRuNE; ++i) mbar_init(&efull[i], 1);
-        mbar_init(hfull, 8);
-        mbar_init(hempty, 1);
+        for (int i = 0; i < kRuNE; ++i) {
+            mbar_init(&efull[i], 1);
+            mbar_init(&eempty[i], 1);
+        }
+        for (int i = 0; i < kRuNH; ++i) {
+            mbar_init(&hfull[i], 8);
+            mbar_init(&hempty[i], 1);
+        }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&afull[i], 1);
             mbar_init(&aempty[i], 4);
@@ -205,6 +224,15 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             *reinterpret_cast<uint4*>(sW + (k >> 6) * (C * 128) + sw128_kmajor_off(row, k & 63)) = v;
         }
     }
+    for (int i = threadIdx.x; i < C; i += kRuThreads) {
+#pragma unroll
+        for (int k = 0; k < 7; ++k) sTap[k * C + i] = args.dw[i * 7 + k];
+        sA1[i] = args.a1[i];
+        sI1[i] = args.i1[i];
+        sDB[i] = args.db[i];
+        sA2[i] = args.a2[i];
+        sI2[i] = args.i2[i];
+    }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -239,18 +267,46 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 }
             }
         }
+    } else if (warp == 14) {
+        if (lane == 0) {
+            // ----------------------------------------- residual loader --
+            int g = 0;
+            for (int tile = blockIdx.x; tile < args.tiles && !*abort_flag; tile += gridDim.x) {
+                const int b = tile / args.t_tiles;
+                const int t0 = (tile - b * args.t_tiles) * kRuTT;
+                bool ok = true;
+                for (int j = 0; j < nslices; ++j, ++g) {
+                    const int e = g % kRuNE;
+                    if (!mbar_wait(&eempty[e], ((g / kRuNE) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&efull[e], kRuBoxBytes);
+                    tma_load_3d(sE + e * kRuBoxBytes, &tmap_res, &efull[e], j * kRuSlice, t0, b);
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (globaltimer_ns() - t0 < 1000000ull) {
+                }
+            }
+        }
     } else if (warp < 8) {
         // ------------------------------------------------------ producers --
         const int tid = threadIdx.x;   // 0..255
         const int cx = tid & 7;        // float4 column within the 32-channel slice
         const int ry = tid >> 3;       // row group 0..31
-        // output sets {base, base+d, base+2d, base+3d}: blocks of 4d rows, d sets each
-        const int nblk = (kRuTT + 4 * d - 1) / (4 * d);
-        const int nsets = nblk * d;
+        // output sets {q0, q0+d, q0+2d, q0+3d}: blocks of 4d rows, d sets each;
+        // this thread takes sets ry and ry + 32 (at most 36 sets for d <= 9)
+        const int nsets = (kRuTT + 4 * d - 1) / (4 * d) * d;
+        auto set_q0 = [&](int set) { return set < nsets ? (set / d) * 3 * d + set : kRuTT; };  // kRuTT: no set
+        const int q0a = set_q0(ry), q0b = set_q0(ry + 32);
         int it = 0, i = 0;
         bool bail = false;
         for (int tile = blockIdx.x; tile < args.tiles && !bail; tile += gridDim.x, ++i) {
-            bool ok = mbar_wait(hempty, (i & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty);
+            const int hbuf = i & 1;
+            bool ok = mbar_wait(&hempty[hbuf], ((i >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty);
             if (ru_prod_bar_any(!ok || *abort_flag != 0)) break;
             const int b = tile / args.t_tiles;
             const int t0 = (tile - b * args.t_tiles) * kRuTT;
@@ -261,9 +317,22 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 ok = mbar_wait(&full[slot], (it / NS) & 1, abort_flag, args.status, kErrWaitFull);
                 const int c = s * kRuSlice + cx * 4;
                 if (ok) {
-                    const float4 al = *reinterpret_cast<const float4*>(args.a1 + c);
-                    const float4 iv = *reinterpret_cast<const float4*>(args.i1 + c);
-                    for (int r = ry; r < R; r += 32) xs[r * 8 + cx] = snake4(xs[r * 8 + cx], al, iv);
+                    // all rows of this thread loaded, activated and stored in
+                    // lockstep: independent chains for the scheduler
+                    constexpr int kRows = (kRuMaxRows + 31) / 32;
+                    const float4 al = *reinterpret_cast<const float4*>(sA1 + c);
+                    const float4 iv = *reinterpret_cast<const float4*>(sI1 + c);
+                    float4 v[kRows];
+#pragma unroll
+                    for (int m = 0; m < kRows; ++m) {
+                        const int r = min(ry + 32 * m, R - 1);
+                        v[m] = xs[r * 8 + cx];
+                    }
+#pragma unroll
+                    for (int m = 0; m < kRows; ++m) v[m] = snake4(v[m], al, iv);
+#pragma unroll
+                    for (int m = 0; m < kRows; ++m)
+                        if (ry + 32 * m < R) xs[(ry + 32 * m) * 8 + cx] = v[m];
                 }
                 if (ru_prod_bar_any(!ok)) {  // also orders snake1's writes before the taps read them
                     bail = true;
@@ -272,17 +341,19 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 float2 wlo[7], whi[7];
 #pragma unroll
                 for (int k = 0; k < 7; ++k) {
-                    wlo[k] = make_float2(args.dw[(c + 0) * 7 + k], args.dw[(c + 1) * 7 + k]);
-                    whi[k] = make_float2(args.dw[(c + 2) * 7 + k], args.dw[(c + 3) * 7 + k]);
+                    const float4 w4 = *reinterpret_cast<const float4*>(sTap + k * C + c);
+                    wlo[k] = make_float2(w4.x, w4.y);
+                    whi[k] = make_float2(w4.z, w4.w);
                 }
-                const float4 bb = *reinterpret_cast<const float4*>(args.db + c);
-                const float4 al2 = *reinterpret_cast<const float4*>(args.a2 + c);
-                const float4 iv2 = *reinterpret_cast<const float4*>(args.i2 + c);
-                uint8_t* hk = sH + (c >> 6) * (kRuTT * 128);
+                const float4 bb = *reinterpret_cast<const float4*>(sDB + c);
+                const float4 al2 = *reinterpret_cast<const float4*>(sA2 + c);
+                const float4 iv2 = *reinterpret_cast<const float4*>(sI2 + c);
+                uint8_t* hk = sH + (hbuf * L.kb + (c >> 6)) * (kRuTT * 128);
                 const int kin = c & 63;
-                for (int set = ry; set < nsets; set += 32) {
-                    const int blk = set / d;
-                    const int q0 = blk * 4 * d + (set - blk * d);  // outputs q0 + j*d, j < 4
+#pragma unroll 1
+                for (int e = 0; e < 2; ++e) {
+                    const int q0 = e == 0 ? q0a : q0b;  // outputs q0 + j*d, j < 4
+                    if (q0 >= kRuTT) break;
                     // rows q0 + m*d, m < 10 (output j uses m = j..j+6)
                     float4 u[10];
 #pragma unroll
@@ -290,25 +361,35 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                         const int rr = q0 + m * d;
                         u[m] = rr < R ? xs[rr * 8 + cx] : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
+                    // the four outputs in lockstep (no control flow until the stores)
+                    float2 lo[4], hi[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        lo[j] = make_float2(bb.x, bb.y);
+                        hi[j] = make_float2(bb.z, bb.w);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 7; ++k) {  // taps in order, one fma per tap and lane
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            lo[j] = ffma2(make_float2(u[j + k].x, u[j + k].y), wlo[k], lo[j]);
+                            hi[j] = ffma2(make_float2(u[j + k].z, u[j + k].w), whi[k], hi[j]);
+                        }
+                    }
+                    float4 yv[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) yv[j] = snake4(make_float4(lo[j].x, lo[j].y, hi[j].x, hi[j].y), al2, iv2);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int q = q0 + j * d;
-                        if (q >= kRuTT) break;
-                        uint2 pk = make_uint2(0u, 0u);
-                        if (q < tv) {
-                            float2 lo = make_float2(bb.x, bb.y), hi = make_float2(bb.z, bb.w);
-#pragma unroll
-                            for (int k = 0; k < 7; ++k) {  // taps in order, one fma per tap and lane
-                                lo = ffma2(make_float2(u[j + k].x, u[j + k].y), wlo[k], lo);
-                                hi = ffma2(make_float2(u[j + k].z, u[j + k].w), whi[k], hi);
-                            }
-                            const float4 yv = snake4(make_float4(lo.x, lo.y, hi.x, hi.y), al2, iv2);
-                            const __half2 h01 = __floats2half2_rn(yv.x, yv.y);
-                            const __half2 h23 = __floats2half2_rn(yv.z, yv.w);
-                            pk.x = *reinterpret_cast<const uint32_t*>(&h01);
-                            pk.y = *reinterpret_cast<const uint32_t*>(&h23);
+                        if (q < kRuTT) {
+                            const __half2 h01 = __floats2half2_rn(yv[j].x, yv[j].y);
+                            const __half2 h23 = __floats2half2_rn(yv[j].z, yv[j].w);
+                            uint2 pk;
+                            pk.x = q < tv ? *reinterpret_cast<const uint32_t*>(&h01) : 0u;
+                            pk.y = q < tv ? *reinterpret_cast<const uint32_t*>(&h23) : 0u;
+                            *reinterpret_cast<uint2*>(hk + sw128_kmajor_off(q, kin)) = pk;
                         }
-                        *reinterpret_cast<uint2*>(hk + sw128_kmajor_off(q, kin)) = pk;
                     }
                 }
                 // generic-proxy writes (snake1 in the slot, H) before the slot
@@ -319,7 +400,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             }
             if (bail) break;
             __syncwarp();
-            if (lane == 0) mbar_arrive(hfull);
+            if (lane == 0) mbar_arrive(&hfull[hbuf]);
         }
     } else if (warp == 8) {
         if (lane == 0) {
@@ -329,10 +410,10 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             for (int tile = blockIdx.x; tile < args.tiles; tile += gridDim.x, ++i) {
                 const int acc = i & 1;
                 if (!mbar_wait(&aempty[acc], ((i >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitAccum)) break;
-                if (!mbar_wait(hfull, i & 1, abort_flag, args.status, kErrWaitFull)) break;
+                if (!mbar_wait(&hfull[acc], (i >> 1) & 1, abort_flag, args.status, kErrWaitFull)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * acc_cols;
-                const uint32_t h_addr = smem_u32(sH);
+                const uint32_t h_addr = smem_u32(sH + acc * L.kb * (kRuTT * 128));
                 const uint32_t w_addr = smem_u32(sW);
                 for (int k16 = 0; k16 < C / 16; ++k16) {
                     const int kb = k16 >> 2, kk = k16 & 3;
@@ -340,7 +421,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                     const uint64_t bdesc = make_sdesc(w_addr + kb * (C * 128) + kk * 32, 16, 1024);
                     umma_f16(d_tmem, adesc, bdesc, idesc, k16 != 0);
                 }
-                umma_commit(hempty);
+                umma_commit(&hempty[acc]);
                 umma_commit(&afull[acc]);
             }
         }
@@ -350,20 +431,6 @@ __global__ void __launch_bounds__(kRuThreads, 1)
         const int row = q * 32 + lane;           // token within the tile
         const bool leader = warp == 10 && lane == 0;
         const int nbox = nslices;                // residual boxes per tile
-        const int my_tiles = (args.tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                             static_cast<int>(gridDim.x);
-        const int total_boxes = my_tiles * nbox;
-        auto load_box = [&](int g) {  // residual box g of this CTA's sequence of boxes
-            const int tile = blockIdx.x + (g / nbox) * gridDim.x;
-            const int j = g % nbox;
-            const int b = tile / args.t_tiles;
-            const int t0 = (tile - b * args.t_tiles) * kRuTT;
-            mbar_arrive_expect_tx(&efull[g % kRuNE], kRuBoxBytes);
-            tma_load_3d(sE + (g % kRuNE) * kRuBoxBytes, &tmap_res, &efull[g % kRuNE], j * kRuSlice, t0, b);
-        };
-        if (leader) {
-            for (int g = 0; g < kRuNE - 1 && g < total_boxes; ++g) load_box(g);
-        }
         int g = 0, i = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < args.tiles && ok; tile += gridDim.x, ++i) {
@@ -381,12 +448,6 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             const uint32_t t_row = tmem_base + acc * acc_cols + (static_cast<uint32_t>(q * 32) << 16);
             for (int j = 0; j < nbox; ++j, ++g) {
                 const int c0 = j * kRuSlice;
-                // keep kRuNE - 1 residual boxes in flight: box g + NE - 1 goes
-                // into the buffer of box g - 1 once that box's store has read it
-                if (leader && g + kRuNE - 1 < total_boxes) {
-                    bulk_wait_read<0>();
-                    load_box(g + kRuNE - 1);
-                }
                 uint32_t r[32];
                 tmem_ld16_issue(t_row + c0, r);
                 tmem_ld16_issue(t_row + c0 + 16, r + 16);
@@ -435,10 +496,17 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                     ok = false;
                     break;
                 }
-                if (leader && EPI != kResSnakeF16) {
-                    // rows past the sequence end fall outside the tensor and are not written
-                    tma_store_3d(&tmap_y, box, c0, t - row, b);
-                    bulk_commit();
+                if (leader) {
+                    if (EPI != kResSnakeF16) {
+                        // box g - 1 is released once its store has read it
+                        bulk_wait_read<0>();
+                        if (g > 0) mbar_arrive(&eempty[(g - 1) % kRuNE]);
+                        // rows past the sequence end fall outside the tensor and are not written
+                        tma_store_3d(&tmap_y, box, c0, t - row, b);
+                        bulk_commit();
+                    } else {
+                        mbar_arrive(&eempty[g % kRuNE]);  // read into registers; stored from there
+                    }
                 }
             }
         }

@@ -72,7 +72,7 @@ struct GemmCfg {
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kRawBytes = Q4 ? 7168 : 0;  // max(128*48, 64*112)
     static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
-    static constexpr int kEpiLD = 33;                            // ConvT: staged columns (+1 carry) per row
+    static constexpr int kEpiLD = 36;                            // ConvT: row stride (carry at 3, columns at 4..35)
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
     static constexpr int kResBytes = kChunk * 128 * 4;           // PW: fp32 [16 tokens][128 channels]
     static constexpr int kOut16Bytes = kChunk * 128 * 2;         // PW: fp16 [16 tokens][128 channels]
@@ -391,47 +391,68 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     }
                 }
             } else {
-                // ConvT: 32-column chunks staged in smem with one carried
-                // column (the previous token), then each thread emits the
-                // outputs of one (phase r, cout) pair for every group-th token.
+                // ConvT: 32-column chunks staged in smem, row stride 36 floats
+                // (16-byte stores at the minimum 4 wavefronts), the previous
+                // chunk's last column carried at index 3.  Then lane = output
+                // token (column c), each warp takes (phase r, 4 couts) quads:
+                //   y[(n*s + r)][co] = D[co*2s + r][c] + D[co*2s + s + r][c-1] + b[co]
+                // (the second term absent at a sequence start), reads along
+                // lanes without bank conflicts, one 16-byte store per quad.
                 const int s = args.s;
                 const int co_lo = mt * args.cpt;
                 const int cpt = min(args.cpt, args.cout - co_lo);
                 const int n_start = nt * (BN - 1) - 1;  // token of D column 0
-                const int npairs = s * args.cpt;        // <= 128
-                const int groups = 128 / npairs;
-                const int pair = et % npairs, grp = et / npairs;
-                const int r = pair / args.cpt, co_l = pair - (pair / args.cpt) * args.cpt;
-                const bool active = grp < groups && co_l < cpt;
-                const float bias = active ? args.bias[co_lo + co_l] : 0.f;
-                const int rowA = (co_l * 2 * s + r) * Cfg::kEpiLD;
-                const int rowB = rowA + s * Cfg::kEpiLD;
+                const int qpr = args.cpt / 4;           // cout quads per phase
+                const int nquads = s * qpr;
+                const int ew = et >> 5;                 // warp within the group
                 float* out = static_cast<float*>(args.out);
+                float4 bq[8];                           // bias of this warp's quads (nquads <= 32)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int qd = ew + 4 * k;
+                    const int co = (qd - (qd / qpr) * qpr) * 4;
+                    bq[k] = (qd < nquads && co < cpt) ? *reinterpret_cast<const float4*>(args.bias + co_lo + co)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
                 float carry = 0.f;
+                float* rowp = sG + row * Cfg::kEpiLD;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     float v[32];
                     tmem_ld16(t_row + c0, v);
                     tmem_ld16(t_row + c0 + 16, v + 16);
-                    sG[row * Cfg::kEpiLD] = carry;  // column c0 - 1
+                    rowp[3] = carry;  // column c0 - 1
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) sG[row * Cfg::kEpiLD + 1 + j] = v[j];
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(rowp + 4 + 4 * j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                     carry = v[31];
                     epi_bar(bar_id);
-                    if (active) {
-                        // output columns c in [c0, min(c0+32, BN)) with c >= 1; token n = n_start + c
-                        const int c_end = min(c0 + 32, BN);
-                        int c = c0 + grp;
-                        int n = n_start + c;
-                        int tpos = (n % args.seq_len + args.seq_len) % args.seq_len;
-                        for (; c < c_end; c += groups, n += groups) {
-                            if (c >= 1 && n < args.N) {
-                                float y = sG[rowA + (c - c0) + 1] + bias;
-                                if (tpos != 0) y += sG[rowB + (c - c0)];
-                                out[(static_cast<size_t>(n) * s + r) * args.cout + co_lo + co_l] = y;
+                    const int c = c0 + lane;
+                    const int n = n_start + c;
+                    if (c >= 1 && c < BN && n < args.N) {
+                        const bool seq_start = (n % args.seq_len) == 0;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int qd = ew + 4 * k;
+                            if (qd >= nquads) break;
+                            const int r = qd / qpr;
+                            const int co = (qd - r * qpr) * 4;
+                            if (co >= cpt) continue;
+                            const float* pa = sG + (co * 2 * s + r) * Cfg::kEpiLD + 4 + lane;  // D[co*2s + r][c]
+                            const float* pb = pa + s * Cfg::kEpiLD - 1;                        // D[co*2s + s + r][c - 1]
+                            const int rs = 2 * s * Cfg::kEpiLD;                                // next cout
+                            float4 y;
+                            y.x = pa[0] + bq[k].x;
+                            y.y = pa[rs] + bq[k].y;
+                            y.z = pa[2 * rs] + bq[k].z;
+                            y.w = pa[3 * rs] + bq[k].w;
+                            if (!seq_start) {
+                                y.x += pb[0];
+                                y.y += pb[rs];
+                                y.z += pb[2 * rs];
+                                y.w += pb[3 * rs];
                             }
-                            tpos += groups;
-                            while (tpos >= args.seq_len) tpos -= args.seq_len;
+                            *reinterpret_cast<float4*>(out + (static_cast<size_t>(n) * s + r) * args.cout + co_lo + co) = y;
                         }
                     }
                     epi_bar(bar_id);

@@ -276,7 +276,7 @@ int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t 
 // (so that every A tile starts on a 16-byte boundary).
 int convt_cpt(int s) {
     for (int c = 128 / (2 * s); c > 0; --c)
-        if ((2 * s * c) % 8 == 0) return c;
+        if ((2 * s * c) % 8 == 0 && c % 4 == 0) return c;
     return 0;
 }
 
@@ -288,6 +288,7 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     if (Cin <= 0 || Cout <= 0 || s <= 0 || s > 32 || N <= 0 || N * s > (int64_t(1) << 31) - 1)
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad extents");
     if (Cin % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: Cin must be a multiple of 8");
+    if (Cout % 4) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: Cout must be a multiple of 4");
     const int M = 2 * s * Cout;
     const int cpt = convt_cpt(s);
     if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");

@@ -132,8 +132,11 @@ inline int res_pre_tt(int C, int T, int B, int sms) {
 // Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c])
 // over the (already Snake-activated) last stage.  A block covers kFinTT time
 // steps of one sequence: rows [t0 - 6, t0 + kFinTT) are staged in shared
-// memory with 16-byte loads; each warp then reduces one output at a time over
-// channels (lanes) and taps.  Requires C % 4 == 0 and C <= 128.
+// memory with 16-byte loads.  Each warp then computes 8 consecutive outputs
+// at once: lane = channel quad, the 14 rows they read are loaded once, every
+// lane accumulates its channels' share of all 8 sums, and one exchange of
+// halves (xor 16, 8, 4) followed by xor 2, 1 leaves each sum complete on four
+// lanes (9 shuffles for 8 outputs).  Requires C % 4 == 0 and C <= 128.
 constexpr int kFinTT = 64;
 
 __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
@@ -163,7 +166,7 @@ __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s,
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // each lane owns channel quads lane, lane + 32, ... (C <= 128: at most one)
+    // each lane owns channel quad `lane` (C <= 128)
     float4 wk[7];
     const bool lv = lane < c4n;
 #pragma unroll
@@ -172,24 +175,52 @@ __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s,
         wk[k] = lv ? make_float4(w[(cc + 0) * 7 + k], w[(cc + 1) * 7 + k], w[(cc + 2) * 7 + k], w[(cc + 3) * 7 + k])
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int tt = warp; tt < kFinTT; tt += 8) {
-        const int t = t0 + tt;
-        if (t >= T) break;
-        float acc = 0.f;
-        if (lv) {
+    const int q0 = warp * 8;  // this warp's outputs q0..q0+7 (smem rows q0..q0+13)
+    if (t0 + q0 >= T) return;
+    float acc[8];
 #pragma unroll
-            for (int k = 0; k < 7; ++k) {
-                const float4 v = fsh4[(tt + k) * c4n + lane];
-                acc = fmaf(v.x, wk[k].x, acc);
-                acc = fmaf(v.y, wk[k].y, acc);
-                acc = fmaf(v.z, wk[k].z, acc);
-                acc = fmaf(v.w, wk[k].w, acc);
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 14; ++r) {
+        const float4 u = (lv && q0 + r < rows) ? fsh4[(q0 + r) * c4n + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int k = r - j;  // tap of row q0 + r for output q0 + j
+            if (k >= 0 && k < 7) {
+                acc[j] = fmaf(u.x, wk[k].x, acc[j]);
+                acc[j] = fmaf(u.y, wk[k].y, acc[j]);
+                acc[j] = fmaf(u.z, wk[k].z, acc[j]);
+                acc[j] = fmaf(u.w, wk[k].w, acc[j]);
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) y[static_cast<long long>(b) * T + t] = tanhf(acc + bias);
     }
+    // exchange halves: after xor 16 a lane keeps 4 sums (outputs 0-3 or 4-7),
+    // after xor 8 two, after xor 4 one
+    const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+    float a4[4], a2[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float give = h16 ? acc[i] : acc[i + 4];
+        const float keep = h16 ? acc[i + 4] : acc[i];
+        a4[i] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float give = h8 ? a4[i] : a4[i + 2];
+        const float keep = h8 ? a4[i + 2] : a4[i];
+        a2[i] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
+    }
+    float sum;
+    {
+        const float give = h4 ? a2[0] : a2[1];
+        const float keep = h4 ? a2[1] : a2[0];
+        sum = keep + __shfl_xor_sync(0xffffffffu, give, 4);
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    const int j = (h16 ? 4 : 0) + (h8 ? 2 : 0) + (h4 ? 1 : 0);  // output this lane's sum belongs to
+    const int t = t0 + q0 + j;
+    if ((lane & 3) == 0 && t < T) y[static_cast<long long>(b) * T + t] = tanhf(sum + bias);
 }
 
 // y[n][c] = snake(x[n][c]) for an fp32 [N][C] tensor.

@@ -76,7 +76,9 @@ struct GemmCfg {
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
     static constexpr int kResBytes = kChunk * 128 * 4;           // PW: fp32 [16 tokens][128 channels]
     static constexpr int kOut16Bytes = kChunk * 128 * 2;         // PW: fp16 [16 tokens][128 channels]
-    static constexpr int kGroupEpiBytes = EPI == kEpiConvT ? 128 * kEpiLD * 4 : 2 * kResBytes + 2 * kOut16Bytes;
+    static constexpr int kEpiRing = 4;                           // PW: residual / output chunk buffers
+    static constexpr int kGroupEpiBytes =
+        EPI == kEpiConvT ? 128 * kEpiLD * 4 : kEpiRing * kResBytes + kEpiRing * kOut16Bytes;
     static constexpr int kEpiBytes = 2 * kGroupEpiBytes;         // two epilogue warpgroups
     static constexpr int kBudget = 220 * 1024 - kEpiBytes - 1024 - kBarrierBytes;
     static constexpr int kStagesFit = kBudget / kStageBytes;
@@ -84,7 +86,7 @@ struct GemmCfg {
     static constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);   // two accumulators
     static constexpr int kAccStride = BN < 32 ? 32 : BN;
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
-    static_assert((3 * kStages + 8) * 8 + 8 <= kBarrierBytes, "barrier area too small");
+    static_assert((3 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
     static constexpr int kThreads = Q4 ? 512 : 384;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
     static_assert(kStages >= 2, "pipeline needs two stages");
@@ -109,8 +111,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     uint64_t* empty_bar = ready_bar + S;  // stage consumed by the MMAs
     uint64_t* tfull_bar = empty_bar + S;  // accumulator [2] complete
     uint64_t* tempty_bar = tfull_bar + 2; // accumulator [2] drained
-    uint64_t* res_bar = tempty_bar + 2;   // PW residual chunk [group][2] landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 4);
+    uint64_t* res_bar = tempty_bar + 2;   // PW residual chunk [group][4] landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -128,8 +130,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull_bar[i], 1);
             mbar_init(&tempty_bar[i], 4);
-            mbar_init(&res_bar[2 * i], 1);
-            mbar_init(&res_bar[2 * i + 1], 1);
+            for (int j = 0; j < 4; ++j) mbar_init(&res_bar[4 * i + j], 1);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -313,7 +314,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
         const int row = q * 32 + lane;           // D row of this thread
         const int et = (threadIdx.x - 128) & 127;  // 0..127 within the group
         float* sG = sE + eg * (Cfg::kGroupEpiBytes / 4);
-        uint64_t* rbar = res_bar + 2 * eg;
+        uint64_t* rbar = res_bar + 4 * eg;
         int tl = eg;                             // local tile index (this group takes tl = eg, eg+2, ...)
         int g_chunk = 0;                         // PW chunks processed by this group (buffer parity)
         for (int tile = blockIdx.x + eg * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, tl += 2) {
@@ -326,10 +327,14 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
             const int mt = tile % args.m_tiles;
             const int nt = tile / args.m_tiles;
             if (EPI == kEpiPW) {
-                // Chunks of 16 tokens: the residual chunk arrives by TMA into
-                // one of two buffers (the next chunk's load is issued before
-                // this one is processed), the result is written in place
-                // (fp32) or to the fp16 buffer, and a TMA store sends it out.
+                // Chunks of 16 tokens, numbered g across this group's tiles
+                // (BN/16 per tile).  Four residual buffers: the load of chunk
+                // g + 2 (possibly of the group's next tile) is issued while
+                // chunk g is processed, once the store of chunk g - 2 has
+                // read its buffer; the result is written in place (fp32) or
+                // to the chunk's fp16 buffer, and a TMA store sends it out.
+                // Chunks past N load zeros and store nothing (TMA clips).
+                constexpr int CPT = BN / Cfg::kChunk;
                 const int m0 = mt * Cfg::kBM;
                 const int m = m0 + row;
                 const int n_start = nt * BN;
@@ -340,30 +345,32 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                                      ? (args.snake_inv ? args.snake_inv[m] : 1.0f / (al + 1e-9f))
                                      : 0.f;
                 const bool has_res = args.res != nullptr;
-                const int nch = min(BN / Cfg::kChunk, (args.N - n_start + Cfg::kChunk - 1) / Cfg::kChunk);
-                auto issue_res = [&](int ch, int gidx) {
-                    const int j = gidx & 1;
-                    bulk_wait_read<0>();  // no store may still read the buffer being refilled
-                    mbar_arrive_expect_tx(&rbar[j], Cfg::kResBytes);
-                    tma_load_2d(sG + j * (Cfg::kResBytes / 4), &tmap_res, &rbar[j], m0, n_start + ch * Cfg::kChunk);
+                auto issue_res = [&](int gl) {  // residual chunk gl of this group's sequence, if any
+                    const int tt = blockIdx.x + (eg + 2 * (gl / CPT)) * gridDim.x;
+                    if (tt >= num_tiles) return;
+                    const int jb = gl & 3;
+                    mbar_arrive_expect_tx(&rbar[jb], Cfg::kResBytes);
+                    tma_load_2d(sG + jb * (Cfg::kResBytes / 4), &tmap_res, &rbar[jb], (tt % args.m_tiles) * Cfg::kBM,
+                                (tt / args.m_tiles) * BN + (gl % CPT) * Cfg::kChunk);
                 };
-                if (has_res && et == 0 && nch > 0) issue_res(0, g_chunk);
+                if (has_res && et == 0 && g_chunk == 0) {
+                    issue_res(0);
+                    issue_res(1);
+                }
 #pragma unroll 1
-                for (int ch = 0; ch < nch; ++ch, ++g_chunk) {
-                    const int j = g_chunk & 1;
-                    if (has_res && et == 0 && ch + 1 < nch) issue_res(ch + 1, g_chunk + 1);
+                for (int ch = 0; ch < CPT; ++ch, ++g_chunk) {
+                    const int j = g_chunk & 3;
+                    if (et == 0) {
+                        bulk_wait_read<1>();  // the store of chunk g - 2 has read its buffers
+                        if (has_res) issue_res(g_chunk + 2);
+                    }
                     float v[16];
                     tmem_ld16(t_row + ch * Cfg::kChunk, v);
                     float* rbuf = sG + j * (Cfg::kResBytes / 4);
-                    __half* obuf = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sG) + 2 * Cfg::kResBytes +
-                                                             j * Cfg::kOut16Bytes);
+                    __half* obuf = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sG) +
+                                                             Cfg::kEpiRing * Cfg::kResBytes + j * Cfg::kOut16Bytes);
                     bool w_ok = true;
-                    if (has_res) {
-                        w_ok = mbar_wait(&rbar[j], (g_chunk >> 1) & 1, abort_flag, args.status, kErrWaitFull);
-                    } else {
-                        if (et == 0) bulk_wait_read<1>();  // the store that last used buffer j has read it
-                        epi_bar(bar_id);
-                    }
+                    if (has_res) w_ok = mbar_wait(&rbar[j], (g_chunk >> 2) & 1, abort_flag, args.status, kErrWaitFull);
                     if (w_ok) {
                         float r[16];
 #pragma unroll

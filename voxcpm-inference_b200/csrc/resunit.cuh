@@ -30,8 +30,8 @@
 //               that runs ahead of the epilogue.
 //   warps 10-13 epilogue, one TMEM lane (= token) per thread, 32 channels at
 //               a time: y = D + b + x is written back into the residual box
-//               (swizzled, conflict-free per-row access) and leaves by TMA;
-//               the fp16 variant stores straight from registers.
+//               (swizzled, conflict-free per-row access; the fp16 variant as
+//               dense 64-byte rows) and leaves by TMA.
 // Every wait is bounded (the status word records a failure and the kernel
 // returns); the CTA always frees its TMEM.
 #pragma once
@@ -84,16 +84,18 @@ struct RuLayout {
     int kb, w_bytes, h_off, e_off, p_off, x_off, bar_off, slots, total;
 };
 
-__host__ __device__ inline RuLayout ru_layout(int C) {
+// hg: the H tiles come from global memory (the pointwise-only variant), no
+// parameters or slices.
+__host__ __device__ inline RuLayout ru_layout(int C, bool hg = false) {
     RuLayout L;
     L.kb = (C + 63) / 64;
     L.w_bytes = L.kb * C * 128;
     L.h_off = L.w_bytes;
     L.e_off = L.h_off + kRuNH * L.kb * kRuTT * 128;
     L.p_off = L.e_off + kRuNE * kRuBoxBytes;
-    L.x_off = L.p_off + (12 * C * 4 + 127) / 128 * 128;
+    L.x_off = L.p_off + (hg ? 0 : (12 * C * 4 + 127) / 128 * 128);
     const int room = kRuSmemLimit - 1024 - kRuBarBytes - L.x_off;
-    L.slots = room / kRuSlotBytes;
+    L.slots = hg ? 0 : room / kRuSlotBytes;
     if (L.slots > kRuMaxSlots) L.slots = kRuMaxSlots;
     L.bar_off = L.x_off + (L.slots > 0 ? L.slots : 0) * kRuSlotBytes;
     L.total = L.bar_off + kRuBarBytes + 1024;
@@ -130,12 +132,18 @@ __device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-template <int EPI>
+// HG = true: the pointwise-only variant for stages whose fused form does not
+// fit shared memory (C <= 192): the H tiles (the prologue kernel's fp16
+// output [B*T][C]) arrive by TMA (tmap_h, boxes {64 k, 128 tokens}, 128-byte
+// swizzle) into the H buffers, issued by the loader warp; the producer warps
+// idle.  Everything else is the same kernel.
+template <int EPI, bool HG>
 __global__ void __launch_bounds__(kRuThreads, 1)
     resunit_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_res,
-                   const __grid_constant__ CUtensorMap tmap_y, const ResUnitArgs args) {
+                   const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_h,
+                   const ResUnitArgs args) {
     const int C = args.C;
-    const RuLayout L = ru_layout(C);
+    const RuLayout L = ru_layout(C, HG);
     const int NS = L.slots;
     extern __shared__ uint8_t ru_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ru_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -167,8 +175,8 @@ __global__ void __launch_bounds__(kRuThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nslices = C / kRuSlice;
     const int d = args.d, halo = 6 * d, R = kRuTT + halo;  // slot rows
-    const int acc_cols = 64 * L.kb;
-    const uint32_t tmem_cols = 2 * acc_cols <= 128 ? 128 : 256;
+    const int acc_cols = L.kb == 3 ? 256 : 64 * L.kb;  // accumulator stride: a power of two
+    const uint32_t tmem_cols = 2 * acc_cols <= 128 ? 128 : (2 * acc_cols <= 256 ? 256 : 512);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             mbar_init(&eempty[i], 1);
         }
         for (int i = 0; i < kRuNH; ++i) {
-            mbar_init(&hfull[i], 8);
+            mbar_init(&hfull[i], HG ? 1 : 8);
             mbar_init(&hempty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -190,9 +198,9 @@ __global__ void __launch_bounds__(kRuThreads, 1)
         mbar_init(done_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
-        prefetch_tmap(&tmap_x);
+        prefetch_tmap(HG ? &tmap_h : &tmap_x);
         prefetch_tmap(&tmap_res);
-        if (EPI != kResSnakeF16) prefetch_tmap(&tmap_y);
+        prefetch_tmap(&tmap_y);
     }
     if (warp == 8) tmem_alloc(tmem_slot, tmem_cols);
 
@@ -224,7 +232,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             *reinterpret_cast<uint4*>(sW + (k >> 6) * (C * 128) + sw128_kmajor_off(row, k & 63)) = v;
         }
     }
-    for (int i = threadIdx.x; i < C; i += kRuThreads) {
+    for (int i = threadIdx.x; i < (HG ? 0 : C); i += kRuThreads) {
 #pragma unroll
         for (int k = 0; k < 7; ++k) sTap[k * C + i] = args.dw[i * 7 + k];
         sA1[i] = args.a1[i];
@@ -243,9 +251,22 @@ __global__ void __launch_bounds__(kRuThreads, 1)
     if (warp == 9) {
         if (lane == 0) {
             // --------------------------------------------------- loader --
+            if (HG) {
+                int i = 0;
+                for (int tile = blockIdx.x; tile < args.tiles && !*abort_flag; tile += gridDim.x, ++i) {
+                    const int hbuf = i & 1;
+                    if (!mbar_wait(&hempty[hbuf], ((i >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) break;
+                    const int b = tile / args.t_tiles;
+                    const int t0 = (tile - b * args.t_tiles) * kRuTT;
+                    mbar_arrive_expect_tx(&hfull[hbuf], static_cast<uint32_t>(L.kb) * kRuTT * 128);
+                    for (int kb = 0; kb < L.kb; ++kb)
+                        tma_load_2d(sH + (hbuf * L.kb + kb) * (kRuTT * 128), &tmap_h, &hfull[hbuf], kb * 64,
+                                    b * args.T + t0);
+                }
+            }
             const uint32_t tx = static_cast<uint32_t>(R) * kRuSlice * 4;
             int it = 0;
-            for (int tile = blockIdx.x; tile < args.tiles && !*abort_flag; tile += gridDim.x) {
+            for (int tile = blockIdx.x; tile < (HG ? 0 : args.tiles) && !*abort_flag; tile += gridDim.x) {
                 const int b = tile / args.t_tiles;
                 const int t0 = (tile - b * args.t_tiles) * kRuTT;
                 bool ok = true;
@@ -292,7 +313,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 }
             }
         }
-    } else if (warp < 8) {
+    } else if (warp < 8 && !HG) {
         // ------------------------------------------------------ producers --
         const int tid = threadIdx.x;   // 0..255
         const int cx = tid & 7;        // float4 column within the 32-channel slice
@@ -425,7 +446,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 umma_commit(&afull[acc]);
             }
         }
-    } else {
+    } else if (warp >= 10 && warp < 14) {
         // ------------------------------------------------------- epilogue --
         const int q = warp & 3;                  // TMEM lane quadrant
         const int row = q * 32 + lane;           // token within the tile
@@ -461,6 +482,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 const bool landed = mbar_wait(&efull[g % kRuNE], (g / kRuNE) & 1, abort_flag, args.status,
                                               kErrWaitFull);
                 uint8_t* box = sE + (g % kRuNE) * kRuBoxBytes;
+                uint2 h16[8];  // kResSnakeF16: the box's fp16 results, written once every thread has read the box
                 if (landed) {
 #pragma unroll
                     for (int cq = 0; cq < 8; ++cq) {
@@ -478,17 +500,22 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                             v = snake4(v, sa, si);
                         }
                         if (EPI == kResSnakeF16) {
-                            if (valid) {
-                                const __half2 h01 = __floats2half2_rn(v.x, v.y);
-                                const __half2 h23 = __floats2half2_rn(v.z, v.w);
-                                uint2 pk;
-                                pk.x = *reinterpret_cast<const uint32_t*>(&h01);
-                                pk.y = *reinterpret_cast<const uint32_t*>(&h23);
-                                *reinterpret_cast<uint2*>(static_cast<__half*>(args.y) + n * C + c0 + cq * 4) = pk;
-                            }
+                            const __half2 h01 = __floats2half2_rn(v.x, v.y);
+                            const __half2 h23 = __floats2half2_rn(v.z, v.w);
+                            h16[cq].x = *reinterpret_cast<const uint32_t*>(&h01);
+                            h16[cq].y = *reinterpret_cast<const uint32_t*>(&h23);
                         } else {
                             *px = v;
                         }
+                    }
+                }
+                if (EPI == kResSnakeF16) {
+                    // dense fp16 rows of 64 B in the box's first 8 KB (the layout of
+                    // the unswizzled fp16 output map) once all rows are read
+                    epi_bar(2);
+                    if (landed) {
+#pragma unroll
+                        for (int cq = 0; cq < 8; ++cq) *reinterpret_cast<uint2*>(box + row * 64 + cq * 8) = h16[cq];
                     }
                 }
                 fence_proxy_async_smem();
@@ -497,16 +524,12 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                     break;
                 }
                 if (leader) {
-                    if (EPI != kResSnakeF16) {
-                        // box g - 1 is released once its store has read it
-                        bulk_wait_read<0>();
-                        if (g > 0) mbar_arrive(&eempty[(g - 1) % kRuNE]);
-                        // rows past the sequence end fall outside the tensor and are not written
-                        tma_store_3d(&tmap_y, box, c0, t - row, b);
-                        bulk_commit();
-                    } else {
-                        mbar_arrive(&eempty[g % kRuNE]);  // read into registers; stored from there
-                    }
+                    // box g - 1 is released once its store has read it
+                    bulk_wait_read<0>();
+                    if (g > 0) mbar_arrive(&eempty[(g - 1) % kRuNE]);
+                    // rows past the sequence end fall outside the tensor and are not written
+                    tma_store_3d(&tmap_y, box, c0, t - row, b);
+                    bulk_commit();
                 }
             }
         }

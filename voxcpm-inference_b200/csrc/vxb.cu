@@ -333,64 +333,82 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
 // read as zero and are not written.  swizzle: the 128-byte swizzle of the
 // residual / output boxes (none for the producers' slices).
 int make_tmap_x3d(CUtensorMap* m, const void* base, uint64_t C, uint64_t T, uint64_t B, uint32_t box_rows,
-                  bool swizzle) {
+                  bool swizzle, bool f16 = false) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (C * 4) % 16)
+    const uint64_t es = f16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (C * es) % 16)
         return fail(VXB_ERR_INVALID_ARGUMENT, "residual-unit tensor needs 16-byte aligned base and rows");
     const cuuint64_t dims[3] = {C, T, B};
-    const cuuint64_t strides[2] = {C * 4, C * 4 * T};
+    const cuuint64_t strides[2] = {C * es, C * es * T};
     const cuuint32_t box[3] = {32, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+    CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                     const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (x3d) failed: " + std::to_string(r));
     return VXB_OK;
 }
 
-template <int EPI>
-int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtensorMap& ty, const ResUnitArgs& a,
-                     int grid, cudaStream_t st) {
+template <int EPI, bool HG>
+int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtensorMap& ty, const CUtensorMap& th,
+                     const ResUnitArgs& a, int grid, cudaStream_t st) {
     static bool attr[64] = {};  // per device
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
     if (!attr[dev]) {
-        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRuSmemLimit));
+        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kRuSmemLimit));
         attr[dev] = true;
     }
-    const size_t smem = static_cast<size_t>(ru_layout(a.C).total);
-    CUDA_TRY(launch_pdl(resunit_kernel<EPI>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, a));
+    const size_t smem = static_cast<size_t>(ru_layout(a.C, HG).total);
+    CUDA_TRY(launch_pdl(resunit_kernel<EPI, HG>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, th, a));
     return VXB_OK;
 }
 
 struct ResUnitOp {
     int epi = 0, grid = 1;
-    CUtensorMap tx{}, tr{}, ty{};
+    bool hg = false;  // pointwise-only variant (H from the prologue kernel)
+    CUtensorMap tx{}, tr{}, ty{}, th{};
     ResUnitArgs args{};
     int launch(cudaStream_t st) const {
-        switch (epi) {
-            case kResPlain: return launch_resunit_t<kResPlain>(tx, tr, ty, args, grid, st);
-            case kResSnakeF16: return launch_resunit_t<kResSnakeF16>(tx, tr, ty, args, grid, st);
-            case kResSnakeF32: return launch_resunit_t<kResSnakeF32>(tx, tr, ty, args, grid, st);
+        switch (epi * 2 + (hg ? 1 : 0)) {
+            case kResPlain * 2: return launch_resunit_t<kResPlain, false>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 2: return launch_resunit_t<kResSnakeF16, false>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 2: return launch_resunit_t<kResSnakeF32, false>(tx, tr, ty, th, args, grid, st);
+            case kResPlain * 2 + 1: return launch_resunit_t<kResPlain, true>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 2 + 1: return launch_resunit_t<kResSnakeF16, true>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 2 + 1: return launch_resunit_t<kResSnakeF32, true>(tx, tr, ty, th, args, grid, st);
             default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported fused residual unit");
         }
     }
-    std::string kernel_name() const { return "resunit_kernel<" + std::to_string(epi) + ">"; }
+    std::string kernel_name() const {
+        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "true" : "false") + ">";
+    }
 };
 
 // Whether a stage of C channels runs its residual units as one fused kernel
 // (the pointwise weights of the unit fit shared memory).
 bool resunit_fits(int C) { return C > 0 && C <= 128 && C % 32 == 0 && ru_layout(C).slots >= 2; }
 
+// Whether the pointwise conv (+ bias + residual [-> Snake]) of a stage of C
+// channels runs as the pointwise-only variant of that kernel (tokens as M,
+// all C output channels in one tile: h is read once, no padded m-tiles).
+bool resunit_hg_fits(int C) {
+    return C > 0 && C <= 192 && C % 32 == 0 && ru_layout(C, true).total <= kRuSmemLimit;
+}
+
 // Fused residual unit over x [B*T][C] -> y; w = the unit's pointwise weight
 // (GGUF bytes: F16 [C][C] or Q4_0 rows), dilation d <= 9.
+// With h16 (the prologue's fp16 output [B*T][C]) the pointwise-only variant.
 int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const float* x, void* y, int epi,
                   const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
                   const float* i2, const float* pb, const float* sa, const float* si, int B, int T, int sms,
-                  int* status) {
-    if (!resunit_fits(C) || d < 1 || d > 9 || B <= 0 || T <= 0)
+                  int* status, const void* h16 = nullptr) {
+    op->hg = h16 != nullptr;
+    if (!(op->hg ? resunit_hg_fits(C) : resunit_fits(C)) || d < 1 || d > 9 || B <= 0 || T <= 0)
         return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: bad extents");
     if (w_type != VXB_TYPE_F16 && w_type != VXB_TYPE_Q4_0)
         return fail(VXB_ERR_INVALID_ARGUMENT, "fused residual unit: weight type must be F16 or Q4_0");
@@ -422,11 +440,13 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
     op->grid = static_cast<int>(std::min<int64_t>(tiles, sms));
     int rc = make_tmap_x3d(&op->tx, x, C, T, B, kRuTT + 6 * d, false);
     if (rc) return rc;
-    if ((rc = make_tmap_x3d(&op->tr, x, C, T, B, kRuTT, true))) return rc;
-    if (epi == kResSnakeF16) {
-        op->ty = op->tr;  // fp16 rows are stored from registers
-        return VXB_OK;
+    if (op->hg) {
+        if ((rc = make_tmap_f16(&op->th, h16, C, uint64_t(B) * T, uint64_t(C) * 2, 64, kRuTT))) return rc;
+    } else {
+        op->th = op->tx;  // unused
     }
+    if ((rc = make_tmap_x3d(&op->tr, x, C, T, B, kRuTT, true))) return rc;
+    if (epi == kResSnakeF16) return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, false, true);
     return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, true);
 }
 
@@ -963,6 +983,35 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
                      double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
                 if (rc) return rc;
+            }
+            if (resunit_hg_fits(C) && int64_t(B) * ((Tb + kRuTT - 1) / kRuTT) >= sms) {
+                // pointwise conv + bias + residual [-> Snake], tokens as M (all C channels in one tile)
+                ResUnitOp op;
+                int epi = kResPlain;
+                const float *sa = nullptr, *si = nullptr;
+                void* y = nxt;
+                double out_bytes = 4;
+                if (r == 2 && !last_block) {
+                    epi = kResSnakeF16;
+                    sa = c->blocks[bi + 1].alpha.v;
+                    si = c->blocks[bi + 1].alpha.inv;
+                    y = d.s16;
+                    out_bytes = 2;
+                } else if (r == 2) {
+                    epi = kResSnakeF32;
+                    sa = c->final_alpha.v;
+                    si = c->final_alpha.inv;
+                }
+                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                                        u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status, d.h16)))
+                    return rc;
+                rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
+                                 {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
+                                  wbytes(u.pw) + double(n) * C * (2 + 4 + out_bytes), op.kernel_name()});
+                if (rc) return rc;
+                if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
+                std::swap(cur, nxt);
+                continue;
             }
             GemmOp op;
             double out_bytes;

@@ -385,7 +385,7 @@ struct ResUnitOp {
         }
     }
     std::string kernel_name() const {
-        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "true" : "false") + ">";
+        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "1" : "0") + ">";  // as ncu names it
     }
 };
 
@@ -981,7 +981,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                         return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
-                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
+                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel<" + std::to_string(res_pre_ct(C)) + ">"});
                 if (rc) return rc;
             }
             if (resunit_hg_fits(C) && int64_t(B) * ((Tb + kRuTT - 1) / kRuTT) >= sms) {

@@ -52,11 +52,19 @@ struct GemmArgs {
     int* status;              // device status word (bounded-wait failures)
 };
 
-// Raw Q4_0 bytes staged per k step: K-major 128 rows x 48 B (two 18-byte
-// blocks from a 16-byte aligned start), MN-major 64 rows x 112 B (up to five
-// blocks covering a 128-wide m range from a 16-byte aligned start).
-constexpr int kRawKBox = 48;
-constexpr int kRawMNBox = 112;
+// Q4_0 weights are staged per k step from their split form (nibbles
+// [rows][blocks][16 B] and fp16 scales [rows][...], see vxb_prepare):
+//   K-major (pointwise): 128 rows x 2 blocks -> nibbles 128 x 32 B, scales
+//     128 x 8 (the aligned group of 8 holding the step's 2 scales);
+//   MN-major (transposed conv): 64 k rows x the up to 5 blocks covering a
+//     128-wide m range -> nibbles 64 x 80 B, scales 64 x 16 (from the aligned
+//     group of 8 holding the first block's scale: the 5 fit in 16).
+constexpr int kQ4KNibBox = 32;     // bytes
+constexpr int kQ4KScaleBox = 8;    // fp16 values
+constexpr int kQ4MNNibBox = 80;    // bytes
+constexpr int kQ4MNScaleBox = 16;  // fp16 values
+constexpr int kQ4KScaleOff = 128 * kQ4KNibBox;   // scale area within the raw stage area
+constexpr int kQ4MNScaleOff = 64 * kQ4MNNibBox;
 
 // Pointwise epilogue chunk: tokens per residual load / output store.  The
 // host builds the residual and output tensor maps with boxes of
@@ -70,7 +78,7 @@ struct GemmCfg {
     static constexpr int kBK = 64;
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kRawBytes = Q4 ? 7168 : 0;  // max(128*48, 64*112)
+    static constexpr int kRawBytes = Q4 ? 7168 : 0;  // max(128*(32+16), 64*(80+32))
     static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
     static constexpr int kEpiLD = 36;                            // ConvT: row stride (carry at 3, columns at 4..35)
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
@@ -96,7 +104,7 @@ template <int AK, int BN, int EPI>
 __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_res, const __grid_constant__ CUtensorMap tmap_out,
-                const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmap_scale, const GemmArgs args) {
     constexpr bool kQ4 = AK >= kAQ4K;
     constexpr bool kMN = (AK == kAF16MN) || (AK == kAQ4MN);
     using Cfg = GemmCfg<BN, kQ4, EPI>;
@@ -136,6 +144,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
         fence_barrier_init();
         prefetch_tmap(&tmap_b);
         prefetch_tmap(&tmap_a);
+        if (kQ4) prefetch_tmap(&tmap_scale);
         if (EPI == kEpiPW) {
             prefetch_tmap(&tmap_out);
             if (args.res) prefetch_tmap(&tmap_res);
@@ -166,8 +175,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     uint8_t* r_dst = b_dst + Cfg::kBBytes;
                     const int k0 = kb * Cfg::kBK;
                     uint32_t tx = kTx;
-                    if (AK == kAQ4K) tx += 128 * kRawKBox;
-                    if (AK == kAQ4MN) tx += 64 * kRawMNBox;
+                    if (AK == kAQ4K) tx += 128 * (kQ4KNibBox + 2 * kQ4KScaleBox);
+                    if (AK == kAQ4MN) tx += 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox);
                     mbar_arrive_expect_tx(&full_bar[st], tx);
                     if (AK == kAF16K) {
                         tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
@@ -175,9 +184,11 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                         tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
                         tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
                     } else if (AK == kAQ4K) {
-                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], (kb * 36) & ~15, m0);
+                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], kb * kQ4KNibBox, m0);
+                        tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &full_bar[st], (2 * kb) & ~7, m0);
                     } else {
-                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], ((m0 >> 5) * 18) & ~15, k0);
+                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], (m0 >> 5) * 16, k0);
+                        tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &full_bar[st], (m0 >> 5) & ~7, k0);
                     }
                     tma_load_2d(b_dst, &tmap_b, &full_bar[st], k0, n_start);
                 }
@@ -245,58 +256,48 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                 const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
                 const int k0 = kb * Cfg::kBK;
                 if (AK == kAQ4K) {
-                    // thread t -> row m0 + t, two blocks (k0..k0+63) at byte
-                    // offset (36 kb) & 15 of its 48-byte raw row
+                    // thread t -> row m0 + t: the step's two blocks (k0..k0+63),
+                    // nibbles 32 B, scales at positions (2 kb) & 7 of the row's 8
                     const int m = m0 + t;
-                    const int off = (kb * 36) & 15;
+                    const uint4* nib = reinterpret_cast<const uint4*>(raw + t * kQ4KNibBox);
+                    const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + t * kQ4KScaleBox + ((2 * kb) & 7);
 #pragma unroll
                     for (int hb = 0; hb < 2; ++hb) {
                         const bool valid = m < args.M && k0 + hb * 32 < args.K;
-                        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(raw + t * kRawKBox + off + hb * 18);
-                        const __half2 d2 = __half2half2(valid ? __ushort_as_half(b16[0]) : __float2half_rn(0.f));
-                        uint32_t q4[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            q4[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
+                        const __half2 d2 = __half2half2(valid ? sc[hb] : __float2half_rn(0.f));
+                        const uint4 q = nib[hb];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             // chunk c: elements 8c..8c+7 = low nibbles of bytes 0-7 / 8-15, then high nibbles
-                            const int wsel = (c & 1) * 2;
                             *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
-                                q4_dequant8(q4[wsel], q4[wsel + 1], c >= 2, d2);
+                                q4_dequant8((c & 1) ? q.z : q.x, (c & 1) ? q.w : q.y, c >= 2, d2);
                         }
                     }
                 } else {
-                    // work item = (k row, block) of the up-to-five blocks that
-                    // intersect [m0, m0 + 128); m0 is a multiple of 8, so a block
-                    // lands on four aligned 16-byte chunks of the MN-major tile
+                    // thread t -> k row kl = t % 64 and blocks h, h + 2, h + 4 (h = t / 64)
+                    // of the up to five that intersect [m0, m0 + 128); m0 is a
+                    // multiple of 8, so a block lands on four aligned 16-byte
+                    // chunks of the MN-major tile
                     const int b_first = m0 >> 5;
                     const int nblk = ((m0 + 127) >> 5) - b_first + 1;
-                    const int base_off = b_first * 18 - ((b_first * 18) & ~15);
-                    const int items = 64 * nblk;
+                    const int kl = t & 63, h = t >> 6;
+                    const __half* sc = reinterpret_cast<const __half*>(raw + kQ4MNScaleOff) + kl * kQ4MNScaleBox + (b_first & 7);
 #pragma unroll
-                    for (int i3 = 0; i3 < 3; ++i3) {
-                        const int item = t + i3 * 128;
-                        if (item >= items) break;
-                        const int kl = item / nblk;
-                        const int bi = item - kl * nblk;
+                    for (int j = 0; j < 3; ++j) {
+                        const int bi = h + 2 * j;
+                        if (bi >= nblk) break;
                         const int blk = b_first + bi;
                         const bool valid = k0 + kl < args.K && blk * 32 < args.M;
-                        const uint16_t* b16 =
-                            reinterpret_cast<const uint16_t*>(raw + kl * kRawMNBox + base_off + bi * 18);
-                        const __half2 d2 = __half2half2(valid ? __ushort_as_half(b16[0]) : __float2half_rn(0.f));
-                        uint32_t q4[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            q4[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
+                        const __half2 d2 = __half2half2(valid ? sc[bi] : __float2half_rn(0.f));
+                        const uint4 q = *reinterpret_cast<const uint4*>(raw + kl * kQ4MNNibBox + bi * 16);
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             const int ml = blk * 32 + c * 8 - m0;
                             if (ml < 0 || ml >= 128) continue;
-                            const int wsel = (c & 1) * 2;
-                            const int h = ml >> 6, mc = (ml & 63) >> 3;
-                            const uint32_t off = h * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
-                            *reinterpret_cast<uint4*>(a_dst + off) = q4_dequant8(q4[wsel], q4[wsel + 1], c >= 2, d2);
+                            const int hh = ml >> 6, mc = (ml & 63) >> 3;
+                            const uint32_t off = hh * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
+                            *reinterpret_cast<uint4*>(a_dst + off) =
+                                q4_dequant8((c & 1) ? q.z : q.x, (c & 1) ? q.w : q.y, c >= 2, d2);
                         }
                     }
                 }

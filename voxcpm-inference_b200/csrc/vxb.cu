@@ -129,13 +129,69 @@ int num_sms(int dev) {
     return cache[dev];
 }
 
-// A conv weight as a GEMM operand: fp16 bytes, or Q4_0 blocks in rows padded
-// to `pitch` bytes (a multiple of 16, for TMA).
+// A conv weight as a GEMM operand: fp16 bytes, or Q4_0 blocks split into
+// their 16 nibble bytes (p: [rows][blocks][16 B], row pitch `pitch` =
+// 16 * blocks) and their fp16 scales (s: [rows][spitch bytes], spitch a
+// multiple of 16) -- both 16-byte aligned for TMA, the values unchanged.
 struct WView {
     const void* p = nullptr;
     int type = 0;
     int pitch = 0;
+    const void* s = nullptr;
+    int spitch = 0;
 };
+
+// Q4_0 rows [rows][nblk x 18 B] -> nibbles [rows][nblk][16 B] + scales
+// [rows][spitch / 2] fp16, one thread per block (the bytes are copied, not
+// re-quantised).
+__global__ void q4_split_kernel(const uint8_t* __restrict__ src, int64_t rows, int nblk, uint8_t* __restrict__ q,
+                                uint8_t* __restrict__ sc, int spitch) {
+    const int64_t total = rows * nblk;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / nblk;
+        const int bi = static_cast<int>(i - r * nblk);
+        const uint8_t* blk = src + i * 18;
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = uint32_t(blk[2 + 4 * j]) | (uint32_t(blk[3 + 4 * j]) << 8) | (uint32_t(blk[4 + 4 * j]) << 16) |
+                   (uint32_t(blk[5 + 4 * j]) << 24);
+        *reinterpret_cast<uint4*>(q + i * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        sc[r * spitch + bi * 2] = blk[0];
+        sc[r * spitch + bi * 2 + 1] = blk[1];
+    }
+}
+
+// Device buffers of a split Q4_0 weight.
+struct SplitQ4 {
+    void* q = nullptr;
+    void* s = nullptr;
+    int pitch = 0, spitch = 0;
+};
+
+// Splits a Q4_0 weight of `rows` rows of `inner` values (stream-ordered).
+int split_q4(const void* w, int64_t inner, int64_t rows, cudaStream_t st, bool async_alloc, SplitQ4* out) {
+    if (inner % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 rows must hold whole blocks");
+    const int nblk = static_cast<int>(inner / 32);
+    out->pitch = nblk * 16;
+    out->spitch = (nblk * 2 + 15) / 16 * 16;
+    const size_t qb = size_t(out->pitch) * rows, sb = size_t(out->spitch) * rows;
+    if (async_alloc) {
+        CUDA_TRY(cudaMallocAsync(&out->q, qb, st));
+        CUDA_TRY(cudaMallocAsync(&out->s, sb, st));
+    } else {
+        CUDA_TRY(cudaMalloc(&out->q, qb));
+        CUDA_TRY(cudaMalloc(&out->s, sb));
+    }
+    CUDA_TRY(cudaMemsetAsync(out->s, 0, sb, st));
+    const int64_t total = rows * nblk;
+    const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    q4_split_kernel<<<std::max(grid, 1), 256, 0, st>>>(static_cast<const uint8_t*>(w), rows, nblk,
+                                                        static_cast<uint8_t*>(out->q), static_cast<uint8_t*>(out->s),
+                                                        out->spitch);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
 
 // --------------------------------------------------------------- launching --
 
@@ -169,6 +225,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 template <int AK, int BN, int EPI>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const CUtensorMap& to,
+                  const CUtensorMap& ts,
                   const GemmArgs& a, cudaStream_t st) {
     constexpr int smem = GemmCfg<BN, (AK >= kAQ4K), EPI>::kSmemBytes;
     constexpr int threads = GemmCfg<BN, (AK >= kAQ4K), EPI>::kThreads;
@@ -182,22 +239,22 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     }
     const int tiles = a.m_tiles * a.n_tiles;
     dim3 g(std::max(1, std::min(tiles, num_sms(dev))));
-    CUDA_TRY(launch_pdl(gemm_kernel<AK, BN, EPI>, g, dim3(threads), smem, st, ta, tb, tr, to, a));
+    CUDA_TRY(launch_pdl(gemm_kernel<AK, BN, EPI>, g, dim3(threads), smem, st, ta, tb, tr, to, ts, a));
     return VXB_OK;
 }
 
 template <int AK, int EPI>
-int launch_gemm_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr,
+int launch_gemm_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const CUtensorMap& ts,
                    const CUtensorMap& to, const GemmArgs& a, cudaStream_t st) {
     switch (bn) {
         case 16:
-            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 16, EPI>(ta, tb, tr, to, a, st);
+            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 16, EPI>(ta, tb, tr, to, ts, a, st);
             return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise tiles are at least 32 wide");
-        case 32: return launch_gemm_t<AK, 32, EPI>(ta, tb, tr, to, a, st);
-        case 64: return launch_gemm_t<AK, 64, EPI>(ta, tb, tr, to, a, st);
-        case 128: return launch_gemm_t<AK, 128, EPI>(ta, tb, tr, to, a, st);
+        case 32: return launch_gemm_t<AK, 32, EPI>(ta, tb, tr, to, ts, a, st);
+        case 64: return launch_gemm_t<AK, 64, EPI>(ta, tb, tr, to, ts, a, st);
+        case 128: return launch_gemm_t<AK, 128, EPI>(ta, tb, tr, to, ts, a, st);
         case 256:
-            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 256, EPI>(ta, tb, tr, to, a, st);
+            if constexpr (EPI == kEpiConvT) return launch_gemm_t<AK, 256, EPI>(ta, tb, tr, to, ts, a, st);
             return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise tiles are at most 128 wide");
         default: return fail(VXB_ERR_INVALID_ARGUMENT, "bad BN");
     }
@@ -210,14 +267,14 @@ std::string gemm_kernel_name(const GemmOp& op);
 struct GemmOp {
     int akind = 0, epi = 0, bn = 16;
     dim3 grid;
-    CUtensorMap ta{}, tb{}, tr{}, to{};
+    CUtensorMap ta{}, tb{}, tr{}, to{}, ts{};  // ts: Q4_0 scales (a copy of ta for fp16 weights)
     GemmArgs args{};
     int launch(cudaStream_t st) const {
         switch (akind * 2 + epi) {
-            case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, ta, tb, tr, to, args, st);
-            case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, ta, tb, tr, to, args, st);
-            case kAF16MN * 2 + kEpiConvT: return launch_gemm_bn<kAF16MN, kEpiConvT>(bn, ta, tb, tr, to, args, st);
-            case kAQ4MN * 2 + kEpiConvT: return launch_gemm_bn<kAQ4MN, kEpiConvT>(bn, ta, tb, tr, to, args, st);
+            case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, ta, tb, tr, ts, to, args, st);
+            case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, ta, tb, tr, ts, to, args, st);
+            case kAF16MN * 2 + kEpiConvT: return launch_gemm_bn<kAF16MN, kEpiConvT>(bn, ta, tb, tr, ts, to, args, st);
+            case kAQ4MN * 2 + kEpiConvT: return launch_gemm_bn<kAQ4MN, kEpiConvT>(bn, ta, tb, tr, ts, to, args, st);
             default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported GEMM kind");
         }
     }
@@ -262,10 +319,14 @@ int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t 
     if (w.type == VXB_TYPE_F16) {
         op->akind = kAF16K;
         rc = make_tmap_f16(&op->ta, w.p, K, M, uint64_t(K) * 2, 64, 128);
+        op->ts = op->ta;
     } else if (w.type == VXB_TYPE_Q4_0) {
         if (K % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 pointwise needs K % 32 == 0");
         op->akind = kAQ4K;
-        rc = make_tmap_u8(&op->ta, w.p, w.pitch, M, kRawKBox, 128);
+        // per k step: 2 blocks of nibbles (32 B) and their 2 scales (box of 8) for 128 rows
+        rc = make_tmap_u8(&op->ta, w.p, w.pitch, M, kQ4KNibBox, 128);
+        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M, kQ4KScaleBox, 128);
+        return rc;
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: weight type must be F16 or Q4_0");
     }
@@ -316,10 +377,14 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
         if ((uint64_t(M) * 2) % 16) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: 2s*Cout must be a multiple of 8");
         op->akind = kAF16MN;
         rc = make_tmap_f16(&op->ta, w.p, M, Cin, uint64_t(M) * 2, 64, 64);
+        op->ts = op->ta;
     } else if (w.type == VXB_TYPE_Q4_0) {
         if (M % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 convt needs 2s*Cout % 32 == 0");
         op->akind = kAQ4MN;
-        rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kRawMNBox, 64);
+        // per k step: up to 5 blocks of nibbles (80 B) and 16 scales around them for 64 rows
+        rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kQ4MNNibBox, 64);
+        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, Cin, kQ4MNScaleBox, 64);
+        return rc;
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: weight type must be F16 or Q4_0");
     }
@@ -476,10 +541,11 @@ struct DevTensor {
     int64_t ne[4] = {1, 1, 1, 1};
     void* dev = nullptr;     // the GGUF bytes, unchanged
     size_t nbytes = 0;
-    void* q4pad = nullptr;   // Q4_0 GEMM weights: same blocks, rows padded to 16 B (made by vxb_prepare)
-    int q4pitch = 0;
+    SplitQ4 q4;              // Q4_0 GEMM weights: nibbles and scales split (made by vxb_prepare)
     int64_t nelem() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
-    WView view() const { return type == VXB_TYPE_Q4_0 ? WView{q4pad, type, q4pitch} : WView{dev, type, 0}; }
+    WView view() const {
+        return type == VXB_TYPE_Q4_0 ? WView{q4.q, type, q4.pitch, q4.s, q4.spitch} : WView{dev, type, 0, nullptr, 0};
+    }
 };
 
 struct Vec {  // derived fp32 vector (+ inverse for Snake alphas)
@@ -624,7 +690,8 @@ int vxb_close(vxb_ctx* c) {
     if (c->plan) free_plan(c->plan.get());
     for (auto& kv : c->tensors) {
         cudaFree(kv.second.dev);
-        cudaFree(kv.second.q4pad);
+        cudaFree(kv.second.q4.q);
+        cudaFree(kv.second.q4.s);
     }
     for (void* p : c->derived_allocs) cudaFree(p);
     cudaFree(c->status);
@@ -672,7 +739,8 @@ int vxb_upload_tensor(vxb_ctx* c, const char* name, int type, const int64_t* ne,
     auto it = c->tensors.find(t.name);
     if (it != c->tensors.end()) {
         cudaFree(it->second.dev);
-        cudaFree(it->second.q4pad);
+        cudaFree(it->second.q4.q);
+        cudaFree(it->second.q4.s);
     }
     c->tensors[t.name] = t;
     c->prepared = false;
@@ -765,8 +833,8 @@ int derive_taps(vxb_ctx* c, const std::string& name, int C, float** out) {
 }
 
 // Binds a conv weight used as a GEMM operand ([outer rows][inner]); for Q4_0
-// it also makes the TMA-friendly copy: the same 18-byte blocks, every row
-// padded with zeros to a multiple of 16 bytes.
+// it also makes the TMA-friendly copy: each 18-byte block split into its 16
+// nibble bytes and its fp16 scale (two 16-byte aligned arrays).
 int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t outer, const DevTensor** out) {
     auto it = c->tensors.find(name);
     if (it == c->tensors.end()) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
@@ -776,13 +844,11 @@ int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t out
     if (t->nelem() != inner * outer) return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
     if (t->type == VXB_TYPE_Q4_0) {
         if (inner % 32) return fail(VXB_ERR_INVALID_FORMAT, name + ": Q4_0 rows must hold whole blocks");
-        const size_t row = size_t(inner) / 32 * 18, pitch = (row + 15) / 16 * 16;
-        cudaFree(t->q4pad);
-        t->q4pad = nullptr;
-        CUDA_TRY(cudaMalloc(&t->q4pad, pitch * outer));
-        CUDA_TRY(cudaMemsetAsync(t->q4pad, 0, pitch * outer, c->stream));
-        CUDA_TRY(cudaMemcpy2DAsync(t->q4pad, pitch, t->dev, row, row, outer, cudaMemcpyDeviceToDevice, c->stream));
-        t->q4pitch = static_cast<int>(pitch);
+        cudaFree(t->q4.q);
+        cudaFree(t->q4.s);
+        t->q4 = SplitQ4{};
+        int rc = split_q4(t->dev, inner, outer, c->stream, false, &t->q4);
+        if (rc) return rc;
     }
     *out = t;
     return VXB_OK;
@@ -1243,28 +1309,24 @@ extern "C" int vxb_snake(const float* x, const float* alpha, int C, int64_t N, f
 
 namespace {
 
-// Unit entry points receive the GGUF bytes as they are; a Q4_0 weight whose
-// rows are not a multiple of 16 bytes gets a stream-ordered padded copy.
+// Unit entry points receive the GGUF bytes as they are; a Q4_0 weight gets a
+// stream-ordered split copy (nibbles + scales), freed after the launch.
 struct PaddedQ4 {
-    void* p = nullptr;
+    SplitQ4 q4;
     cudaStream_t s = nullptr;
     ~PaddedQ4() {
-        if (p) cudaFreeAsync(p, s);
+        if (q4.q) cudaFreeAsync(q4.q, s);
+        if (q4.s) cudaFreeAsync(q4.s, s);
     }
 };
 
 int view_for(const void* w, int w_type, int64_t inner, int64_t rows, cudaStream_t st, PaddedQ4* tmp, WView* out) {
-    *out = WView{w, w_type, 0};
+    *out = WView{w, w_type, 0, nullptr, 0};
     if (w_type != VXB_TYPE_Q4_0) return VXB_OK;
-    if (inner % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 rows must hold whole blocks");
-    const size_t row = size_t(inner) / 32 * 18, pitch = (row + 15) / 16 * 16;
-    out->pitch = static_cast<int>(pitch);
-    if (pitch == row && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return VXB_OK;
     tmp->s = st;
-    CUDA_TRY(cudaMallocAsync(&tmp->p, pitch * rows, st));
-    CUDA_TRY(cudaMemsetAsync(tmp->p, 0, pitch * rows, st));
-    CUDA_TRY(cudaMemcpy2DAsync(tmp->p, pitch, w, row, row, rows, cudaMemcpyDeviceToDevice, st));
-    out->p = tmp->p;
+    int rc = split_q4(w, inner, rows, st, true, &tmp->q4);
+    if (rc) return rc;
+    *out = WView{tmp->q4.q, w_type, tmp->q4.pitch, tmp->q4.s, tmp->q4.spitch};
     return VXB_OK;
 }
 

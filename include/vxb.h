@@ -180,6 +180,20 @@ VXB_API int vxb_snake(const float* x, const float* alpha, int C, int64_t N, floa
 VXB_API int vxb_pointwise(const void* w, int w_type, int K, int M, const void* x_f16, int64_t N, const float* bias,
                   const float* res, const float* snake_alpha, int out_f16, void* y, void* stream);
 
+/* One residual unit on device buffers (reference residual_unit_forward_l2,
+ * src/audio-vae.cpp:1481-1518): y = x + pw(snake2(dw_d(snake1(x)))) + pb,
+ * then, when out_alpha is given, the next layer's Snake with that alpha
+ * (fp16 output if out_f16, else fp32).  x and y are [batch][T][C], channels
+ * fastest; w is the unit's pointwise weight as GGUF bytes (F16 [C][C] or
+ * Q4_0 rows of C/32 blocks); dw the depthwise taps [C][7] fp32; a1, a2, db,
+ * pb, out_alpha fp32 [C]; 1 <= d <= 9.  Runs the fused residual-unit kernel
+ * for C <= 128 (C % 32 == 0), the prologue + pointwise-only kernel for
+ * C <= 192 when the batch has a tile of 128 tokens per SM, else the prologue
+ * + pointwise GEMM.  Enqueued on `stream`; temporaries are stream-ordered. */
+VXB_API int vxb_residual_unit(const void* w, int w_type, int C, int d, const float* x, int batch, int T,
+                              const float* a1, const float* dw, const float* db, const float* a2, const float* pb,
+                              const float* out_alpha, int out_f16, void* y, void* stream);
+
 /* Causal transposed conv (kernel 2s, stride s, cropped to T*s) as one
  * implicit GEMM with a col2im epilogue: x fp16 [B*T][Cin] -> y fp32
  * [B*T*s][Cout]; W is the folded GGUF [2s*Cout, Cin] weight (F16 or Q4_0).

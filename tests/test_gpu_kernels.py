@@ -153,3 +153,56 @@ def test_snake_error_bound_wide_range(vxb):
     err = np.abs(y.cpu().numpy().astype(np.float64) - y64)
     bound = inv * 1.2e-6 + np.abs(X64) * 2.0 ** -22 + np.abs(y64) * 2.0 ** -24
     assert np.all(err <= bound), float(np.max(err / bound))
+
+
+@pytest.mark.parametrize("C,d,B,T,wt,snk,out16", [
+    (96, 9, 2, 3000, "q4", False, False),    # fused residual-unit kernel
+    (96, 1, 1, 700, "f16", True, False),     # fused, final Snake (fp32)
+    (64, 3, 3, 400, "q4", True, True),       # fused, next block's Snake (fp16)
+    (192, 3, 2, 9600, "q4", False, False),   # prologue + pointwise-only kernel (150 tiles of 128 tokens)
+    (192, 9, 2, 9600, "f16", True, True),    # the same with Snake + fp16 output
+    (192, 1, 1, 500, "q4", False, False),    # prologue + pointwise GEMM (few tiles)
+    (384, 3, 1, 300, "f16", True, False),    # prologue + pointwise GEMM (wide stage)
+])
+def test_residual_unit_matches_oracle(vxb, C, d, B, T, wt, snk, out16):
+    """vxb_residual_unit (every kernel path the decoder uses for a residual
+    unit) against the oracle's snake -> dilated dw -> snake -> pointwise
+    (fp16 operand rounding) -> + bias + x [-> Snake] composition."""
+    rng = np.random.default_rng(C * 7 + d + T)
+    N = B * T
+    x = rng.standard_normal((N, C)).astype(np.float32)
+    a1 = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    a2 = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    ao = rng.uniform(0.5, 1.5, C).astype(np.float32) if snk else None
+    dw = (rng.standard_normal((C, 7)) * (0.5 / np.sqrt(7))).astype(np.float32)
+    db = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    pb = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    W = (rng.standard_normal((C, C)) * (0.5 / np.sqrt(C))).astype(np.float32)
+    if wt == "f16":
+        raw = W.astype(np.float16)
+        Wf, typ, raw_bytes = raw.astype(np.float32), vxb.TYPE_F16, raw.view(np.uint8).reshape(-1)
+    else:
+        raw_bytes = S.quantize_q4_0(W).reshape(-1)
+        Wf, typ = S.dequantize_q4_0(raw_bytes).reshape(C, C), vxb.TYPE_Q4_0
+    L = O.lib()
+    h1 = np.zeros_like(x)
+    L.vo_snake(O.P(x), O.P(a1), C, N, O.P(h1))
+    h2 = np.zeros_like(x)
+    L.vo_dwconv(O.P(h1), O.P(dw), O.P(db), C, T, B, d, O.P(h2))
+    h3 = np.zeros_like(x)
+    L.vo_snake(O.P(h2), O.P(a2), C, N, O.P(h3))
+    ref = np.zeros_like(x)
+    L.vo_pointwise(O.P(np.ascontiguousarray(Wf)), O.P(raw_bytes), 1 if wt == "f16" else 2, O.P(pb), O.P(x), O.P(h3),
+                   N, C, C, O.MODE_GPU, O.P(ref))
+    if snk:
+        tmp = ref.copy()
+        L.vo_snake(O.P(tmp), O.P(ao), C, N, O.P(ref))
+    y = torch.empty((N, C), dtype=torch.float16 if out16 else torch.float32, device="cuda")
+    vxb.residual_unit(dev(raw_bytes), typ, C, d, dev(x), B, T, dev(a1), dev(dw), dev(db), dev(a2), dev(pb), y,
+                      out_alpha=dev(ao) if snk else None, out_f16=out16)
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    scale = max(1.0, float(np.abs(ref).max()))
+    tol = (2e-3 if out16 else 5e-4) * scale
+    err = float(np.abs(got - ref).max())
+    assert err <= tol, f"C={C} d={d} B={B} T={T} {wt}: max|d| {err:.3e} > {tol:.3e}"

@@ -515,6 +515,17 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
     return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, true);
 }
 
+// Residual-unit prologue over x [B][T][C] -> h fp16, dilation d.
+int launch_res_pre(const float* x, const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
+                   const float* i2, __half* h, int C, int B, int T, int d, int sms, cudaStream_t s) {
+    const int tt = res_pre_tt(C, T, B, sms);
+    const int ct = res_pre_ct(C);
+    dim3 grid((C + ct - 1) / ct, (T + tt - 1) / tt, B);
+    const cudaError_t e = launch_pdl(ct == 64 ? res_pre_kernel<64> : res_pre_kernel<32>, grid, dim3(256),
+                                     res_pre_smem(d, tt, ct), s, x, a1, i1, dw, db, a2, i2, h, C, T, d, tt);
+    return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("prologue launch: ") + cudaGetErrorString(e));
+}
+
 int grid_1d(int64_t work, int threads) {
     const int64_t b = (work + threads - 1) / threads;
     return static_cast<int>(std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 32));
@@ -1035,16 +1046,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                 const float* x = cur;
                 __half* h = d.h16;
                 const int Bq = B, Tq = Tb;
-                const int tt = res_pre_tt(C, Tq, Bq, sms);
-                const int ct = res_pre_ct(C);
                 rc = sink.kernel(
                     [=](cudaStream_t s) {
-                        dim3 grid((C + ct - 1) / ct, (Tq + tt - 1) / tt, Bq);
-                        const size_t sm = res_pre_smem(dl, tt, ct);
-                        const cudaError_t e =
-                            launch_pdl(ct == 64 ? res_pre_kernel<64> : res_pre_kernel<32>, grid, dim3(256), sm, s, x,
-                                       u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C, Tq, dl, tt);
-                        return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "prologue launch");
+                        return launch_res_pre(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C, Bq, Tq, dl,
+                                              sms, s);
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
                      double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel<" + std::to_string(res_pre_ct(C)) + ">"});
@@ -1345,6 +1350,82 @@ extern "C" int vxb_pointwise(const void* w, int w_type, int K, int M, const void
     rc = setup_pointwise(&op, wv, K, M, x_f16, N, bias, res, snake_alpha, nullptr, out_f16, y, nullptr);
     if (rc) return rc;
     return op.launch(st);
+}
+
+namespace {
+
+// Stream-ordered scratch for the unit entry points, freed when it goes out of scope.
+struct Scratch {
+    std::vector<void*> p;
+    cudaStream_t s;
+    explicit Scratch(cudaStream_t st) : s(st) {}
+    ~Scratch() {
+        for (void* q : p) cudaFreeAsync(q, s);
+    }
+    template <typename T>
+    int get(size_t n, T** out) {
+        void* q = nullptr;
+        CUDA_TRY(cudaMallocAsync(&q, sizeof(T) * std::max<size_t>(n, 1), s));
+        p.push_back(q);
+        *out = static_cast<T*>(q);
+        return VXB_OK;
+    }
+};
+
+// 1 / (alpha + 1e-9) on the device (the reference's derived Snake vector).
+int inv_of(const float* alpha, int C, Scratch& sc, float** inv) {
+    int rc = sc.get(size_t(C), inv);
+    if (rc) return rc;
+    float* copy = nullptr;
+    if ((rc = sc.get(size_t(C), &copy))) return rc;
+    vec_to_f32_kernel<<<grid_1d(C, 256), 256, 0, sc.s>>>(alpha, VXB_TYPE_F32, C, copy, *inv);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_residual_unit(const void* w, int w_type, int C, int d, const float* x, int batch, int T,
+                                 const float* a1, const float* dw, const float* db, const float* a2,
+                                 const float* pb, const float* out_alpha, int out_f16, void* y, void* stream) {
+    if (!w || !x || !a1 || !dw || !db || !a2 || !pb || !y || C <= 0 || batch <= 0 || T <= 0 || d < 1 || d > 9)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "residual unit: bad arguments");
+    if (C % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "residual unit: C must be a multiple of 8");
+    if (out_f16 && !out_alpha) return fail(VXB_ERR_INVALID_ARGUMENT, "residual unit: fp16 output needs a Snake");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    const int sms = num_sms(dev);
+    Scratch sc(st);
+    float *i1 = nullptr, *i2 = nullptr, *io = nullptr;
+    int rc = inv_of(a1, C, sc, &i1);
+    if (!rc) rc = inv_of(a2, C, sc, &i2);
+    if (!rc && out_alpha) rc = inv_of(out_alpha, C, sc, &io);
+    if (rc) return rc;
+    const int epi = !out_alpha ? kResPlain : (out_f16 ? kResSnakeF16 : kResSnakeF32);
+    const int64_t N = int64_t(batch) * T;
+    ResUnitOp op;
+    if (resunit_fits(C)) {
+        if ((rc = setup_resunit(&op, w, w_type, C, d, x, y, epi, a1, i1, dw, db, a2, i2, pb, out_alpha, io, batch,
+                                T, sms, nullptr)))
+            return rc;
+        return op.launch(st);
+    }
+    __half* h = nullptr;
+    if ((rc = sc.get(size_t(N) * C, &h))) return rc;
+    if ((rc = launch_res_pre(x, a1, i1, dw, db, a2, i2, h, C, batch, T, d, sms, st))) return rc;
+    if (resunit_hg_fits(C) && int64_t(batch) * ((T + kRuTT - 1) / kRuTT) >= sms) {
+        if ((rc = setup_resunit(&op, w, w_type, C, d, x, y, epi, a1, i1, dw, db, a2, i2, pb, out_alpha, io, batch,
+                                T, sms, nullptr, h)))
+            return rc;
+        return op.launch(st);
+    }
+    PaddedQ4 tmp;
+    WView wv;
+    if ((rc = view_for(w, w_type, C, C, st, &tmp, &wv))) return rc;
+    GemmOp g;
+    if ((rc = setup_pointwise(&g, wv, C, C, h, N, pb, x, out_alpha, io, out_f16, y, nullptr))) return rc;
+    return g.launch(st);
 }
 
 extern "C" int vxb_convt(const void* w, int w_type, int Cin, int Cout, int s, const void* x_f16, int B, int T,

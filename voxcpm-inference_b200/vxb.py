@@ -55,6 +55,7 @@ SIGNATURES = {
     "vxb_snake": (_i, [_vp, _vp, _i, _i64, _vp, _vp]),
     "vxb_pointwise": (_i, [_vp, _i, _i, _i, _vp, _i64, _vp, _vp, _vp, _i, _vp, _vp]),
     "vxb_convt": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
+    "vxb_residual_unit": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
 }
 
 
@@ -260,3 +261,9 @@ def pointwise(w, w_type: int, K: int, M: int, x16, N: int, bias, y, res=None, sn
 
 def convt(w, w_type: int, Cin: int, Cout: int, s: int, x16, B: int, T: int, bias, y, stream=None):
     check(lib().vxb_convt(ptr(w), w_type, Cin, Cout, s, ptr(x16), B, T, ptr(bias), ptr(y), _stream(stream)))
+
+
+def residual_unit(w, w_type: int, C: int, d: int, x, batch: int, T: int, a1, dw, db, a2, pb, y, out_alpha=None,
+                  out_f16: bool = False, stream=None):
+    check(lib().vxb_residual_unit(ptr(w), w_type, C, d, ptr(x), batch, T, ptr(a1), ptr(dw), ptr(db), ptr(a2), ptr(pb),
+                                  ptr(out_alpha), 1 if out_f16 else 0, ptr(y), _stream(stream)))

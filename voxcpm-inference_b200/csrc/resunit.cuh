@@ -31,7 +31,8 @@
 //   warps 10-13 epilogue, one TMEM lane (= token) per thread, 32 channels at
 //               a time: y = D + b + x is written back into the residual box
 //               (swizzled, conflict-free per-row access; the fp16 variant as
-//               dense 64-byte rows) and leaves by TMA.
+//               dense 64-byte rows) and each warp sends its 32 rows out by
+//               TMA, with no barrier across the epilogue warps.
 // Every wait is bounded (the status word records a failure and the kernel
 // returns); the CTA always frees its TMEM.
 #pragma once
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
         }
         for (int i = 0; i < kRuNE; ++i) {
             mbar_init(&efull[i], 1);
-            mbar_init(&eempty[i], 1);
+            mbar_init(&eempty[i], 4);  // one arrival per epilogue warp
         }
         for (int i = 0; i < kRuNH; ++i) {
             mbar_init(&hfull[i], HG ? 1 : 8);
@@ -448,24 +449,27 @@ __global__ void __launch_bounds__(kRuThreads, 1)
         }
     } else if (warp >= 10 && warp < 14) {
         // ------------------------------------------------------- epilogue --
+        // Each warp owns the 32 rows (tokens) of its TMEM quadrant in every
+        // residual box: it reads them, writes y back in place (fp16: as a
+        // dense [32][64 B] block inside its own rows' bytes) and sends them
+        // out with its own TMA store -- no barrier across the epilogue warps.
+        // A box is released (eempty, 4 arrivals) once each warp's store of it
+        // has read shared memory.
         const int q = warp & 3;                  // TMEM lane quadrant
         const int row = q * 32 + lane;           // token within the tile
-        const bool leader = warp == 10 && lane == 0;
         const int nbox = nslices;                // residual boxes per tile
         int g = 0, i = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < args.tiles && ok; tile += gridDim.x, ++i) {
             const int acc = i & 1;
             ok = mbar_wait(&afull[acc], (i >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
-            if (epi_bar_any(1 + 1, !ok)) {  // named barrier 2 over the 4 epilogue warps
+            if (__any_sync(0xffffffffu, !ok)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int b = tile / args.t_tiles;
-            const int t = (tile - b * args.t_tiles) * kRuTT + row;
-            const bool valid = t < args.T;
-            const size_t n = static_cast<size_t>(b) * args.T + (valid ? t : 0);
+            const int t0 = (tile - b * args.t_tiles) * kRuTT;
             const uint32_t t_row = tmem_base + acc * acc_cols + (static_cast<uint32_t>(q * 32) << 16);
             for (int j = 0; j < nbox; ++j, ++g) {
                 const int c0 = j * kRuSlice;
@@ -481,59 +485,55 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 }
                 const bool landed = mbar_wait(&efull[g % kRuNE], (g / kRuNE) & 1, abort_flag, args.status,
                                               kErrWaitFull);
-                uint8_t* box = sE + (g % kRuNE) * kRuBoxBytes;
-                uint2 h16[8];  // kResSnakeF16: the box's fp16 results, written once every thread has read the box
-                if (landed) {
-#pragma unroll
-                    for (int cq = 0; cq < 8; ++cq) {
-                        const float4 pb = __ldg(reinterpret_cast<const float4*>(args.pb + c0) + cq);
-                        float4* px = reinterpret_cast<float4*>(box + ru_box_off(row, cq * 4));
-                        const float4 xr = *px;
-                        float4 v;
-                        v.x = (__uint_as_float(r[4 * cq + 0]) + pb.x) + xr.x;
-                        v.y = (__uint_as_float(r[4 * cq + 1]) + pb.y) + xr.y;
-                        v.z = (__uint_as_float(r[4 * cq + 2]) + pb.z) + xr.z;
-                        v.w = (__uint_as_float(r[4 * cq + 3]) + pb.w) + xr.w;
-                        if (EPI != kResPlain) {
-                            const float4 sa = __ldg(reinterpret_cast<const float4*>(args.sa + c0) + cq);
-                            const float4 si = __ldg(reinterpret_cast<const float4*>(args.si + c0) + cq);
-                            v = snake4(v, sa, si);
-                        }
-                        if (EPI == kResSnakeF16) {
-                            const __half2 h01 = __floats2half2_rn(v.x, v.y);
-                            const __half2 h23 = __floats2half2_rn(v.z, v.w);
-                            h16[cq].x = *reinterpret_cast<const uint32_t*>(&h01);
-                            h16[cq].y = *reinterpret_cast<const uint32_t*>(&h23);
-                        } else {
-                            *px = v;
-                        }
-                    }
-                }
-                if (EPI == kResSnakeF16) {
-                    // dense fp16 rows of 64 B in the box's first 8 KB (the layout of
-                    // the unswizzled fp16 output map) once all rows are read
-                    epi_bar(2);
-                    if (landed) {
-#pragma unroll
-                        for (int cq = 0; cq < 8; ++cq) *reinterpret_cast<uint2*>(box + row * 64 + cq * 8) = h16[cq];
-                    }
-                }
-                fence_proxy_async_smem();
-                if (epi_bar_any(2, !landed)) {
+                if (__any_sync(0xffffffffu, !landed)) {
                     ok = false;
                     break;
                 }
-                if (leader) {
-                    // box g - 1 is released once its store has read it
+                uint8_t* box = sE + (g % kRuNE) * kRuBoxBytes;
+                uint8_t* own = box + q * 32 * 128;  // this warp's rows (4 KB, 1024-byte aligned)
+                uint2 h16[8];
+#pragma unroll
+                for (int cq = 0; cq < 8; ++cq) {
+                    const float4 pb = __ldg(reinterpret_cast<const float4*>(args.pb + c0) + cq);
+                    float4* px = reinterpret_cast<float4*>(box + ru_box_off(row, cq * 4));
+                    const float4 xr = *px;
+                    float4 v;
+                    v.x = (__uint_as_float(r[4 * cq + 0]) + pb.x) + xr.x;
+                    v.y = (__uint_as_float(r[4 * cq + 1]) + pb.y) + xr.y;
+                    v.z = (__uint_as_float(r[4 * cq + 2]) + pb.z) + xr.z;
+                    v.w = (__uint_as_float(r[4 * cq + 3]) + pb.w) + xr.w;
+                    if (EPI != kResPlain) {
+                        const float4 sa = __ldg(reinterpret_cast<const float4*>(args.sa + c0) + cq);
+                        const float4 si = __ldg(reinterpret_cast<const float4*>(args.si + c0) + cq);
+                        v = snake4(v, sa, si);
+                    }
+                    if (EPI == kResSnakeF16) {
+                        const __half2 h01 = __floats2half2_rn(v.x, v.y);
+                        const __half2 h23 = __floats2half2_rn(v.z, v.w);
+                        h16[cq].x = *reinterpret_cast<const uint32_t*>(&h01);
+                        h16[cq].y = *reinterpret_cast<const uint32_t*>(&h23);
+                    } else {
+                        *px = v;
+                    }
+                }
+                if (EPI == kResSnakeF16) {
+                    __syncwarp();  // the warp's fp32 rows are read before the fp16 block overwrites them
+#pragma unroll
+                    for (int cq = 0; cq < 8; ++cq) *reinterpret_cast<uint2*>(own + lane * 64 + cq * 8) = h16[cq];
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    // the warp's store of box g - 1 has read its rows: release that box
                     bulk_wait_read<0>();
                     if (g > 0) mbar_arrive(&eempty[(g - 1) % kRuNE]);
                     // rows past the sequence end fall outside the tensor and are not written
-                    tma_store_3d(&tmap_y, box, c0, t - row, b);
+                    tma_store_3d(&tmap_y, own, c0, t0 + q * 32, b);
                     bulk_commit();
                 }
             }
         }
-        if (leader) bulk_wait_all();  // stores done before the CTA's shared memory goes away
+        if (lane == 0) bulk_wait_all();  // stores done before the CTA's shared memory goes away
     }
 
     if (warp == 8 && lane == 0) {

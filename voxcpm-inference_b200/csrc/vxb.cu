@@ -511,8 +511,9 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
         op->th = op->tx;  // unused
     }
     if ((rc = make_tmap_x3d(&op->tr, x, C, T, B, kRuTT, true))) return rc;
-    if (epi == kResSnakeF16) return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, false, true);
-    return make_tmap_x3d(&op->ty, y, C, T, B, kRuTT, true);
+    // output: one box of 32 channels x 32 rows per epilogue warp
+    if (epi == kResSnakeF16) return make_tmap_x3d(&op->ty, y, C, T, B, 32, false, true);
+    return make_tmap_x3d(&op->ty, y, C, T, B, 32, true);
 }
 
 // Residual-unit prologue over x [B][T][C] -> h fp16, dilation d.

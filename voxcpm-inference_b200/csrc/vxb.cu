@@ -1212,15 +1212,19 @@ int run_plan(vxb_ctx* c, cudaStream_t s) {
     return VXB_OK;
 }
 
+// Bounded wait for a stream: polls without sleeping for the first 2 ms (a
+// streaming decode completes in well under that; a sleep would add the OS
+// timer slack to every call), then sleeps between polls until the timeout.
 int wait_stream(cudaStream_t s, int timeout_ms) {
     const auto t0 = std::chrono::steady_clock::now();
     while (true) {
         cudaError_t e = cudaStreamQuery(s);
         if (e == cudaSuccess) return VXB_OK;
         if (e != cudaErrorNotReady) return fail(VXB_ERR_BACKEND, std::string("stream: ") + cudaGetErrorString(e));
-        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+        const auto waited = std::chrono::steady_clock::now() - t0;
+        if (waited > std::chrono::milliseconds(timeout_ms))
             return fail(VXB_ERR_TIMEOUT, "timed out waiting for the device");
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (waited > std::chrono::milliseconds(2)) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 

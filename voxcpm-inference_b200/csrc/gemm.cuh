@@ -415,12 +415,15 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                 const int ew = et >> 5;                 // warp within the group
                 float* out = static_cast<float*>(args.out);
                 float4 bq[8];                           // bias of this warp's quads (nquads <= 32)
+                int rco[8];                             // (phase << 16) | cout offset of each quad, -1 if none
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     const int qd = ew + 4 * k;
-                    const int co = (qd - (qd / qpr) * qpr) * 4;
-                    bq[k] = (qd < nquads && co < cpt) ? *reinterpret_cast<const float4*>(args.bias + co_lo + co)
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const int r = qd / qpr;
+                    const int co = (qd - r * qpr) * 4;
+                    const bool on = qd < nquads && co < cpt;
+                    rco[k] = on ? (r << 16) | co : -1;
+                    bq[k] = on ? *reinterpret_cast<const float4*>(args.bias + co_lo + co) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
                 float carry = 0.f;
                 float* rowp = sG + row * Cfg::kEpiLD;
@@ -439,16 +442,16 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     const int n = n_start + c;
                     if (c >= 1 && c < BN && n < args.N) {
                         const bool seq_start = (n % args.seq_len) == 0;
+                        float* orow = out + static_cast<size_t>(n) * s * args.cout + co_lo;  // y row (n*s + 0)
+                        const float* sgl = sG + 4 + lane;
+                        const int rs = 2 * s * Cfg::kEpiLD;                                  // next cout
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
-                            const int qd = ew + 4 * k;
-                            if (qd >= nquads) break;
-                            const int r = qd / qpr;
-                            const int co = (qd - r * qpr) * 4;
-                            if (co >= cpt) continue;
-                            const float* pa = sG + (co * 2 * s + r) * Cfg::kEpiLD + 4 + lane;  // D[co*2s + r][c]
-                            const float* pb = pa + s * Cfg::kEpiLD - 1;                        // D[co*2s + s + r][c - 1]
-                            const int rs = 2 * s * Cfg::kEpiLD;                                // next cout
+                            if (rco[k] < 0) continue;
+                            const int r = rco[k] >> 16;
+                            const int co = rco[k] & 0xffff;
+                            const float* pa = sgl + (co * 2 * s + r) * Cfg::kEpiLD;  // D[co*2s + r][c]
+                            const float* pb = pa + s * Cfg::kEpiLD - 1;               // D[co*2s + s + r][c - 1]
                             float4 y;
                             y.x = pa[0] + bq[k].x;
                             y.y = pa[rs] + bq[k].y;
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                                 y.z += pb[2 * rs];
                                 y.w += pb[3 * rs];
                             }
-                            *reinterpret_cast<float4*>(out + (static_cast<size_t>(n) * s + r) * args.cout + co_lo + co) = y;
+                            *reinterpret_cast<float4*>(orow + r * args.cout + co) = y;
                         }
                     }
                     epi_bar(bar_id);

@@ -94,7 +94,7 @@ struct GemmCfg {
     static constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);   // two accumulators
     static constexpr int kAccStride = BN < 32 ? 32 : BN;
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
-    static_assert((3 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
+    static_assert((4 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
     static constexpr int kThreads = Q4 ? 512 : 384;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
     static_assert(kStages >= 2, "pipeline needs two stages");
@@ -120,7 +120,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     uint64_t* tfull_bar = empty_bar + S;  // accumulator [2] complete
     uint64_t* tempty_bar = tfull_bar + 2; // accumulator [2] drained
     uint64_t* res_bar = tempty_bar + 2;   // PW residual chunk [group][4] landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 8);
+    uint64_t* raw_bar = res_bar + 8;      // Q4_0 raw blocks of a stage landed (the B tile lands on full_bar)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_bar + S);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
             mbar_init(&full_bar[i], 1);
             mbar_init(&ready_bar[i], 4);
             mbar_init(&empty_bar[i], 1);
+            mbar_init(&raw_bar[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull_bar[i], 1);
@@ -174,21 +176,23 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     uint8_t* b_dst = a_dst + Cfg::kABytes;
                     uint8_t* r_dst = b_dst + Cfg::kBBytes;
                     const int k0 = kb * Cfg::kBK;
-                    uint32_t tx = kTx;
-                    if (AK == kAQ4K) tx += 128 * (kQ4KNibBox + 2 * kQ4KScaleBox);
-                    if (AK == kAQ4MN) tx += 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox);
-                    mbar_arrive_expect_tx(&full_bar[st], tx);
+                    // Q4_0: the raw blocks complete raw_bar (the dequantisers
+                    // start as soon as they land), the B tile full_bar
+                    if (AK == kAQ4K) {
+                        mbar_arrive_expect_tx(&raw_bar[st], 128 * (kQ4KNibBox + 2 * kQ4KScaleBox));
+                        tma_load_2d(r_dst, &tmap_a, &raw_bar[st], kb * kQ4KNibBox, m0);
+                        tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &raw_bar[st], (2 * kb) & ~7, m0);
+                    } else if (AK == kAQ4MN) {
+                        mbar_arrive_expect_tx(&raw_bar[st], 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox));
+                        tma_load_2d(r_dst, &tmap_a, &raw_bar[st], (m0 >> 5) * 16, k0);
+                        tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &raw_bar[st], (m0 >> 5) & ~7, k0);
+                    }
+                    mbar_arrive_expect_tx(&full_bar[st], kTx);
                     if (AK == kAF16K) {
                         tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
                     } else if (AK == kAF16MN) {
                         tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
                         tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
-                    } else if (AK == kAQ4K) {
-                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], kb * kQ4KNibBox, m0);
-                        tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &full_bar[st], (2 * kb) & ~7, m0);
-                    } else {
-                        tma_load_2d(r_dst, &tmap_a, &full_bar[st], (m0 >> 5) * 16, k0);
-                        tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &full_bar[st], (m0 >> 5) & ~7, k0);
                     }
                     tma_load_2d(b_dst, &tmap_b, &full_bar[st], k0, n_start);
                 }
@@ -213,8 +217,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                 bool ok = true;
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % S;
-                    uint64_t* bar = kQ4 ? &ready_bar[st] : &full_bar[st];
-                    if (!mbar_wait(bar, (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
+                    if (!mbar_wait(&full_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull) ||
+                        (kQ4 && !mbar_wait(&ready_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull))) {
                         ok = false;
                         break;
                     }
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
             bool ok = true;
             for (int kb = 0; kb < num_kb; ++kb, ++it) {
                 const int st = it % S;
-                if (!mbar_wait(&full_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
+                if (!mbar_wait(&raw_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
                     ok = false;
                     break;
                 }

@@ -161,6 +161,11 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Pulls the 128-byte line holding p into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
+}
+
 // Makes generic-proxy shared-memory writes visible to the async proxy
 // (tcgen05.mma reads operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {

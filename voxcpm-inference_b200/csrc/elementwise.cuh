@@ -73,6 +73,17 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     const int rows = min(tt, T - t0) + halo;
     const bool cv = c < C;
     const float* xb = x + static_cast<long long>(b) * T * C;
+    {
+        // the per-channel parameters are not written by earlier kernels: pull
+        // this block's lines into L2 while the previous kernel finishes
+        const int c0 = blockIdx.x * CT, nc = min(CT, C - c0), i = threadIdx.x;
+        if (i < 10) {
+            const float* v = i < 2 ? a1 : i < 4 ? i1 : i < 6 ? bias : i < 8 ? a2 : i2;
+            if ((i & 1) * 32 < nc) prefetch_l2(v + c0 + (i & 1) * 32);
+        } else if (i < 10 + 2 * CT * 7 / 64) {
+            if ((i - 10) * 32 < nc * 7) prefetch_l2(w + c0 * 7 + (i - 10) * 32);
+        }
+    }
     grid_dep_sync();
     for (int r = ry; r < rows; r += RG) {
         const int t = t0 - halo + r;
@@ -147,6 +158,7 @@ __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s,
     const int b = blockIdx.y;
     const int rows = min(kFinTT, T - t0) + 6;
     const float* sb = s + static_cast<long long>(b) * T * C;
+    if (threadIdx.x * 32 < C * 7) prefetch_l2(w + threadIdx.x * 32);  // taps: constant, into L2 before the wait
     grid_dep_sync();
     constexpr int kMaxLd = ((kFinTT + 6) * 32 + 255) / 256;  // float4 per thread for C <= 128
     float4 v[kMaxLd];

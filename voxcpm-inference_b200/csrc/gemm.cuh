@@ -157,12 +157,48 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    grid_dep_sync();  // setup above overlaps the previous kernel's tail
+
+    // Stage st's weight (A) part for k step kb of the tile at row m0: fp16
+    // tiles complete full_bar[st] (which also expects the B tile); Q4_0 raw
+    // blocks complete raw_bar[st], so the dequantisers start as soon as they
+    // land, and full_bar[st] then expects the B tile only.
+    constexpr uint32_t kTx = (kQ4 ? 0 : Cfg::kABytes) + Cfg::kBBytes;
+    auto issue_a = [&](int st, int kb, int m0) {
+        uint8_t* a_dst = smem + st * Cfg::kStageBytes;
+        uint8_t* r_dst = a_dst + Cfg::kABytes + Cfg::kBBytes;
+        const int k0 = kb * Cfg::kBK;
+        if (AK == kAQ4K) {
+            mbar_arrive_expect_tx(&raw_bar[st], 128 * (kQ4KNibBox + 2 * kQ4KScaleBox));
+            tma_load_2d(r_dst, &tmap_a, &raw_bar[st], kb * kQ4KNibBox, m0);
+            tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &raw_bar[st], (2 * kb) & ~7, m0);
+        } else if (AK == kAQ4MN) {
+            mbar_arrive_expect_tx(&raw_bar[st], 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox));
+            tma_load_2d(r_dst, &tmap_a, &raw_bar[st], (m0 >> 5) * 16, k0);
+            tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &raw_bar[st], (m0 >> 5) & ~7, k0);
+        }
+        mbar_arrive_expect_tx(&full_bar[st], kTx);
+        if (AK == kAF16K) {
+            tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
+        } else if (AK == kAF16MN) {
+            tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
+            tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
+        }
+    };
+    // The weights are not written by earlier kernels: the A parts of the
+    // first min(S, num_kb) k steps of the CTA's first tile are issued before
+    // the grid dependency wait (every stage is free at this point), so their
+    // HBM latency overlaps the previous kernel.  Only the threads that touch
+    // activations wait -- the producer (B tiles) and the epilogue (residual
+    // in, output out); the MMA issuer and the dequantisers work on shared
+    // memory and TMEM alone and start on the prefetched stages at once.
+    const int n_pre = blockIdx.x < num_tiles ? min(S, num_kb) : 0;
+    if (warp == 0 && lane == 0)
+        for (int kb = 0; kb < n_pre; ++kb) issue_a(kb, kb, (blockIdx.x % args.m_tiles) * rows_per_tile);
+    if (warp == 0 || (warp >= 4 && warp < 12)) grid_dep_sync();
 
     if (warp == 0) {
         if (lane == 0) {
             // ------------------------------------------------ TMA producer --
-            constexpr uint32_t kTx = (kQ4 ? 0 : Cfg::kABytes) + Cfg::kBBytes;
             int it = 0;
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
                 const int m0 = (tile % args.m_tiles) * rows_per_tile;
@@ -170,31 +206,13 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                 const int n_start = EPI == kEpiConvT ? nt * (BN - 1) - 1 : nt * BN;
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % S;
-                    if (!mbar_wait(&empty_bar[st], ((it / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty))
-                        break;
-                    uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-                    uint8_t* b_dst = a_dst + Cfg::kABytes;
-                    uint8_t* r_dst = b_dst + Cfg::kBBytes;
-                    const int k0 = kb * Cfg::kBK;
-                    // Q4_0: the raw blocks complete raw_bar (the dequantisers
-                    // start as soon as they land), the B tile full_bar
-                    if (AK == kAQ4K) {
-                        mbar_arrive_expect_tx(&raw_bar[st], 128 * (kQ4KNibBox + 2 * kQ4KScaleBox));
-                        tma_load_2d(r_dst, &tmap_a, &raw_bar[st], kb * kQ4KNibBox, m0);
-                        tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &raw_bar[st], (2 * kb) & ~7, m0);
-                    } else if (AK == kAQ4MN) {
-                        mbar_arrive_expect_tx(&raw_bar[st], 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox));
-                        tma_load_2d(r_dst, &tmap_a, &raw_bar[st], (m0 >> 5) * 16, k0);
-                        tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &raw_bar[st], (m0 >> 5) & ~7, k0);
+                    if (it >= n_pre) {  // (the first n_pre A parts went out before the wait)
+                        if (!mbar_wait(&empty_bar[st], ((it / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty))
+                            break;
+                        issue_a(st, kb, m0);
                     }
-                    mbar_arrive_expect_tx(&full_bar[st], kTx);
-                    if (AK == kAF16K) {
-                        tma_load_2d(a_dst, &tmap_a, &full_bar[st], k0, m0);
-                    } else if (AK == kAF16MN) {
-                        tma_load_2d(a_dst, &tmap_a, &full_bar[st], m0, k0);
-                        tma_load_2d(a_dst + 8192, &tmap_a, &full_bar[st], m0 + 64, k0);
-                    }
-                    tma_load_2d(b_dst, &tmap_b, &full_bar[st], k0, n_start);
+                    tma_load_2d(smem + st * Cfg::kStageBytes + Cfg::kABytes, &tmap_b, &full_bar[st],
+                                kb * Cfg::kBK, n_start);
                 }
             }
             if (*abort_flag) {

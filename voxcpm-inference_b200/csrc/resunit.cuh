@@ -247,7 +247,10 @@ __global__ void __launch_bounds__(kRuThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    grid_dep_sync();
+    // Only the warps that touch activations in global memory wait for the
+    // previous kernel (the loaders, the epilogue's stores); the producers and
+    // the MMA issuer work on shared memory and TMEM alone.
+    if (warp >= 9) grid_dep_sync();
 
     if (warp == 9) {
         if (lane == 0) {

@@ -84,7 +84,11 @@ struct GemmCfg {
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
     static constexpr int kResBytes = kChunk * 128 * 4;           // PW: fp32 [16 tokens][128 channels]
     static constexpr int kOut16Bytes = kChunk * 128 * 2;         // PW: fp16 [16 tokens][128 channels]
-    static constexpr int kEpiRing = 4;                           // PW: residual / output chunk buffers
+    // PW: residual / output chunk buffers per group; loads run kEpiAhead
+    // chunks ahead.  Narrow tiles (one or two tiles per CTA on short
+    // sequences) take a ring of 2 and spend the room on mainloop stages.
+    static constexpr int kEpiRing = BN <= 64 ? 2 : 4;
+    static constexpr int kEpiAhead = kEpiRing / 2;
     static constexpr int kGroupEpiBytes =
         EPI == kEpiConvT ? 128 * kEpiLD * 4 : kEpiRing * kResBytes + kEpiRing * kOut16Bytes;
     static constexpr int kEpiBytes = 2 * kGroupEpiBytes;         // two epilogue warpgroups
@@ -191,9 +195,44 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     // activations wait -- the producer (B tiles) and the epilogue (residual
     // in, output out); the MMA issuer and the dequantisers work on shared
     // memory and TMEM alone and start on the prefetched stages at once.
+    // The tile's later k steps (beyond the S stages) are prefetched into L2.
     const int n_pre = blockIdx.x < num_tiles ? min(S, num_kb) : 0;
-    if (warp == 0 && lane == 0)
-        for (int kb = 0; kb < n_pre; ++kb) issue_a(kb, kb, (blockIdx.x % args.m_tiles) * rows_per_tile);
+    if (warp == 0 && lane == 0 && n_pre > 0) {
+        const int m0 = (blockIdx.x % args.m_tiles) * rows_per_tile;
+        for (int kb = 0; kb < n_pre; ++kb) issue_a(kb, kb, m0);
+        for (int kb = n_pre; kb < num_kb; ++kb) {
+            const int k0 = kb * Cfg::kBK;
+            if (AK == kAQ4K) {
+                tma_prefetch_2d(&tmap_a, kb * kQ4KNibBox, m0);
+                if ((kb & 3) == 0) tma_prefetch_2d(&tmap_scale, (2 * kb) & ~7, m0);
+            } else if (AK == kAQ4MN) {
+                tma_prefetch_2d(&tmap_a, (m0 >> 5) * 16, k0);
+                tma_prefetch_2d(&tmap_scale, (m0 >> 5) & ~7, k0);
+            } else if (AK == kAF16K) {
+                tma_prefetch_2d(&tmap_a, k0, m0);
+            } else {
+                tma_prefetch_2d(&tmap_a, m0, k0);
+                tma_prefetch_2d(&tmap_a, m0 + 64, k0);
+            }
+        }
+    }
+    if (warp >= 4 && warp < 12 && lane == 0) {
+        // the epilogue's per-row parameters of the group's first tile into L2
+        const int tile = blockIdx.x + ((warp - 4) >> 2) * gridDim.x;
+        if (tile < num_tiles) {
+            const int mt = tile % args.m_tiles, qq = warp & 3;
+            if (EPI == kEpiPW) {
+                const int m = mt * Cfg::kBM + qq * 32;
+                if (m < args.M) {
+                    prefetch_l2(args.bias + m);
+                    if (args.snake_alpha) prefetch_l2(args.snake_alpha + m);
+                    if (args.snake_inv) prefetch_l2(args.snake_inv + m);
+                }
+            } else if (mt * args.cpt + qq * 32 < args.cout) {
+                prefetch_l2(args.bias + mt * args.cpt + qq * 32);
+            }
+        }
+    }
     if (warp == 0 || (warp >= 4 && warp < 12)) grid_dep_sync();
 
     if (warp == 0) {
@@ -340,24 +379,41 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
         uint64_t* rbar = res_bar + 4 * eg;
         int tl = eg;                             // local tile index (this group takes tl = eg, eg+2, ...)
         int g_chunk = 0;                         // PW chunks processed by this group (buffer parity)
+        // PW: chunks of 16 tokens, numbered g across this group's tiles
+        // (BN/16 per tile).  A ring of R = 2A residual buffers: the load of
+        // chunk g + A (possibly of the group's next tile) is issued while
+        // chunk g is processed, once the store of chunk g - A has read its
+        // buffer; the first A go out before the group's first accumulator is
+        // complete.
+        constexpr int CPT = EPI == kEpiPW ? BN / Cfg::kChunk : 1;
+        auto issue_res = [&](int gl) {  // residual chunk gl of this group's sequence, if any
+            const int tt = blockIdx.x + (eg + 2 * (gl / CPT)) * gridDim.x;
+            if (tt >= num_tiles) return;
+            const int jb = gl % Cfg::kEpiRing;
+            mbar_arrive_expect_tx(&rbar[jb], Cfg::kResBytes);
+            tma_load_2d(sG + jb * (Cfg::kResBytes / 4), &tmap_res, &rbar[jb], (tt % args.m_tiles) * Cfg::kBM,
+                        (tt / args.m_tiles) * BN + (gl % CPT) * Cfg::kChunk);
+        };
+        if (EPI == kEpiPW && args.res != nullptr && et == 0) {
+            for (int l = 0; l < Cfg::kEpiAhead; ++l) issue_res(l);
+        }
         for (int tile = blockIdx.x + eg * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, tl += 2) {
             const int acc = eg;
-            bool ok = mbar_wait(&tfull_bar[acc], (tl >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
-            ok = !epi_bar_any(bar_id, !ok || *abort_flag != 0);  // uniform over the group
-            if (!ok) break;
-            tc_fence_after();
+            // the tile's parameters are loaded first, then the accumulator awaited
+            auto acc_ready = [&]() -> bool {
+                bool r = mbar_wait(&tfull_bar[acc], (tl >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
+                r = !epi_bar_any(bar_id, !r || *abort_flag != 0);  // uniform over the group
+                if (r) tc_fence_after();
+                return r;
+            };
+            bool ok = true;
             const uint32_t t_row = tmem_base + acc * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
             const int mt = tile % args.m_tiles;
             const int nt = tile / args.m_tiles;
             if (EPI == kEpiPW) {
-                // Chunks of 16 tokens, numbered g across this group's tiles
-                // (BN/16 per tile).  Four residual buffers: the load of chunk
-                // g + 2 (possibly of the group's next tile) is issued while
-                // chunk g is processed, once the store of chunk g - 2 has
-                // read its buffer; the result is written in place (fp32) or
-                // to the chunk's fp16 buffer, and a TMA store sends it out.
-                // Chunks past N load zeros and store nothing (TMA clips).
-                constexpr int CPT = BN / Cfg::kChunk;
+                // The result is written in place (fp32) or to the chunk's fp16
+                // buffer, and a TMA store sends it out.  Chunks past N load
+                // zeros and store nothing (TMA clips).
                 const int m0 = mt * Cfg::kBM;
                 const int m = m0 + row;
                 const int n_start = nt * BN;
@@ -368,24 +424,14 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                                      ? (args.snake_inv ? args.snake_inv[m] : 1.0f / (al + 1e-9f))
                                      : 0.f;
                 const bool has_res = args.res != nullptr;
-                auto issue_res = [&](int gl) {  // residual chunk gl of this group's sequence, if any
-                    const int tt = blockIdx.x + (eg + 2 * (gl / CPT)) * gridDim.x;
-                    if (tt >= num_tiles) return;
-                    const int jb = gl & 3;
-                    mbar_arrive_expect_tx(&rbar[jb], Cfg::kResBytes);
-                    tma_load_2d(sG + jb * (Cfg::kResBytes / 4), &tmap_res, &rbar[jb], (tt % args.m_tiles) * Cfg::kBM,
-                                (tt / args.m_tiles) * BN + (gl % CPT) * Cfg::kChunk);
-                };
-                if (has_res && et == 0 && g_chunk == 0) {
-                    issue_res(0);
-                    issue_res(1);
-                }
+                if (!(ok = acc_ready())) break;
 #pragma unroll 1
                 for (int ch = 0; ch < CPT; ++ch, ++g_chunk) {
-                    const int j = g_chunk & 3;
+                    const int j = g_chunk % Cfg::kEpiRing;
                     if (et == 0) {
-                        bulk_wait_read<1>();  // the store of chunk g - 2 has read its buffers
-                        if (has_res) issue_res(g_chunk + 2);
+                        // the store of chunk g - ahead has read its buffers
+                        bulk_wait_read<Cfg::kEpiAhead - 1>();
+                        if (has_res) issue_res(g_chunk + Cfg::kEpiAhead);
                     }
                     float v[16];
                     tmem_ld16(t_row + ch * Cfg::kChunk, v);
@@ -393,7 +439,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     __half* obuf = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sG) +
                                                              Cfg::kEpiRing * Cfg::kResBytes + j * Cfg::kOut16Bytes);
                     bool w_ok = true;
-                    if (has_res) w_ok = mbar_wait(&rbar[j], (g_chunk >> 2) & 1, abort_flag, args.status, kErrWaitFull);
+                    if (has_res) w_ok = mbar_wait(&rbar[j], (g_chunk / Cfg::kEpiRing) & 1, abort_flag, args.status, kErrWaitFull);
                     if (w_ok) {
                         float r[16];
 #pragma unroll
@@ -447,6 +493,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                     rco[k] = on ? (r << 16) | co : -1;
                     bq[k] = on ? *reinterpret_cast<const float4*>(args.bias + co_lo + co) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+                if (!(ok = acc_ready())) break;
                 float carry = 0.f;
                 float* rowp = sG + row * Cfg::kEpiLD;
 #pragma unroll 1

@@ -162,6 +162,25 @@ __global__ void q4_split_kernel(const uint8_t* __restrict__ src, int64_t rows, i
     }
 }
 
+// Q4_0 rows -> fp16, (q - 8) * d rounded once (the value the GEMM's
+// in-kernel dequantiser produces), same element order: the F16 layout of a
+// tensor of the same shape.  One thread per block.
+__global__ void q4_to_f16_kernel(const uint8_t* __restrict__ src, int64_t nblk, __half* __restrict__ out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < nblk; i += int64_t(gridDim.x) * blockDim.x) {
+        const uint8_t* blk = src + i * 18;
+        const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
+        __half v[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            v[j] = __float2half_rn(static_cast<float>(static_cast<int>(blk[2 + j] & 15u) - 8) * d);
+            v[j + 16] = __float2half_rn(static_cast<float>(static_cast<int>(blk[2 + j] >> 4) - 8) * d);
+        }
+        uint4* o = reinterpret_cast<uint4*>(out + i * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = reinterpret_cast<const uint4*>(v)[j];
+    }
+}
+
 // Device buffers of a split Q4_0 weight.
 struct SplitQ4 {
     void* q = nullptr;
@@ -189,6 +208,17 @@ int split_q4(const void* w, int64_t inner, int64_t rows, cudaStream_t st, bool a
     q4_split_kernel<<<std::max(grid, 1), 256, 0, st>>>(static_cast<const uint8_t*>(w), rows, nblk,
                                                         static_cast<uint8_t*>(out->q), static_cast<uint8_t*>(out->s),
                                                         out->spitch);
+    CUDA_TRY(cudaGetLastError());
+    return VXB_OK;
+}
+
+// The exact fp16 copy of a Q4_0 weight of `nelem` values (synchronous allocation).
+int q4_make_f16(const void* w, int64_t nelem, cudaStream_t st, void** out) {
+    CUDA_TRY(cudaMalloc(out, size_t(nelem) * 2));
+    const int64_t nblk = nelem / 32;
+    const int grid = static_cast<int>(std::min<int64_t>((nblk + 255) / 256, 148 * 16));
+    q4_to_f16_kernel<<<std::max(grid, 1), 256, 0, st>>>(static_cast<const uint8_t*>(w), nblk,
+                                                         static_cast<__half*>(*out));
     CUDA_TRY(cudaGetLastError());
     return VXB_OK;
 }
@@ -553,11 +583,17 @@ struct DevTensor {
     int64_t ne[4] = {1, 1, 1, 1};
     void* dev = nullptr;     // the GGUF bytes, unchanged
     size_t nbytes = 0;
-    SplitQ4 q4;              // Q4_0 GEMM weights: nibbles and scales split (made by vxb_prepare)
+    void* f16 = nullptr;     // Q4_0 conv weights: the exact fp16 copy (made by vxb_prepare)
     int64_t nelem() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
-    WView view() const {
-        return type == VXB_TYPE_Q4_0 ? WView{q4.q, type, q4.pitch, q4.s, q4.spitch} : WView{dev, type, 0, nullptr, 0};
-    }
+    // The operand the decode plan's kernels read: a Q4_0 weight's exact fp16
+    // copy (made at prepare; the same values the in-kernel dequantiser
+    // produces, so the same results).  Measured on B200, streaming included
+    // (weights cold in HBM every step), reading 16 bits per value beats
+    // dequantising 4.5 bits per value inside the GEMM, which sits on each
+    // k step's critical path and is repeated for every token tile.
+    WView gemm_view() const { return WView{type == VXB_TYPE_Q4_0 ? f16 : dev, VXB_TYPE_F16, 0, nullptr, 0}; }
+    // Weight bytes one pass over gemm_view() reads.
+    double gemm_bytes() const { return double(nelem()) * 2; }
 };
 
 struct Vec {  // derived fp32 vector (+ inverse for Snake alphas)
@@ -702,8 +738,7 @@ int vxb_close(vxb_ctx* c) {
     if (c->plan) free_plan(c->plan.get());
     for (auto& kv : c->tensors) {
         cudaFree(kv.second.dev);
-        cudaFree(kv.second.q4.q);
-        cudaFree(kv.second.q4.s);
+        cudaFree(kv.second.f16);
     }
     for (void* p : c->derived_allocs) cudaFree(p);
     cudaFree(c->status);
@@ -751,8 +786,7 @@ int vxb_upload_tensor(vxb_ctx* c, const char* name, int type, const int64_t* ne,
     auto it = c->tensors.find(t.name);
     if (it != c->tensors.end()) {
         cudaFree(it->second.dev);
-        cudaFree(it->second.q4.q);
-        cudaFree(it->second.q4.s);
+        cudaFree(it->second.f16);
     }
     c->tensors[t.name] = t;
     c->prepared = false;
@@ -845,8 +879,7 @@ int derive_taps(vxb_ctx* c, const std::string& name, int C, float** out) {
 }
 
 // Binds a conv weight used as a GEMM operand ([outer rows][inner]); for Q4_0
-// it also makes the TMA-friendly copy: each 18-byte block split into its 16
-// nibble bytes and its fp16 scale (two 16-byte aligned arrays).
+// it also makes the exact fp16 copy that the decode plan's kernels read.
 int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t outer, const DevTensor** out) {
     auto it = c->tensors.find(name);
     if (it == c->tensors.end()) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
@@ -856,11 +889,9 @@ int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t out
     if (t->nelem() != inner * outer) return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
     if (t->type == VXB_TYPE_Q4_0) {
         if (inner % 32) return fail(VXB_ERR_INVALID_FORMAT, name + ": Q4_0 rows must hold whole blocks");
-        cudaFree(t->q4.q);
-        cudaFree(t->q4.s);
-        t->q4 = SplitQ4{};
-        int rc = split_q4(t->dev, inner, outer, c->stream, false, &t->q4);
-        if (rc) return rc;
+        cudaFree(t->f16);
+        t->f16 = nullptr;
+        if (int rc = q4_make_f16(t->dev, t->nelem(), c->stream, &t->f16)) return rc;
     }
     *out = t;
     return VXB_OK;
@@ -962,7 +993,6 @@ struct OpSink {
 //   final k7 conv + tanh.
 int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
     const int L = c->latent_dim, D = c->decoder_dim;
-    auto wbytes = [](const DevTensor* t) { return double(t->nbytes); };
     const double n0 = double(B) * T;
     int rc;
     {
@@ -980,10 +1010,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
     {
         GemmOp op;
         const Block& b0 = c->blocks[0];
-        if ((rc = setup_pointwise(&op, c->pw1->view(), L, D, d.h16, int64_t(B) * T, c->b1.v, nullptr, b0.alpha.v,
-                                  b0.alpha.inv, 1, d.s16, d.status)))
+        if ((rc = setup_pointwise(&op, c->pw1->gemm_view(), L, D, d.h16, int64_t(B) * T, c->b1.v, nullptr,
+                                  b0.alpha.v, b0.alpha.inv, 1, d.s16, d.status)))
             return rc;
-        if ((rc = sink.gemm(op, {"pw_model1", 2.0 * D * L * n0, wbytes(c->pw1) + n0 * L * 2 + n0 * D * 2,
+        if ((rc = sink.gemm(op, {"pw_model1", 2.0 * D * L * n0, c->pw1->gemm_bytes() + n0 * L * 2 + n0 * D * 2,
                                  gemm_kernel_name(op)})))
             return rc;
     }
@@ -996,10 +1026,11 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
         const bool last_block = bi + 1 == c->blocks.size();
         {
             GemmOp op;
-            if ((rc = setup_convt(&op, b.convt->view(), b.cin, b.cout, b.s, d.s16, B, Tb, b.bias.v, d.xa, d.status)))
+            if ((rc = setup_convt(&op, b.convt->gemm_view(), b.cin, b.cout, b.s, d.s16, B, Tb, b.bias.v, d.xa,
+                                  d.status)))
                 return rc;
             if ((rc = sink.gemm(op, {"convt_b" + std::to_string(bi), 2.0 * (2.0 * b.s * b.cout) * b.cin * double(n),
-                                     wbytes(b.convt) + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4,
+                                     b.convt->gemm_bytes() + double(n) * b.cin * 2 + double(n) * b.s * b.cout * 4,
                                      gemm_kernel_name(op)})))
                 return rc;
         }
@@ -1031,13 +1062,13 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
                 }
-                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status)))
                     return rc;
                 rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
                                  {"resunit_b" + std::to_string(bi) + "u" + std::to_string(r),
                                   2.0 * C * C * double(n) + 20.0 * double(n) * C,
-                                  wbytes(u.pw) + double(n) * C * (4 + out_bytes), op.kernel_name()});
+                                  u.pw->gemm_bytes() + double(n) * C * (4 + out_bytes), op.kernel_name()});
                 if (rc) return rc;
                 if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
                 std::swap(cur, nxt);
@@ -1074,12 +1105,12 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
                 }
-                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status, d.h16)))
                     return rc;
                 rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
                                  {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
-                                  wbytes(u.pw) + double(n) * C * (2 + 4 + out_bytes), op.kernel_name()});
+                                  u.pw->gemm_bytes() + double(n) * C * (2 + 4 + out_bytes), op.kernel_name()});
                 if (rc) return rc;
                 if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
                 std::swap(cur, nxt);
@@ -1088,22 +1119,22 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             GemmOp op;
             double out_bytes;
             if (r < 2) {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, nullptr, nullptr, 0, nxt,
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, nullptr, nullptr, 0, nxt,
                                      d.status);
                 out_bytes = 4;
             } else if (!last_block) {
                 const Block& nb = c->blocks[bi + 1];
-                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, nb.alpha.v, nb.alpha.inv, 1,
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, nb.alpha.v, nb.alpha.inv, 1,
                                      d.s16, d.status);
                 out_bytes = 2;
             } else {
-                rc = setup_pointwise(&op, u.pw->view(), C, C, d.h16, n, u.pb.v, cur, c->final_alpha.v,
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, c->final_alpha.v,
                                      c->final_alpha.inv, 0, nxt, d.status);
                 out_bytes = 4;
             }
             if (rc) return rc;
             if ((rc = sink.gemm(op, {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
-                                     wbytes(u.pw) + double(n) * C * (2 + 4 + out_bytes), gemm_kernel_name(op)})))
+                                     u.pw->gemm_bytes() + double(n) * C * (2 + 4 + out_bytes), gemm_kernel_name(op)})))
                 return rc;
             if (r < 2) sink.stage(stage0 + 1 + r, nxt, size_t(n) * C);
             std::swap(cur, nxt);

@@ -233,6 +233,18 @@ int pick_bn(int64_t n) {
     return 16;
 }
 
+// Halves a tile width (down to 32) while the layer's m_tiles x n_tiles tiles
+// would leave SMs of the current device idle: on short sequences more,
+// narrower tiles shorten every CTA's chain (fewer epilogue chunks per CTA).
+// Token tiles advance by bn - overlap tokens.
+int fill_bn(int bn, int m_tiles, int64_t N, int overlap) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t sms = num_sms(dev);
+    while (bn > 32 && int64_t(m_tiles) * ((N + bn - overlap - 1) / (bn - overlap)) < sms) bn /= 2;
+    return bn;
+}
+
 // Launches a decode kernel with programmatic stream serialisation (the
 // kernel calls grid_dep_sync before it touches activations), so its launch
 // and setup overlap the previous kernel; captured into graphs as
@@ -321,7 +333,7 @@ int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t 
         return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: bad extents");
     if (K % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: K must be a multiple of 8");
     op->epi = kEpiPW;
-    op->bn = std::max(32, std::min(128, pick_bn(N)));
+    op->bn = fill_bn(std::max(32, std::min(128, pick_bn(N))), (M + 127) / 128, N, 0);
     op->grid = dim3(1);
     int rc = make_tmap_f16(&op->tb, x16, K, N, uint64_t(K) * 2, 64, op->bn);
     if (rc) return rc;
@@ -384,7 +396,7 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     const int cpt = convt_cpt(s);
     if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");
     op->epi = kEpiConvT;
-    op->bn = pick_bn(N + 1);
+    op->bn = fill_bn(pick_bn(N + 1), (Cout + cpt - 1) / cpt, N, 1);
     op->grid = dim3(1);
     int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, op->bn);
     if (rc) return rc;

@@ -1,6 +1,6 @@
 """Benchmark: AudioVAE decode on B200 (decoded audio-seconds per second).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c1|c3|c4|c5f|c5q]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c1|c3|c4|c5f|c5q|e1]
                     [--impl ours|reference]
 
 Workloads (seeded synthetic weights in the reference's GGUF layout and seeded
@@ -18,6 +18,9 @@ distributed):
       evenly over the ranks (strong scaling).
   c5f / c5q  64 utterances z=[64,64,750] (AR(1) 0.9), F16 / Q4_0-mixed, split
       evenly over the ranks (strong scaling).
+  e1  the encoder: 16 waveforms of 30 s (seeded partials + noise) -> latents
+      z=[16,64,750], Q4_0-mixed, split evenly over the ranks (strong
+      scaling); a step is one encode of the per-rank batch.
 A step is one decode of the per-rank batch.  For c2/c1 every rank replays its
 own stream (weak scaling).  Under torchrun each rank drives one GPU; nothing
 crosses GPUs on the data path (the path shards with no exchange).
@@ -65,6 +68,9 @@ DESCR = {
     "c5f": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, F16",
     "c5q": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, Q4_0-mixed",
 }
+# Encoder workloads: name -> (quant, waveforms per step (global), latent frames per waveform)
+ENCODE_WORKLOADS = {"e1": ("q4_0", 16, 750)}
+DESCR["e1"] = "batched encode 16 x 30 s waveforms (16 kHz) -> z=[16,64,750], Q4_0-mixed encoder"
 FLUSH_BYTES = 256 << 20
 
 
@@ -162,6 +168,42 @@ def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: 
     return statistics.median(times), len(times), label, cores, times
 
 
+def roofline(ops, op_ms, hbm, tfl, peak_src, workload):
+    """The dominant kernel (largest total device time over one pass of the
+    plan, launches grouped by template instance as ncu names them) against
+    the measured peak of the resource its algorithmic intensity makes it
+    bound by; its per-launch DRAM traffic from profiles/traffic.json."""
+    fam = {}
+    for op, ms in zip(ops, op_ms):
+        f = fam.setdefault(op["kernel"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "launches": 0, "ops": []})
+        f["ms"] += ms
+        f["bytes"] += op["bytes"]
+        f["flops"] += op["flops"]
+        f["launches"] += 1
+        f["ops"].append(op["name"])
+    kname, f = max(fam.items(), key=lambda kv: kv[1]["ms"])
+    t_s = f["ms"] / 1e3
+    intensity = f["flops"] / max(f["bytes"], 1.0)
+    if intensity > (tfl * 1e12) / (hbm * 1e9):
+        roof = {"bound": "tensor", "achieved": f["flops"] / t_s / 1e12, "peak": tfl, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": f["bytes"] / t_s / 1e9, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = f"{peak_src} (MEASURED_PEAKS.json burst figure)" if peak_src == "measured" else peak_src
+    roof["kernel"] = kname
+    roof["launches_per_step"] = f["launches"]
+    roof["ms_per_launch"] = f["ms"] / f["launches"]
+    roof["share"] = f["ms"] / sum(op_ms)
+    roof["algorithmic_per_launch"] = {"bytes": f["bytes"] / f["launches"], "flops": f["flops"] / f["launches"]}
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as fh:
+            traffic = json.load(fh).get(workload, {}).get(kname)
+    roof["traffic"] = traffic
+    return roof
+
+
 C3_HALO = 20  # frames of left context per time chunk (receptive field 18.49)
 
 
@@ -179,9 +221,11 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + sorted(ENCODE_WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args()
+    if args.workload in ENCODE_WORKLOADS:
+        return main_encode(args)
     ws, rank, local = dist_env()
     quant, streams, T, emit, scaling, ar = WORKLOADS[args.workload]
     per_rank = streams if scaling == "weak" else max(1, streams // ws)
@@ -317,36 +361,7 @@ def main():
     op_ms = d.time_ops(reps=10, flush=flush, flush_bytes=FLUSH_BYTES)
     clk = clocks.stop()
     ops = d.ops()
-    # Group the launches of one decode by kernel (template instance, as ncu
-    # names them); the dominant kernel is the one with the largest total time.
-    fam = {}
-    for op, ms in zip(ops, op_ms):
-        f = fam.setdefault(op["kernel"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "launches": 0, "ops": []})
-        f["ms"] += ms
-        f["bytes"] += op["bytes"]
-        f["flops"] += op["flops"]
-        f["launches"] += 1
-        f["ops"].append(op["name"])
-    kname, f = max(fam.items(), key=lambda kv: kv[1]["ms"])
-    t_s = f["ms"] / 1e3
-    intensity = f["flops"] / max(f["bytes"], 1.0)
-    if intensity > (tfl * 1e12) / (hbm * 1e9):
-        roof = {"bound": "tensor", "achieved": f["flops"] / t_s / 1e12, "peak": tfl, "unit": "TFLOP/s"}
-    else:
-        roof = {"bound": "hbm", "achieved": f["bytes"] / t_s / 1e9, "peak": hbm, "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["peak_source"] = f"{peak_src} (MEASURED_PEAKS.json burst figure)" if peak_src == "measured" else peak_src
-    roof["kernel"] = kname
-    roof["launches_per_step"] = f["launches"]
-    roof["ms_per_launch"] = f["ms"] / f["launches"]
-    roof["share"] = f["ms"] / sum(op_ms)
-    roof["algorithmic_per_launch"] = {"bytes": f["bytes"] / f["launches"], "flops": f["flops"] / f["launches"]}
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tf):
-        with open(tf) as fh:
-            traffic = json.load(fh).get(args.workload, {}).get(kname)
-    roof["traffic"] = traffic
+    roof = roofline(ops, op_ms, hbm, tfl, peak_src, args.workload)
 
     cpu = None
     if rank == 0 and ws == 1:
@@ -377,6 +392,184 @@ def main():
             "clocks": clk,
         }
         print(json.dumps(line))
+    d.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference_encode_time(model_path: str, audio: np.ndarray, budget_s: float = 20.0):
+    """Times the reference's own CPU encoder (AudioVAE::encode through
+    oracle/_ref) on all host cores, one waveform at a time, until budget_s.
+    Returns (seconds per waveform, waveforms timed, cores, times)."""
+    import ctypes
+
+    so = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
+    if not os.path.exists(so):
+        return None
+    L = ctypes.CDLL(so)
+    L.ref_open.restype = ctypes.c_void_p
+    L.ref_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.ref_close.argtypes = [ctypes.c_void_p]
+    L.ref_encode.restype = ctypes.c_longlong
+    L.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_longlong]
+    cores = os.cpu_count() or 1
+    h = L.ref_open(model_path.encode(), cores)
+    n = audio.shape[1]
+    out = np.zeros(64 * ((n + HOP - 1) // HOP), np.float32)
+    a0 = np.ascontiguousarray(audio[0])
+    L.ref_encode(h, a0.ctypes.data, n, out.ctypes.data, out.size)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    for i in range(audio.shape[0]):
+        a = np.ascontiguousarray(audio[i])
+        t0 = time.perf_counter()
+        L.ref_encode(h, a.ctypes.data, n, out.ctypes.data, out.size)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    L.ref_close(h)
+    return statistics.median(times), len(times), cores, times
+
+
+# CPU sample of the encoder: waveforms of this many latent frames (0.24 s each;
+# the reference's encoder runs well below real time on the host cores)
+REF_ENCODE_FRAMES = 6
+
+
+def main_encode(args):
+    """Encode workload: a step encodes this rank's share of the batch of
+    waveforms (strong scaling: the global batch is split over the ranks, no
+    exchange).  value = encoded audio seconds of the whole job per device
+    second (max over ranks); e2e through the blocking vxb_encode with pinned
+    host buffers."""
+    ws, rank, local = dist_env()
+    quant, streams, T = ENCODE_WORKLOADS[args.workload]
+    per_rank = max(1, streams // ws)
+    audio_per_step = ws * per_rank * T * HOP / SR
+    hbm, tfl, peak_src = peaks()
+    tmpdir = tempfile.mkdtemp(prefix="vxb_bench_")
+    model = os.path.join(tmpdir, f"{quant}_enc.gguf")
+    S.write_model(model, quant=quant, seed=0, encoder=True)
+    cfg = {"workload": f"{args.workload}: {DESCR[args.workload]}", "weights": quant, "batch_per_gpu": per_rank,
+           "frames": T, "samples_per_waveform": T * HOP, "sample_rate": SR,
+           "l2": "flushed before every step (256 MiB memset outside the timed events)",
+           "parallelism": f"dp{ws} (independent waveforms per GPU, no collective)"}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        a = S.make_audio(REF_ENCODE_FRAMES * HOP, min(args.steps, 40), seed=3000)
+        r = reference_encode_time(model, a)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/liboracle_ref.so not built"}))
+            return
+        sec, n, cores, times = r
+        val = (REF_ENCODE_FRAMES * HOP / SR) / sec
+        sample = f"{n} waveforms of {REF_ENCODE_FRAMES} frames, AudioVAE::encode, {cores} threads"
+        print(json.dumps({"impl": "reference", "metric": "encoded audio-sec/sec", "value": val, "unit": "audio-s/s",
+                          "n_gpus": ws, "steps": n, "warmup": 1, "ms_per_step": sec * 1e3, "higher_is_better": True,
+                          "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": cfg, "cpu_baseline": {"value": val, "unit": "audio-s/s", "cores": cores,
+                                                          "kind": "reference", "sample": sample},
+                          "e2e": {"value": val, "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import vxb
+
+    d = vxb.Decoder(local)
+    d.load_gguf(model)
+    d.prepare()
+    d.build_encode_plan(per_rank, T)
+    nops = len(d.encode_ops())
+    K, W = args.steps, max(3, args.warmup)
+    audio_host = S.make_audio(T * HOP, per_rank, seed=2000 + rank)
+    a_dev = torch.from_numpy(audio_host).cuda()
+    z_dev = torch.empty((per_rank, 64, T), dtype=torch.float32, device="cuda")
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    clocks = ClockSampler(local)
+    time.sleep(0.5)
+    for _ in range(W):
+        d.encode_device(a_dev, z_dev, stream)
+    d.sync()
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        ev0[i].record(stream)
+        d.encode_device(a_dev, z_dev, stream)
+        ev1[i].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    d.sync()
+    step_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+    total_ms = sum(step_ms)
+    if dist:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    value = audio_per_step * K / (total_ms / 1e3)
+
+    a_pin = torch.from_numpy(audio_host).pin_memory()
+    z_pin = torch.empty((per_rank, 64, T), dtype=torch.float32).pin_memory()
+    d.encode_host_ptrs(a_pin.data_ptr(), z_pin.data_ptr())
+    e2e_ms = []
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        d.encode_host_ptrs(a_pin.data_ptr(), z_pin.data_ptr())
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e_total = sum(e2e_ms)
+    if dist:
+        t = torch.tensor([e2e_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = audio_per_step * K / (e2e_total / 1e3)
+
+    op_ms = d.encode_time_ops(reps=3, flush=flush, flush_bytes=FLUSH_BYTES)
+    clk = clocks.stop()
+    ops = d.encode_ops()
+    roof = roofline(ops, op_ms, hbm, tfl, peak_src, args.workload)
+    cpu = None
+    if rank == 0 and ws == 1:
+        r = reference_encode_time(model, S.make_audio(REF_ENCODE_FRAMES * HOP, 40, seed=3000))
+        if r is not None:
+            sec, n, cores, _ = r
+            cpu = {"value": (REF_ENCODE_FRAMES * HOP / SR) / sec, "unit": "audio-s/s", "cores": cores,
+                   "kind": "reference",
+                   "sample": f"{n} waveforms of {REF_ENCODE_FRAMES} frames, AudioVAE::encode, {cores} threads"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "encoded audio-sec/sec", "value": value, "unit": "audio-s/s", "n_gpus": ws, "steps": K,
+            "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded weights and waveforms)", "config": cfg,
+            "latency_ms": {"p50": float(np.percentile(step_ms, 50)), "e2e_p50": float(np.percentile(e2e_ms, 50))},
+            "e2e": {"value": e2e_value, "unit": "audio-s/s", "clock": "host (blocking call)",
+                    "h2d_bytes_per_step": int(audio_host.nbytes), "d2h_bytes_per_step": int(z_pin.numel() * 4)},
+            "gpu_launches": K * nops, "wall_s_timed_region": wall, "roofline": roof,
+            "per_op_ms": {op["name"]: round(ms, 5) for op, ms in zip(ops, op_ms)},
+            "cpu_baseline": cpu, "clocks": clk}))
     d.close()
     if dist:
         dist.barrier()

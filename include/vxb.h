@@ -163,6 +163,49 @@ VXB_API int vxb_time_ops(vxb_ctx* ctx, int reps, void* flush, size_t flush_bytes
  * always allocates its compute arena (src/backend.cpp:241-287). */
 VXB_API int vxb_decode_static(vxb_ctx* ctx, const float* z_dev, float* out_dev, int batch, int T, void* stream);
 
+/* ---- encoder: waveform -> latent ---- */
+
+/* Sets the encoder config for callers that upload tensors themselves
+ * (vxb_load_gguf reads it from voxcpm_audio_vae_config_encoder_dim / _rates):
+ * head width and the downsampling rates, in the roles of AudioVAEConfig's
+ * encoder_dim / encoder_rates (include/voxcpm/config.h:34-133). */
+VXB_API int vxb_set_encoder_config(vxb_ctx* ctx, int encoder_dim, const int* rates, int n_rates);
+
+/* Waveform samples per latent frame: the product of the encoder rates
+ * (AudioVAEConfig::hop_length); 0 without an encoder config. */
+VXB_API int vxb_encoder_hop(const vxb_ctx* ctx);
+
+/* Binds the encoder weights (audio_vae.encoder.*, the names
+ * load_encoder_weights reads, src/audio-vae.cpp:331-363; F16 conv weights
+ * [K, Cin, Cout] or Q4_0 folded [K*Cin, Cout], :64-103) on its first call
+ * after vxb_prepare, then allocates the activation arena for `batch`
+ * waveforms of T * vxb_encoder_hop samples each.  Replaces the graph build +
+ * gallocr reserve of AudioVAE::encode (src/audio-vae.cpp:652-664) for that
+ * shape.  VXB_ERR_INVALID_FORMAT if the model's encoder tensors are
+ * placeholders; encoder rates must be 2, 3, 5 or 8. */
+VXB_API int vxb_build_encode_plan(vxb_ctx* ctx, int batch, int T);
+
+/* One encode of the planned shape: audio [batch][T*hop] (16 kHz samples;
+ * pad a shorter waveform with zeros to the hop multiple, as the reference's
+ * AudioVAE::preprocess does, src/audio-vae.cpp:465-474) -> latent
+ * [batch][latent_dim][T] (t fastest: each one the reference's ne=[T, latent],
+ * the input layout of vxb_decode), both HOST pointers; copies in, runs,
+ * copies out and waits (bounded, VXB_ERR_TIMEOUT after 60 s).  Replaces
+ * AudioVAE::encode + VoxCPMBackend::compute + tensor_get
+ * (src/audio-vae.cpp:640-664, src/backend.cpp:293-339). */
+VXB_API int vxb_encode(vxb_ctx* ctx, const float* audio_host, float* latent_host);
+
+/* Same with DEVICE pointers, enqueued on `stream` (NULL = the context's
+ * stream) without waiting; completion via vxb_sync. */
+VXB_API int vxb_encode_device(vxb_ctx* ctx, const float* audio_dev, float* latent_dev, void* stream);
+
+/* The encode plan's launches, as vxb_plan_num_ops / vxb_plan_op_info /
+ * vxb_time_ops for the decode plan. */
+VXB_API int vxb_encode_num_ops(const vxb_ctx* ctx);
+VXB_API int vxb_encode_op_info(const vxb_ctx* ctx, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
+                               double* flops, double* bytes);
+VXB_API int vxb_encode_time_ops(vxb_ctx* ctx, int reps, void* flush, size_t flush_bytes, float* ms_out);
+
 /* ---- single-kernel entry points (device pointers, enqueued on `stream`) ---- */
 
 /* Q4_0 blocks -> fp32 ((q - 8) * d), bit-exact with ggml's

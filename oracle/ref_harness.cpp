@@ -1,5 +1,5 @@
 // Test infrastructure only: a thin extern "C" harness around the reference's
-// own decoder code (nowang6/voxcpm-inference, compiled unmodified from its
+// own decoder and encoder code (nowang6/voxcpm-inference, compiled unmodified from its
 // sources by oracle/Makefile.ref into oracle/_ref/liboracle_ref.so).
 //
 // It is the checker and the CPU baseline, never part of the product path.
@@ -150,6 +150,77 @@ int ref_decode_l1_stage(void* h, const float* z, int T, int stage, float* out) {
 
 int ref_decode_l2(void* h, const float* z, int T, float* out) {
     return run_decode(static_cast<RefModel*>(h), z, T, out, false);
+}
+
+// The reference's own encoder, AudioVAE::encode (src/audio-vae.cpp:652-664,
+// graph from encode_tensor :640-650), on one waveform of n samples (padded
+// to a hop multiple by its preprocess, :465-474); the latent [64][T] (t
+// fastest) into out.  Returns its element count, or < 0 on failure.
+long long ref_encode(void* h, const float* audio, long long n, float* out, long long cap) {
+    RefModel* m = static_cast<RefModel*>(h);
+    VoxCPMContext gc(ContextType::Graph, 32768, 262144);
+    std::vector<float> a(audio, audio + n);
+    ggml_tensor* y = m->vae->encode(gc, a, -1);
+    ggml_cgraph* g = gc.new_graph();
+    gc.build_forward(g, y);
+    m->backend->reserve_compute_memory(g);
+    m->backend->alloc_graph(g);
+    const std::vector<float>& pa = m->vae->last_preprocessed_audio();
+    m->backend->tensor_set(m->vae->last_input_tensor(), pa.data(), 0, pa.size() * sizeof(float));
+    if (m->backend->compute(g) != GGML_STATUS_SUCCESS) return -4;
+    const long long ne = ggml_nelements(y);
+    if (ne > cap) return -5;
+    m->backend->tensor_get(y, out, 0, (size_t)ne * sizeof(float));
+    return ne;
+}
+
+// The same encoder built from the reference's own layer functions with an
+// early exit: stage 0 = head conv, then per block b: 1+4b..3+4b the residual
+// units, 4+4b the Snake + strided conv (encode_tensor :640-650,
+// encoder_block_forward :553-570).  The activation is returned as [t][c].
+long long ref_encode_stage(void* h, const float* audio, long long n, int stage, float* out, long long cap) {
+    RefModel* m = static_cast<RefModel*>(h);
+    AudioVAE& vae = *m->vae;
+    const AudioVAEWeights& W = vae.weights_;
+    VoxCPMContext gc(ContextType::Graph, 32768, 262144);
+    ggml_context* c = gc.raw_context();
+    std::vector<float> a = vae.preprocess(std::vector<float>(audio, audio + n), -1);
+    ggml_tensor* in = gc.new_tensor_3d(GGML_TYPE_F32, (int64_t)a.size(), 1, 1);
+    ggml_set_input(in);
+    int cur = 0;
+    ggml_tensor* y = nullptr;
+    auto at_stage = [&](ggml_tensor* t) {
+        if (stage == cur++) y = ggml_cont(c, ggml_transpose(c, ggml_reshape_2d(c, t, t->ne[0], t->ne[1])));
+        return y != nullptr;
+    };
+    ggml_tensor* x = vae.causal_conv1d(c, in, W.encoder_block_0_weight, W.encoder_block_0_bias, 7, 1, 1, 3);
+    if (!at_stage(x)) {
+        for (int i = 0; i < vae.config_.num_encoder_blocks(); ++i) {
+            const EncoderBlockWeights& bw = W.encoder_blocks[(size_t)i];
+            const int s = vae.config_.encoder_rates[(size_t)i];
+            x = vae.residual_unit_forward(c, x, bw.res0, 1);
+            if (at_stage(x)) break;
+            x = vae.residual_unit_forward(c, x, bw.res1, 3);
+            if (at_stage(x)) break;
+            x = vae.residual_unit_forward(c, x, bw.res2, 9);
+            if (at_stage(x)) break;
+            x = snake_activation(c, x, bw.snake_alpha);
+            x = vae.causal_conv1d(c, x, bw.conv_weight, bw.conv_bias, s * 2, s, 1, (int)std::ceil(s / 2.0f));
+            if (at_stage(x)) break;
+        }
+    }
+    if (!y) return -6;
+    ggml_set_output(y);
+    ggml_cgraph* g = gc.new_graph();
+    gc.build_forward(g, y);
+    m->backend->reserve_compute_memory(g);
+    m->backend->alloc_graph(g);
+    m->backend->tensor_set(in, a.data(), 0, a.size() * sizeof(float));
+    if (m->backend->compute(g) != GGML_STATUS_SUCCESS) return -4;
+    const long long ne = ggml_nelements(y);
+    if (ne > cap) return -5;
+    m->backend->tensor_get(y, out, 0, (size_t)ne * sizeof(float));
+    return ne;
 }
 
 // ggml's own Q4_0 row conversion (ggml-quants.c:459-477 dequantize_row_q4_0,

@@ -1,7 +1,7 @@
 /*
  * vae_oracle.c -- TEST INFRASTRUCTURE ONLY (the checker, never the product).
  *
- * A plain-C restatement of the reference AudioVAE decoder
+ * A plain-C restatement of the reference AudioVAE decoder (and encoder)
  * (nowang6/voxcpm-inference) used by tests/, __graft_entry__.smoke() and the
  * cpu_baseline leg of bench.py to check the CUDA path.  Nothing in the product
  * library links or calls this file.
@@ -171,6 +171,8 @@ typedef struct {
 typedef struct {
     int latent_dim, decoder_dim, n_rates;
     int rates[8];
+    int encoder_dim, n_enc_rates;
+    int enc_rates[8];
     int n_tensors;
     vo_tensor* tensors;
     uint8_t* file;
@@ -284,6 +286,16 @@ vo_model* vo_open(const char* path) {
             m->latent_dim = (int)rd_u32(&p);
         } else if (!strcmp(key, "voxcpm_audio_vae_config_decoder_dim") && t == 4) {
             m->decoder_dim = (int)rd_u32(&p);
+        } else if (!strcmp(key, "voxcpm_audio_vae_config_encoder_dim") && t == 4) {
+            m->encoder_dim = (int)rd_u32(&p);
+        } else if (!strcmp(key, "voxcpm_audio_vae_config_encoder_rates") && t == 9) {
+            const uint32_t et = rd_u32(&p);
+            const uint64_t n = rd_u64(&p);
+            m->n_enc_rates = (int)n;
+            for (uint64_t j = 0; j < n; ++j) {
+                if (et == 5 || et == 4) m->enc_rates[j] = (int)rd_u32(&p);
+                else skip_value(&p, et);
+            }
         } else if (!strcmp(key, "general.alignment") && t == 4) {
             alignment = rd_u32(&p);
         } else if (!strcmp(key, "voxcpm_audio_vae_config_decoder_rates") && t == 9) {
@@ -648,4 +660,161 @@ int64_t vo_decode(const vo_model* m, const float* z, int T, int B, int mode, int
     (void)cur;
     return N;
 #undef STAGE_DONE
+}
+
+/* ------------------------------------------------------------ encoder --- */
+
+/* Causal conv1d as the reference runs it (causal_conv1d, audio-vae.cpp:476-493:
+ * left pad 2*padding = lpad, then im2col + mul_mat, :218-234): kernel K,
+ * stride s, weight [Cout][Cin*K] in memory (row j = ci*K + k, the F16
+ * [K, Cin, Cout] tensor or the folded Q4_0 [K*Cin, Cout]); x [B*Lin][Cin]
+ * -> y [B*Lout][Cout], Lout = (Lin + lpad - K)/s + 1.  The im2col row is the
+ * GEMM input, so the numerics modes apply to it as to a pointwise conv. */
+static int64_t conv1d_k(const vo_tensor* wt, const float* b, const float* x, int64_t Lin, int B, int Cin,
+                        int Cout, int K, int s, int lpad, int mode, float* y) {
+    const int64_t Lout = (Lin + lpad - K) / s + 1;
+    const int KC = K * Cin;
+    float* col = (float*)calloc((size_t)B * Lout * KC, sizeof(float));
+    for (int bb = 0; bb < B; ++bb)
+        for (int64_t t = 0; t < Lout; ++t)
+            for (int ci = 0; ci < Cin; ++ci)
+                for (int k = 0; k < K; ++k) {
+                    const int64_t src = t * s + k - lpad;
+                    if (src < 0 || src >= Lin) continue;
+                    col[((int64_t)bb * Lout + t) * KC + (int64_t)ci * K + k] = x[((int64_t)bb * Lin + src) * Cin + ci];
+                }
+    float* W = to_f32(wt);
+    vo_pointwise(W, wt->data, wt->type, b, NULL, col, (int64_t)B * Lout, KC, Cout, mode, y);
+    free(W);
+    free(col);
+    return Lout;
+}
+
+int vo_encoder_dim(const vo_model* m) { return m->encoder_dim; }
+int vo_encoder_hop(const vo_model* m) {
+    int h = 1;
+    for (int i = 0; i < m->n_enc_rates; ++i) h *= m->enc_rates[i];
+    return h;
+}
+
+/* Full encode of B waveforms audio[b][n] (AudioVAE::encode / encode_tensor,
+ * audio-vae.cpp:640-664): zero-padded to a multiple of the hop (preprocess,
+ * :465-474), head conv k7 (pad 3) -> per block three residual units (d = 1,
+ * 3, 9), Snake, conv k 2s stride s (pad ceil(s/2)) doubling the channels
+ * (encoder_block_forward, :553-570) -> fc_mu conv k3 (pad 1).  The latent goes
+ * to out[b][c][t] (ggml ne=[T, latent] per waveform).  Returns T, or -1 when
+ * the model holds no encoder (placeholder tensors). */
+int64_t vo_encode_stage(const vo_model* m, const float* audio, int64_t n, int B, int mode, int stage, float* out);
+int64_t vo_encode(const vo_model* m, const float* audio, int64_t n, int B, int mode, float* out) {
+    return vo_encode_stage(m, audio, n, B, mode, -1, out);
+}
+
+/* As vo_encode; stage >= 0 stops after that stage (0 = head conv, then per
+ * block b: 1+4b..3+4b the residual units, 4+4b the Snake + strided conv) and
+ * copies its activation [B*L][C] to out, returning the element count. */
+int64_t vo_encode_stage(const vo_model* m, const float* audio, int64_t n, int B, int mode, int stage, float* out) {
+    int cur = 0;
+#define ENC_STAGE(buf, count)                                  \
+    do {                                                       \
+        if (stage == cur) {                                    \
+            memcpy(out, buf, sizeof(float) * (size_t)(count)); \
+            free(buf);                                         \
+            return (count);                                    \
+        }                                                      \
+        ++cur;                                                 \
+    } while (0)
+    char nm[256];
+    const char* pre = "audio_vae.encoder.";
+    const int E = m->encoder_dim, hop = vo_encoder_hop(m);
+    snprintf(nm, sizeof nm, "%sblock.0.weight", pre);
+    const vo_tensor* w0 = find(m, nm);
+    if (!w0 || E <= 0 || nelem(w0) != 7 * (int64_t)E || m->n_enc_rates <= 0) return -1;
+    const int64_t Lp = (n + hop - 1) / hop * hop;
+    float* x = (float*)calloc((size_t)B * Lp, sizeof(float));
+    for (int bb = 0; bb < B; ++bb) memcpy(x + (int64_t)bb * Lp, audio + (int64_t)bb * n, sizeof(float) * (size_t)n);
+    int64_t L = Lp;
+    int C = E;
+    snprintf(nm, sizeof nm, "%sblock.0.bias", pre);
+    float* b0 = vec_f32(m, nm);
+    float* y = (float*)malloc(sizeof(float) * (size_t)B * L * C);
+    conv1d_k(w0, b0, x, L, B, 1, C, 7, 1, 6, mode, y);
+    free(b0);
+    free(x);
+    x = y;
+    ENC_STAGE(x, (int64_t)B * L * C);
+    const int dil[3] = {1, 3, 9};
+    for (int bi = 0; bi < m->n_enc_rates; ++bi) {
+        const int s = m->enc_rates[bi];
+        const int64_t N = (int64_t)B * L;
+        for (int r = 0; r < 3; ++r) {
+            char rp[128];
+            snprintf(rp, sizeof rp, "%sblock.%d.block.%d.block.", pre, bi + 1, r);
+            snprintf(nm, sizeof nm, "%s0.alpha", rp);
+            float* a1 = vec_f32(m, nm);
+            snprintf(nm, sizeof nm, "%s1.weight", rp);
+            float* dw = vec_f32(m, nm);
+            snprintf(nm, sizeof nm, "%s1.bias", rp);
+            float* db = vec_f32(m, nm);
+            snprintf(nm, sizeof nm, "%s2.alpha", rp);
+            float* a2 = vec_f32(m, nm);
+            snprintf(nm, sizeof nm, "%s3.weight", rp);
+            const vo_tensor* pw = find(m, nm);
+            snprintf(nm, sizeof nm, "%s3.bias", rp);
+            float* pb = vec_f32(m, nm);
+            float* W = to_f32(pw);
+            float* h1 = (float*)malloc(sizeof(float) * (size_t)N * C);
+            float* h2 = (float*)malloc(sizeof(float) * (size_t)N * C);
+            vo_snake(x, a1, C, N, h1);
+            vo_dwconv(h1, dw, db, C, (int)L, B, dil[r], h2);
+            vo_snake(h2, a2, C, N, h1);
+            float* yr = (float*)malloc(sizeof(float) * (size_t)N * C);
+            vo_pointwise(W, pw->data, pw->type, pb, x, h1, N, C, C, mode, yr);
+            free(W);
+            free(h1);
+            free(h2);
+            free(a1);
+            free(dw);
+            free(db);
+            free(a2);
+            free(pb);
+            free(x);
+            x = yr;
+            ENC_STAGE(x, N * C);
+        }
+        snprintf(nm, sizeof nm, "%sblock.%d.block.3.alpha", pre, bi + 1);
+        float* a = vec_f32(m, nm);
+        float* h = (float*)malloc(sizeof(float) * (size_t)N * C);
+        vo_snake(x, a, C, N, h);
+        free(a);
+        free(x);
+        snprintf(nm, sizeof nm, "%sblock.%d.block.4.weight", pre, bi + 1);
+        const vo_tensor* wc = find(m, nm);
+        snprintf(nm, sizeof nm, "%sblock.%d.block.4.bias", pre, bi + 1);
+        float* bc = vec_f32(m, nm);
+        const int64_t Lo = (L + 2 * ((s + 1) / 2) - 2 * s) / s + 1;
+        y = (float*)malloc(sizeof(float) * (size_t)B * Lo * 2 * C);
+        conv1d_k(wc, bc, h, L, B, C, 2 * C, 2 * s, s, 2 * ((s + 1) / 2), mode, y);
+        free(bc);
+        free(h);
+        x = y;
+        L = Lo;
+        C *= 2;
+        ENC_STAGE(x, (int64_t)B * L * C);
+    }
+    const int Lt = m->latent_dim;
+    snprintf(nm, sizeof nm, "%sfc_mu.weight", pre);
+    const vo_tensor* wf = find(m, nm);
+    snprintf(nm, sizeof nm, "%sfc_mu.bias", pre);
+    float* bf = vec_f32(m, nm);
+    y = (float*)malloc(sizeof(float) * (size_t)B * L * Lt);
+    conv1d_k(wf, bf, x, L, B, C, Lt, 3, 1, 2, mode, y);
+    free(bf);
+    free(x);
+    for (int bb = 0; bb < B; ++bb)
+        for (int c = 0; c < Lt; ++c)
+            for (int64_t t = 0; t < L; ++t) out[((int64_t)bb * Lt + c) * L + t] = y[((int64_t)bb * L + t) * Lt + c];
+    free(y);
+    (void)cur;
+    return L;
+#undef ENC_STAGE
 }

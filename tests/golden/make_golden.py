@@ -7,9 +7,10 @@ built from them (``make -f oracle/Makefile.ref REF=<reference checkout>``):
 
 Every fixture holds inputs drawn from fixed seeds and the outputs of the
 reference's own code (oracle/_ref/liboracle_ref.so): ggml's fp16 and Q4_0
-conversions, HEAD's fused Snake callback, ggml mul_mat, and whole decodes
+conversions, HEAD's fused Snake callback, ggml mul_mat, whole decodes
 through the reference's L1 graph functions and (for Q4_0 models) through
-HEAD's AudioVAE::decode.  Models are not stored: they are regenerated
+HEAD's AudioVAE::decode, and whole encodes through AudioVAE::encode
+(``python tests/golden/make_golden.py encode_f16_t6`` regenerates one case).  Models are not stored: they are regenerated
 bit-identically from their seeds by vxb_synth.make_model, and each fixture
 records the sha256 of the model bytes it was made from.
 """
@@ -43,6 +44,14 @@ DECODE_CASES = {
 }
 
 
+# Encode fixtures: name -> (model kwargs, audio kwargs)
+ENCODE_CASES = {
+    "f32_t2": (dict(quant="f32", seed=0, encoder=True), dict(n=2 * 640 - 37, batch=2, seed=11)),
+    "f16_t6": (dict(quant="f16", seed=0, encoder=True), dict(n=6 * 640, batch=2, seed=7)),
+    "q4_t6": (dict(quant="q4_0", seed=0, encoder=True), dict(n=6 * 640, batch=2, seed=7)),
+}
+
+
 def lib():
     path = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
     L = ctypes.CDLL(path)
@@ -52,6 +61,8 @@ def lib():
     L.ref_close.argtypes = [vp]
     for f in ("ref_decode_l1", "ref_decode_l2"):
         getattr(L, f).argtypes = [vp, vp, i, vp]
+    L.ref_encode.restype = ll
+    L.ref_encode.argtypes = [vp, vp, ll, vp, ll]
     L.ref_dequant_q4_0.argtypes = [vp, ll, vp]
     L.ref_quantize_q4_0.argtypes = [vp, ll, vp]
     L.ref_fp32_to_fp16.argtypes = [ctypes.c_float]
@@ -159,16 +170,44 @@ def decode_fixture(L, name, mk, lk, do_l2):
           ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
 
 
+def encode_fixture(L, name, mk, ak):
+    """The reference's own AudioVAE::encode on each waveform of a seeded batch."""
+    data = S.make_model(**mk)
+    sha = hashlib.sha256(data).hexdigest()
+    audio = S.make_audio(**ak)
+    B, n = audio.shape
+    hop = 640
+    T = (n + hop - 1) // hop
+    lat = np.zeros((B, 64, T), np.float32)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "m.gguf")
+        with open(path, "wb") as f:
+            f.write(data)
+        h = L.ref_open(path.encode(), os.cpu_count() or 4)
+        assert h, "reference failed to open the model"
+        for b in range(B):
+            got = L.ref_encode(h, P(np.ascontiguousarray(audio[b])), n, P(lat[b]), lat[b].size)
+            assert got == 64 * T, got
+        L.ref_close(h)
+    np.savez_compressed(os.path.join(HERE, f"encode_{name}.npz"), audio=audio, latent=lat, sha=np.array(sha),
+                        model=np.array(repr(mk)), audio_kw=np.array(repr(ak)))
+    print("encode", name, sha[:12], "max|latent| %.3f" % np.abs(lat).max())
+
+
 def main():
     L = lib()
-    fp16_fixture(L)
-    q4_fixture(L)
-    snake_fixture(L)
-    mulmat_fixture(L)
     only = sys.argv[1:]
+    if not only:
+        fp16_fixture(L)
+        q4_fixture(L)
+        snake_fixture(L)
+        mulmat_fixture(L)
     for name, (mk, lk, do_l2) in DECODE_CASES.items():
         if not only or name in only:
             decode_fixture(L, name, mk, lk, do_l2)
+    for name, (mk, ak) in ENCODE_CASES.items():
+        if not only or "encode_" + name in only:
+            encode_fixture(L, name, mk, ak)
 
 
 if __name__ == "__main__":

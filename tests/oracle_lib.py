@@ -47,6 +47,11 @@ def lib():
             getattr(L, f).argtypes = [vp]
         L.vo_rate.restype = i
         L.vo_rate.argtypes = [vp, i]
+        L.vo_encode.restype = i64
+        L.vo_encode.argtypes = [vp, vp, i64, i, i, vp]
+        for f in ("vo_encoder_dim", "vo_encoder_hop"):
+            getattr(L, f).restype = i
+            getattr(L, f).argtypes = [vp]
         _lib = L
     return _lib
 
@@ -94,3 +99,16 @@ class OracleModel:
         n = lib().vo_decode(self.h, P(z), T, B, mode, stage, P(out))
         assert n == out.size, (n, out.size)
         return out.reshape(B, -1) if stage < 0 else out
+
+    def encode(self, audio: np.ndarray, mode: int = MODE_REF) -> np.ndarray:
+        """audio: float32 [B, n] -> latent [B, latent, T], T = ceil(n / hop)."""
+        audio = np.ascontiguousarray(audio, dtype=np.float32)
+        B, n = audio.shape
+        hop = lib().vo_encoder_hop(self.h)
+        T = (n + hop - 1) // hop
+        out = np.zeros((B, self.latent_dim, T), np.float32)
+        got = lib().vo_encode(self.h, P(audio), n, B, mode, P(out))
+        if got < 0:
+            raise RuntimeError("the model holds no encoder")
+        assert got == T, (got, T)
+        return out

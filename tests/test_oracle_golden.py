@@ -102,3 +102,38 @@ def test_decode_matches_reference_l1(name):
         # HEAD's L2 path re-quantises the transposed-conv weights to Q8_0; the
         # reference disagrees with itself by a few 1e-3 (its gate is 1e-2).
         assert np.abs(got - f["l2"]).max() <= 1e-2
+
+
+# Encoder: the oracle's restatement against the reference's own
+# AudioVAE::encode.  With F32 weights nothing is rounded to fp16 and only
+# the fp32 summation order differs (the restatement of every layer is pinned
+# to about 1e-6).  With F16 weights the reference rounds each conv's input
+# to fp16; a 1-ulp fp32 difference that straddles an fp16 rounding boundary
+# then moves that input by one fp16 step, and the 16 fp16-rounded conv
+# layers of the encoder compound such flips to about 1e-3 of the latent's
+# scale.  With Q4_0 weights the rounding is the reference's Q8_0 activation
+# quantisation (steps of amax/127 per block of 32), so flips are coarser:
+# a few per cent.  Tolerances are relative to max|latent|.
+ENCODE_TOL = {"f32": 1e-5, "f16": 3e-3, "q4_0": 5e-2}
+
+
+@pytest.mark.parametrize("name", ["f32_t2", "f16_t6", "q4_t6"])
+def test_encode_matches_reference(name):
+    f = load(f"encode_{name}.npz")
+    mk = ast.literal_eval(str(f["model"]))
+    path, sha = model_path(**mk)
+    assert sha == str(f["sha"]), "seeded model generator drifted from the fixture"
+    audio = f["audio"]
+    assert np.array_equal(audio, S.make_audio(**ast.literal_eval(str(f["audio_kw"]))))
+    m = O.OracleModel(path)
+    got = m.encode(audio, O.MODE_REF)
+    ref = f["latent"]
+    assert got.shape == ref.shape
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= ENCODE_TOL[mk["quant"]], f"oracle vs reference encode: relative max|d| {err:.3e}"
+
+
+def test_encode_placeholder_model_has_no_encoder():
+    path, _ = model_path(quant="f16", seed=0)
+    with pytest.raises(RuntimeError):
+        O.OracleModel(path).encode(np.zeros((1, 640), np.float32))

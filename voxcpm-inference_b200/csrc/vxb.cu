@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "elementwise.cuh"
+#include "encoder.cuh"
 #include "gemm.cuh"
 #include "resunit.cuh"
 #include "gguf_reader.h"
@@ -626,6 +627,13 @@ struct Block {
     ResUnit ru[3];
 };
 
+struct EncBlock {
+    int cin = 0, cout = 0, s = 0;  // residual units at cin channels, then a conv k 2s stride s to cout
+    ResUnit ru[3];
+    Vec alpha, bias;
+    const DevTensor* conv = nullptr;  // [Cout][Cin][2s] in memory
+};
+
 struct OpInfo {
     std::string name;
     double flops = 0, bytes = 0;  // algorithmic work: 2*M*K*N, minimal HBM traffic
@@ -682,6 +690,16 @@ struct vxb_ctx {
     float* final_w = nullptr;
     float final_bias = 0.f;
     std::unique_ptr<Plan> plan;
+    // encoder: config (GGUF keys or vxb_set_encoder_config), weights bound at
+    // the first vxb_build_encode_plan after vxb_prepare, its own plan
+    int encoder_dim = 0;
+    std::vector<int> enc_rates;
+    bool enc_bound = false;
+    float* enc_w0 = nullptr;  // head conv [E][7]
+    Vec enc_b0, fc_b;
+    std::vector<EncBlock> enc_blocks;
+    const DevTensor* fc_mu = nullptr;
+    std::unique_ptr<Plan> enc_plan;
     int* status = nullptr;         // device status word
     int* status_host = nullptr;    // pinned mirror
 };
@@ -748,6 +766,7 @@ int vxb_close(vxb_ctx* c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
     if (c->plan) free_plan(c->plan.get());
+    if (c->enc_plan) free_plan(c->enc_plan.get());
     for (auto& kv : c->tensors) {
         cudaFree(kv.second.dev);
         cudaFree(kv.second.f16);
@@ -829,6 +848,13 @@ int vxb_load_gguf(vxb_ctx* c, const char* path) {
     std::vector<int> rates(r->arr_i.begin(), r->arr_i.end());
     int rc = vxb_set_config(c, latent, dec, rates.data(), static_cast<int>(rates.size()));
     if (rc) return rc;
+    // encoder config: optional (a decoder-only caller never needs it)
+    int enc = 0;
+    const GgufValue* er = f.kv("voxcpm_audio_vae_config_encoder_rates");
+    if (u32("voxcpm_audio_vae_config_encoder_dim", &enc) && er && !er->arr_i.empty()) {
+        std::vector<int> erates(er->arr_i.begin(), er->arr_i.end());
+        if ((rc = vxb_set_encoder_config(c, enc, erates.data(), static_cast<int>(erates.size())))) return rc;
+    }
     std::vector<uint8_t> buf;
     for (const auto& t : f.tensors) {
         if (t.nbytes == 0) continue;  // types this path never reads (encoder-only extras)
@@ -844,6 +870,24 @@ int vxb_hop(const vxb_ctx* c) {
     if (!c) return 0;
     int h = 1;
     for (int r : c->rates) h *= r;
+    return h;
+}
+
+int vxb_set_encoder_config(vxb_ctx* c, int encoder_dim, const int* rates, int n_rates) {
+    if (!c || encoder_dim <= 0 || !rates || n_rates <= 0 || n_rates > 8)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "bad encoder config");
+    for (int i = 0; i < n_rates; ++i)
+        if (rates[i] <= 0 || rates[i] > 32) return fail(VXB_ERR_INVALID_ARGUMENT, "bad encoder rates");
+    c->encoder_dim = encoder_dim;
+    c->enc_rates.assign(rates, rates + n_rates);
+    c->enc_bound = false;
+    return VXB_OK;
+}
+
+int vxb_encoder_hop(const vxb_ctx* c) {
+    if (!c || c->enc_rates.empty()) return 0;
+    int h = 1;
+    for (int r : c->enc_rates) h *= r;
     return h;
 }
 
@@ -918,6 +962,13 @@ extern "C" int vxb_prepare(vxb_ctx* c) {
     for (void* p : c->derived_allocs) cudaFree(p);
     c->derived_allocs.clear();
     c->blocks.clear();
+    // the encoder's derived weights went with the allocations above
+    c->enc_bound = false;
+    c->enc_blocks.clear();
+    if (c->enc_plan) {
+        free_plan(c->enc_plan.get());
+        c->enc_plan.reset();
+    }
     // The reference refuses a store whose encoder tensors are absent
     // (load_encoder_weights, src/audio-vae.cpp:331-363); the decoder never
     // reads them, so only their presence is checked.
@@ -1190,6 +1241,224 @@ struct PlanSink : OpSink {
     void stage(int stage, float* buf, size_t floats) override { P.stage_buf[stage] = {buf, floats, P.ops.size() - 1}; }
 };
 
+// Binds the encoder weights (audio_vae.encoder.*, the names and layouts
+// load_encoder_weights reads, src/audio-vae.cpp:331-363) and derives their
+// fp32 vectors / fp16 conv copies, once per vxb_prepare.
+int bind_encoder(vxb_ctx* c) {
+    if (c->enc_bound) return VXB_OK;
+    const int E = c->encoder_dim, nb = static_cast<int>(c->enc_rates.size());
+    if (E <= 0 || nb == 0) return fail(VXB_ERR_NOT_READY, "no encoder config (GGUF keys or vxb_set_encoder_config)");
+    const std::string p = "audio_vae.encoder.";
+    const DevTensor* w0 = get(c, p + "block.0.weight");
+    if (!w0) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + p + "block.0.weight");
+    if (w0->nelem() != int64_t(7) * E)
+        return fail(VXB_ERR_INVALID_FORMAT, "the model carries no encoder weights (placeholder encoder tensors)");
+    int rc;
+    if ((rc = derive_taps(c, p + "block.0.weight", E, &c->enc_w0))) return rc;
+    if ((rc = derive_vec(c, p + "block.0.bias", E, false, &c->enc_b0))) return rc;
+    c->enc_blocks.clear();
+    int C = E;
+    for (int bi = 0; bi < nb; ++bi) {
+        EncBlock b;
+        b.cin = C;
+        b.cout = 2 * C;
+        b.s = c->enc_rates[bi];
+        // channel counts: 16-byte vectors in the elementwise kernels, TMA rows in the GEMMs
+        if (C % 32) return fail(VXB_ERR_INVALID_FORMAT, "encoder channels must be multiples of 32");
+        const std::string bp = p + "block." + std::to_string(bi + 1) + ".block.";
+        for (int r = 0; r < 3; ++r) {
+            const std::string rp = bp + std::to_string(r) + ".block.";
+            ResUnit& u = b.ru[r];
+            if ((rc = derive_vec(c, rp + "0.alpha", C, true, &u.a1))) return rc;
+            if ((rc = derive_taps(c, rp + "1.weight", C, &u.dw))) return rc;
+            if ((rc = derive_vec(c, rp + "1.bias", C, false, &u.db))) return rc;
+            if ((rc = derive_vec(c, rp + "2.alpha", C, true, &u.a2))) return rc;
+            if ((rc = check_matrix(c, rp + "3.weight", C, C, &u.pw))) return rc;
+            if ((rc = derive_vec(c, rp + "3.bias", C, false, &u.pb))) return rc;
+        }
+        if ((rc = derive_vec(c, bp + "3.alpha", C, true, &b.alpha))) return rc;
+        if ((rc = check_matrix(c, bp + "4.weight", int64_t(2) * b.s * C, b.cout, &b.conv))) return rc;
+        if (!(b.conv->n_dims == 3 ? b.conv->ne[0] == 2 * b.s && b.conv->ne[1] == C : b.conv->ne[0] == 2 * b.s * C))
+            return fail(VXB_ERR_INVALID_FORMAT, bp + "4.weight: expected [2s, Cin, Cout] or [2s*Cin, Cout]");
+        if ((rc = derive_vec(c, bp + "4.bias", b.cout, false, &b.bias))) return rc;
+        c->enc_blocks.push_back(b);
+        C *= 2;
+    }
+    const int Lt = c->latent_dim;
+    if ((rc = check_matrix(c, p + "fc_mu.weight", int64_t(3) * C, Lt, &c->fc_mu))) return rc;
+    if (!(c->fc_mu->n_dims == 3 ? c->fc_mu->ne[0] == 3 && c->fc_mu->ne[1] == C : c->fc_mu->ne[0] == 3 * C))
+        return fail(VXB_ERR_INVALID_FORMAT, "fc_mu.weight: expected [3, C, latent] or [3*C, latent]");
+    if ((rc = derive_vec(c, p + "fc_mu.bias", Lt, false, &c->fc_b))) return rc;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    c->enc_bound = true;
+    return VXB_OK;
+}
+
+// Largest activation (floats) and largest im2col operand (halves) of an
+// encode of B waveforms of T latent frames.
+void enc_arena_sizes(const vxb_ctx* c, int B, int T, int64_t* max_x, int64_t* max_col) {
+    int64_t L = int64_t(T) * vxb_encoder_hop(c);
+    *max_x = int64_t(B) * L * c->encoder_dim;
+    *max_col = 0;
+    for (const EncBlock& b : c->enc_blocks) {
+        const int64_t Lo = L / b.s;
+        *max_col = std::max(*max_col, int64_t(B) * Lo * b.cin * 2 * b.s);
+        *max_x = std::max(*max_x, int64_t(B) * L * b.cin);
+        L = Lo;
+        *max_x = std::max(*max_x, int64_t(B) * L * b.cout);
+    }
+    *max_col = std::max(*max_col, int64_t(B) * L * c->enc_blocks.back().cout * 3);
+}
+
+int launch_im2col(const float* x, const float* alpha, const float* inv, __half* col, int B, int Lin, int C, int K,
+                  int s, int lpad, int Lout, cudaStream_t st) {
+    const dim3 grid(grid_1d(int64_t(B) * Lout * C, 256)), block(256);
+    cudaError_t e;
+    switch (K) {
+        case 3: e = launch_pdl(snake_im2col_kernel<3>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
+        case 4: e = launch_pdl(snake_im2col_kernel<4>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
+        case 6: e = launch_pdl(snake_im2col_kernel<6>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
+        case 10: e = launch_pdl(snake_im2col_kernel<10>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
+        case 16: e = launch_pdl(snake_im2col_kernel<16>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
+        default: return fail(VXB_ERR_INVALID_ARGUMENT, "encoder conv: kernel size must be 3, 4, 6, 10 or 16");
+    }
+    return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("im2col launch: ") + cudaGetErrorString(e));
+}
+
+// The launch sequence of one encode of B waveforms of T latent frames
+// (T * hop samples each; encode_tensor, src/audio-vae.cpp:640-650):
+//   head conv k7 -> per block: 3 residual units (the decoder's kernels: the
+//   fused unit up to 128 channels, else prologue + pointwise GEMM), Snake +
+//   im2col (k 2s, stride s, left pad 2 ceil(s/2)) -> the conv as one
+//   pointwise GEMM (K = 2s Cin) doubling the channels
+//   -> fc_mu: im2col (k 3, left pad 2) -> GEMM -> transpose to [B][L][T].
+int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
+    const int E = c->encoder_dim, Lt = c->latent_dim;
+    const int sms = num_sms(c->device);
+    int64_t L = int64_t(T) * vxb_encoder_hop(c);
+    int rc;
+    {
+        const float *a = d.z, *w = c->enc_w0, *bb = c->enc_b0.v;
+        float* o = d.xa;
+        const int64_t n = int64_t(B) * L;
+        const long long Lq = L;
+        rc = sink.kernel(
+            [=](cudaStream_t s) {
+                const cudaError_t e = launch_pdl(enc_head_kernel, dim3(grid_1d(n * E / 4, 256)), dim3(256), 0, s, a,
+                                                 w, bb, o, B, Lq, E);
+                return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "encoder head launch");
+            },
+            {"enc_head", 14.0 * double(n) * E, double(n) * (4 + E * 4), "enc_head_kernel"});
+        if (rc) return rc;
+    }
+    float* cur = d.xa;
+    float* nxt = d.xb;
+    static const int kDil[3] = {1, 3, 9};
+    for (size_t bi = 0; bi < c->enc_blocks.size(); ++bi) {
+        const EncBlock& b = c->enc_blocks[bi];
+        const int C = b.cin;
+        const int Lb = static_cast<int>(L);
+        const int64_t n = int64_t(B) * L;
+        const std::string tag = "enc_b" + std::to_string(bi);
+        for (int r = 0; r < 3; ++r) {
+            const ResUnit& u = b.ru[r];
+            const int dl = kDil[r];
+            const std::string nm = tag + "u" + std::to_string(r);
+            if (resunit_fits(C)) {
+                ResUnitOp op;
+                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, nxt, kResPlain,
+                                        u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, u.pb.v, nullptr, nullptr, B,
+                                        Lb, sms, d.status)))
+                    return rc;
+                rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
+                                 {"resunit_" + nm, 2.0 * C * C * double(n) + 20.0 * double(n) * C,
+                                  u.pw->gemm_bytes() + double(n) * C * 8, op.kernel_name()});
+                if (rc) return rc;
+                std::swap(cur, nxt);
+                continue;
+            }
+            {
+                const float* x = cur;
+                __half* h = d.h16;
+                rc = sink.kernel(
+                    [=](cudaStream_t s) {
+                        return launch_res_pre(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, h, C, B, Lb, dl,
+                                              sms, s);
+                    },
+                    {"res_pre_" + nm, double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4,
+                     "res_pre_kernel<" + std::to_string(res_pre_ct(C)) + ">"});
+                if (rc) return rc;
+            }
+            GemmOp op;
+            if ((rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, nullptr, nullptr, 0, nxt,
+                                      d.status)))
+                return rc;
+            if ((rc = sink.gemm(op, {"pw_" + nm, 2.0 * C * C * double(n), u.pw->gemm_bytes() + double(n) * C * 10,
+                                     gemm_kernel_name(op)})))
+                return rc;
+            std::swap(cur, nxt);
+        }
+        // Snake + im2col, then the strided conv as one GEMM
+        const int K = 2 * b.s, lpad = 2 * ((b.s + 1) / 2);
+        const int Lo = static_cast<int>((L + lpad - K) / b.s + 1);
+        const int64_t no = int64_t(B) * Lo;
+        {
+            const float* x = cur;
+            __half* col = d.s16;
+            const float *al = b.alpha.v, *iv = b.alpha.inv;
+            const int s = b.s;
+            rc = sink.kernel(
+                [=](cudaStream_t st) { return launch_im2col(x, al, iv, col, B, Lb, C, K, s, lpad, Lo, st); },
+                {"im2col_" + tag, 20.0 * double(no) * C * K, double(n) * C * 4 + double(no) * C * K * 2,
+                 "snake_im2col_kernel<" + std::to_string(K) + ">"});
+            if (rc) return rc;
+        }
+        GemmOp op;
+        if ((rc = setup_pointwise(&op, b.conv->gemm_view(), C * K, b.cout, d.s16, no, b.bias.v, nullptr, nullptr,
+                                  nullptr, 0, nxt, d.status)))
+            return rc;
+        if ((rc = sink.gemm(op, {"conv_" + tag, 2.0 * b.cout * double(C) * K * double(no),
+                                 b.conv->gemm_bytes() + double(no) * C * K * 2 + double(no) * b.cout * 4,
+                                 gemm_kernel_name(op)})))
+            return rc;
+        std::swap(cur, nxt);
+        L = Lo;
+    }
+    // fc_mu: conv k3 (left pad 2) -> [B*T][Lt], then the latent layout [B][Lt][T]
+    const int C = c->enc_blocks.back().cout;
+    const int64_t n = int64_t(B) * L;
+    {
+        const float* x = cur;
+        __half* col = d.s16;
+        const int Lb = static_cast<int>(L);
+        rc = sink.kernel(
+            [=](cudaStream_t st) { return launch_im2col(x, nullptr, nullptr, col, B, Lb, C, 3, 1, 2, Lb, st); },
+            {"im2col_fc_mu", 0.0, double(n) * C * 4 + double(n) * C * 3 * 2, "snake_im2col_kernel<3>"});
+        if (rc) return rc;
+    }
+    GemmOp op;
+    if ((rc = setup_pointwise(&op, c->fc_mu->gemm_view(), C * 3, Lt, d.s16, n, c->fc_b.v, nullptr, nullptr, nullptr, 0,
+                              nxt, d.status)))
+        return rc;
+    if ((rc = sink.gemm(op, {"conv_fc_mu", 2.0 * Lt * double(C) * 3 * double(n),
+                             c->fc_mu->gemm_bytes() + double(n) * C * 3 * 2 + double(n) * Lt * 4, gemm_kernel_name(op)})))
+        return rc;
+    {
+        const float* y = nxt;
+        float* z = d.out;
+        const int Tq = static_cast<int>(L);
+        rc = sink.kernel(
+            [=](cudaStream_t s) {
+                const cudaError_t e = launch_pdl(latent_transpose_kernel, dim3(grid_1d(n * Lt, 256)), dim3(256), 0, s,
+                                                 y, z, B, Tq, Lt);
+                return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "latent transpose launch");
+            },
+            {"latent_transpose", 0.0, double(n) * Lt * 8, "latent_transpose_kernel"});
+        if (rc) return rc;
+    }
+    return VXB_OK;
+}
+
 }  // namespace
 
 extern "C" int vxb_build_plan(vxb_ctx* c, int B, int T, int use_graph) {
@@ -1307,6 +1576,82 @@ extern "C" int vxb_decode_device(vxb_ctx* c, const float* z_dev, float* out_dev,
     int rc = run_plan(c, s);
     if (rc) return rc;
     if (out_dev != P.out) CUDA_TRY(cudaMemcpyAsync(out_dev, P.out, zout, cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return VXB_OK;
+}
+
+extern "C" int vxb_build_encode_plan(vxb_ctx* c, int B, int T) {
+    if (!c || B <= 0 || T <= 0) return fail(VXB_ERR_INVALID_ARGUMENT, "bad encode plan shape");
+    if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare before vxb_build_encode_plan");
+    DeviceGuard g(c->device);
+    int rc = bind_encoder(c);
+    if (rc) return rc;
+    const int64_t hop = vxb_encoder_hop(c);
+    if (int64_t(T) * hop > (int64_t(1) << 30) / c->encoder_dim)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "encode plan: waveform too long for one plan");
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (c->enc_plan) free_plan(c->enc_plan.get());
+    c->enc_plan = std::make_unique<Plan>();
+    Plan& P = *c->enc_plan;
+    P.B = B;
+    P.T = T;
+    int64_t max_x, max_col;
+    enc_arena_sizes(c, B, T, &max_x, &max_col);
+    CUDA_TRY(cudaMalloc(&P.z, sizeof(float) * B * T * hop));                 // waveforms
+    CUDA_TRY(cudaMalloc(&P.out, sizeof(float) * int64_t(B) * c->latent_dim * T));  // latents
+    DecodeBufs& d = P.bufs;
+    CUDA_TRY(cudaMalloc(&d.xa, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&d.xb, sizeof(float) * max_x));
+    CUDA_TRY(cudaMalloc(&d.h16, sizeof(__half) * max_x));
+    CUDA_TRY(cudaMalloc(&d.s16, sizeof(__half) * max_col));
+    d.z = P.z;
+    d.out = P.out;
+    d.status = c->status;
+    P.bytes = sizeof(float) * (int64_t(B) * T * hop + int64_t(B) * c->latent_dim * T + 2 * max_x) +
+              sizeof(__half) * (max_x + max_col);
+    PlanSink sink(P);
+    return emit_encode(c, d, B, T, sink);
+}
+
+namespace {
+
+int run_ops(vxb_ctx* c, Plan& P, cudaStream_t s) {
+    CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), s));
+    for (auto& op : P.ops)
+        if (int rc = op(s)) return rc;
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_encode(vxb_ctx* c, const float* audio_host, float* latent_host) {
+    if (!c || !audio_host || !latent_host) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!c->enc_plan) return fail(VXB_ERR_NOT_READY, "no encode plan: call vxb_build_encode_plan");
+    DeviceGuard g(c->device);
+    Plan& P = *c->enc_plan;
+    const size_t ain = sizeof(float) * P.B * P.T * vxb_encoder_hop(c);
+    const size_t lout = sizeof(float) * int64_t(P.B) * c->latent_dim * P.T;
+    CUDA_TRY(cudaMemcpyAsync(P.z, audio_host, ain, cudaMemcpyHostToDevice, c->stream));
+    int rc = run_ops(c, P, c->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(latent_host, P.out, lout, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = wait_stream(c->stream, 60000))) return rc;
+    return check_status(c);
+}
+
+extern "C" int vxb_encode_device(vxb_ctx* c, const float* audio_dev, float* latent_dev, void* stream) {
+    if (!c || !audio_dev || !latent_dev) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    if (!c->enc_plan) return fail(VXB_ERR_NOT_READY, "no encode plan: call vxb_build_encode_plan");
+    DeviceGuard g(c->device);
+    Plan& P = *c->enc_plan;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    const size_t ain = sizeof(float) * P.B * P.T * vxb_encoder_hop(c);
+    const size_t lout = sizeof(float) * int64_t(P.B) * c->latent_dim * P.T;
+    if (audio_dev != P.z) CUDA_TRY(cudaMemcpyAsync(P.z, audio_dev, ain, cudaMemcpyDeviceToDevice, s));
+    int rc = run_ops(c, P, s);
+    if (rc) return rc;
+    if (latent_dev != P.out) CUDA_TRY(cudaMemcpyAsync(latent_dev, P.out, lout, cudaMemcpyDeviceToDevice, s));
     CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, s));
     return VXB_OK;
 }
@@ -1493,15 +1838,17 @@ extern "C" int vxb_convt(const void* w, int w_type, int Cin, int Cout, int s, co
 
 // ------------------------------------------------------------ introspection --
 
-extern "C" int vxb_plan_num_ops(const vxb_ctx* c) {
-    return (c && c->plan) ? static_cast<int>(c->plan->ops.size()) : 0;
+namespace {
+
+const Plan* plan_of(const vxb_ctx* c, int which) {
+    if (!c) return nullptr;
+    return which == 1 ? c->enc_plan.get() : c->plan.get();
 }
 
-extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
-                                double* flops, double* bytes) {
-    if (!c || !c->plan || idx < 0 || idx >= static_cast<int>(c->plan->info.size()))
-        return fail(VXB_ERR_INVALID_ARGUMENT, "bad op index");
-    const auto& in = c->plan->info[idx];
+int op_info(const Plan* P, int idx, char* name, int name_cap, char* kernel, int kernel_cap, double* flops,
+            double* bytes) {
+    if (!P || idx < 0 || idx >= static_cast<int>(P->info.size())) return fail(VXB_ERR_INVALID_ARGUMENT, "bad op index");
+    const auto& in = P->info[idx];
     if (name && name_cap > 0) std::snprintf(name, name_cap, "%s", in.name.c_str());
     if (kernel && kernel_cap > 0) std::snprintf(kernel, kernel_cap, "%s", in.kernel.c_str());
     if (flops) *flops = in.flops;
@@ -1509,10 +1856,11 @@ extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_
     return VXB_OK;
 }
 
-extern "C" int vxb_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_bytes, float* ms_out) {
-    if (!c || !c->plan || reps <= 0 || !ms_out) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+// Device time of every op of a plan (CUDA events between launches on the
+// context's stream), averaged over reps, the buffer `flush` rewritten
+// before each rep.
+int time_plan_ops(vxb_ctx* c, Plan& P, int reps, void* flush, size_t flush_bytes, float* ms_out) {
     DeviceGuard g(c->device);
-    Plan& P = *c->plan;
     const size_t nops = P.ops.size();
     std::vector<cudaEvent_t> ev(nops + 1);
     for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
@@ -1538,6 +1886,36 @@ extern "C" int vxb_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_byte
     if (rc) return rc;
     for (size_t i = 0; i < nops; ++i) ms_out[i] = static_cast<float>(acc[i] / reps);
     return check_status(c);
+}
+
+}  // namespace
+
+extern "C" int vxb_plan_num_ops(const vxb_ctx* c) {
+    return (c && c->plan) ? static_cast<int>(c->plan->ops.size()) : 0;
+}
+
+extern "C" int vxb_plan_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
+                                double* flops, double* bytes) {
+    return op_info(plan_of(c, 0), idx, name, name_cap, kernel, kernel_cap, flops, bytes);
+}
+
+extern "C" int vxb_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_bytes, float* ms_out) {
+    if (!c || !c->plan || reps <= 0 || !ms_out) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+    return time_plan_ops(c, *c->plan, reps, flush, flush_bytes, ms_out);
+}
+
+extern "C" int vxb_encode_num_ops(const vxb_ctx* c) {
+    return (c && c->enc_plan) ? static_cast<int>(c->enc_plan->ops.size()) : 0;
+}
+
+extern "C" int vxb_encode_op_info(const vxb_ctx* c, int idx, char* name, int name_cap, char* kernel, int kernel_cap,
+                                  double* flops, double* bytes) {
+    return op_info(plan_of(c, 1), idx, name, name_cap, kernel, kernel_cap, flops, bytes);
+}
+
+extern "C" int vxb_encode_time_ops(vxb_ctx* c, int reps, void* flush, size_t flush_bytes, float* ms_out) {
+    if (!c || !c->enc_plan || reps <= 0 || !ms_out) return fail(VXB_ERR_INVALID_ARGUMENT, "bad arguments");
+    return time_plan_ops(c, *c->enc_plan, reps, flush, flush_bytes, ms_out);
 }
 
 // ------------------------------------------------ allocation-free decode --

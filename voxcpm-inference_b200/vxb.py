@@ -56,6 +56,15 @@ SIGNATURES = {
     "vxb_pointwise": (_i, [_vp, _i, _i, _i, _vp, _i64, _vp, _vp, _vp, _i, _vp, _vp]),
     "vxb_convt": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
     "vxb_residual_unit": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
+    "vxb_set_encoder_config": (_i, [_vp, _i, ctypes.POINTER(_i), _i]),
+    "vxb_encoder_hop": (_i, [_vp]),
+    "vxb_build_encode_plan": (_i, [_vp, _i, _i]),
+    "vxb_encode": (_i, [_vp, _vp, _vp]),
+    "vxb_encode_device": (_i, [_vp, _vp, _vp, _vp]),
+    "vxb_encode_num_ops": (_i, [_vp]),
+    "vxb_encode_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
+                                ctypes.POINTER(ctypes.c_double)]),
+    "vxb_encode_time_ops": (_i, [_vp, _i, _vp, _sz, ctypes.POINTER(ctypes.c_float)]),
 }
 
 
@@ -235,6 +244,60 @@ class Decoder:
         n = lib().vxb_plan_num_ops(self.h)
         ms = (ctypes.c_float * n)()
         check(lib().vxb_time_ops(self.h, reps, ptr(flush), flush_bytes, ms))
+        return list(ms)
+
+    # ---------------------------------------------------------- encoder --
+
+    @property
+    def encoder_hop(self) -> int:
+        return lib().vxb_encoder_hop(self.h)
+
+    def build_encode_plan(self, batch: int, T: int):
+        check(lib().vxb_build_encode_plan(self.h, batch, T))
+        self.eB, self.eT = batch, T
+
+    def encode(self, audio: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Host waveforms [B, n] (16 kHz; zero-padded here to a hop multiple, as
+        the reference's preprocess does) -> host latents [B, latent, T], T = ceil(n / hop)."""
+        audio = np.asarray(audio, dtype=np.float32)
+        if audio.ndim == 1:
+            audio = audio[None]
+        B, n = audio.shape
+        hop = self.encoder_hop
+        if hop <= 0:
+            raise VxbError(ERR_NOT_READY, "no encoder config")
+        T = (n + hop - 1) // hop
+        if n != T * hop:
+            audio = np.concatenate([audio, np.zeros((B, T * hop - n), np.float32)], axis=1)
+        audio = np.ascontiguousarray(audio)
+        if (B, T) != (getattr(self, "eB", None), getattr(self, "eT", None)):
+            self.build_encode_plan(B, T)
+        if out is None:
+            out = np.empty((B, self.config()["latent_dim"], T), np.float32)
+        check(lib().vxb_encode(self.h, ptr(audio), ptr(out)))
+        return out
+
+    def encode_host_ptrs(self, audio_ptr: int, latent_ptr: int):
+        check(lib().vxb_encode(self.h, audio_ptr, latent_ptr))
+
+    def encode_device(self, audio_dev, latent_dev, stream=None):
+        check(lib().vxb_encode_device(self.h, ptr(audio_dev), ptr(latent_dev), _stream(stream)))
+
+    def encode_ops(self) -> list[dict]:
+        """[{name, kernel, flops, bytes}] for every launch of the encode plan."""
+        out = []
+        for i in range(lib().vxb_encode_num_ops(self.h)):
+            name, kern = ctypes.create_string_buffer(64), ctypes.create_string_buffer(64)
+            fl, by = ctypes.c_double(), ctypes.c_double()
+            check(lib().vxb_encode_op_info(self.h, i, name, 64, kern, 64, ctypes.byref(fl), ctypes.byref(by)))
+            out.append({"name": name.value.decode(), "kernel": kern.value.decode(), "flops": fl.value,
+                        "bytes": by.value})
+        return out
+
+    def encode_time_ops(self, reps: int = 10, flush=None, flush_bytes: int = 0) -> list[float]:
+        n = lib().vxb_encode_num_ops(self.h)
+        ms = (ctypes.c_float * n)()
+        check(lib().vxb_encode_time_ops(self.h, reps, ptr(flush), flush_bytes, ms))
         return list(ms)
 
     def debug_stage(self, stage: int, n: int) -> np.ndarray:

@@ -13,7 +13,11 @@ seed and written in the reference's own GGUF layout:
 * Q4_0 blocks of 32 with an fp16 scale, quantised with the deterministic
   rounding of ggml's ``quantize_row_q4_0_ref`` (ggml-quants.c:113-145);
 * encoder tensors present by name only (``load_encoder_weights`` only checks
-  that they exist, audio-vae.cpp:331-363).
+  that they exist, audio-vae.cpp:331-363), or with ``encoder=True`` the full
+  encoder (audio-vae.cpp:553-570, 640-650): head conv ``[7, 1, E]``, per block
+  three residual units, Snake alpha and the strided conv ``[2s, Cin, Cout]``
+  (F16) or folded ``[2s*Cin, Cout]`` (Q4_0, row ``j = cin*2s + k``,
+  audio-vae.cpp:78-88), then ``fc_mu`` ``[3, C, latent]`` / ``[3*C, latent]``.
 
 Weights: N(0, gain^2 / fan_in) for every conv, alpha ~ U(0.5, 1.5), bias ~
 N(0, 0.01^2).  gain = 0.5 keeps the waveform well inside tanh's linear range
@@ -127,19 +131,28 @@ def decoder_plan(decoder_dim=1536, rates=DEFAULT_RATES):
 
 
 def make_model(quant: str = "f16", seed: int = 0, gain: float = 0.5, decoder_dim: int = 1536,
-               latent_dim: int = 64, rates=DEFAULT_RATES, convt_3d: bool = False) -> bytes:
+               latent_dim: int = 64, rates=DEFAULT_RATES, convt_3d: bool = False, encoder: bool = False,
+               encoder_dim: int = 128, encoder_gain: float = 0.85) -> bytes:
     """Returns the bytes of a seeded decoder GGUF.
 
-    quant: "f16" (all tensors F16) or "q4_0" (Q4_0-mixed: model.1, the 4
+    quant: "f16" (all tensors F16), "f32" (all F32: a model with no fp16
+    rounding anywhere, for pinning the oracle's structure against the
+    reference; the GPU path takes F16 / Q4_0 only) or "q4_0" (Q4_0-mixed: model.1, the 4
     transposed convs and the 12 residual pointwise convs as Q4_0, the 17
     encoder matrices likewise, everything else F16).  convt_3d writes F16
     transposed-conv weights as the 3-D [2s, Cout, Cin] tensor the F16
     checkpoints use (same memory order as the folded 2-D layout).
+    encoder=True writes a full encoder of width encoder_dim (its weights
+    drawn after the decoder's, so the decoder is the same either way; convs
+    N(0, encoder_gain^2 / fan_in): the Snake residual units amplify, so the
+    latent's scale is steep in the gain -- 0.85 gives a latent of std about
+    1.3 on make_audio input, 0.7 about 0.06, 1.0 about 12);
+    otherwise the encoder tensors are 32-value placeholders.
     """
-    assert quant in ("f16", "q4_0")
+    assert quant in ("f16", "q4_0", "f32")
     rng = np.random.default_rng(seed)
     w = GGUFWriter()
-    w.u32("voxcpm_audio_vae_config_encoder_dim", 128)
+    w.u32("voxcpm_audio_vae_config_encoder_dim", encoder_dim)
     w.u32("voxcpm_audio_vae_config_decoder_dim", decoder_dim)
     w.u32("voxcpm_audio_vae_config_latent_dim", latent_dim)
     w.u32("voxcpm_audio_vae_config_sample_rate", 16000)
@@ -153,6 +166,8 @@ def make_model(quant: str = "f16", seed: int = 0, gain: float = 0.5, decoder_dim
         ne = ne if ne is not None else tuple(reversed(arr.shape))
         if q and quant == "q4_0":
             w.tensor(name, ne, GGML_Q4_0, quantize_q4_0(arr).tobytes())
+        elif quant == "f32":
+            w.tensor(name, ne, GGML_F32, arr.tobytes())
         else:
             w.tensor(name, ne, GGML_F16, arr.astype(np.float16).tobytes())
 
@@ -194,6 +209,38 @@ def make_model(quant: str = "f16", seed: int = 0, gain: float = 0.5, decoder_dim
     add(f"{p}{nb + 3}.bias", bias(1))
 
     e = "audio_vae.encoder."
+    if encoder:
+        def conv_e(shape, fan_in):
+            return rng.normal(0.0, encoder_gain / np.sqrt(fan_in), shape)
+
+        def conv_k(name, cout, cin, k):
+            # [Cout][Cin][K] in memory: F16 as the 3-D [K, Cin, Cout] tensor,
+            # Q4_0 folded to 2-D [K*Cin, Cout] (blocks need 32 | K*Cin)
+            arr = conv_e((cout, cin, k), cin * k)
+            if quant == "q4_0":
+                add(name, arr.reshape(cout, cin * k), q=True)
+            else:
+                add(name, arr)
+
+        add(e + "block.0.weight", conv_e((encoder_dim, 1, 7), 7))
+        add(e + "block.0.bias", bias(encoder_dim))
+        c = encoder_dim
+        for b, s in enumerate(reversed(rates), start=1):
+            for r in range(3):
+                rp = f"{e}block.{b}.block.{r}.block."
+                add(rp + "0.alpha", alpha(c))
+                add(rp + "1.weight", conv_e((c, 1, 7), 7))
+                add(rp + "1.bias", bias(c))
+                add(rp + "2.alpha", alpha(c))
+                add(rp + "3.weight", conv_e((c, c), c), q=True)
+                add(rp + "3.bias", bias(c))
+            add(f"{e}block.{b}.block.3.alpha", alpha(c))
+            conv_k(f"{e}block.{b}.block.4.weight", 2 * c, c, 2 * s)
+            add(f"{e}block.{b}.block.4.bias", bias(2 * c))
+            c *= 2
+        conv_k(e + "fc_mu.weight", latent_dim, c, 3)
+        add(e + "fc_mu.bias", bias(latent_dim))
+        return w.tobytes()
     zeros = np.zeros(32, dtype=np.float32)
     add(e + "block.0.weight", zeros)
     add(e + "block.0.bias", zeros)
@@ -214,6 +261,21 @@ def write_model(path: str, **kw) -> str:
     with open(path, "wb") as f:
         f.write(data)
     return hashlib.sha256(data).hexdigest()
+
+
+def make_audio(n: int, batch: int = 1, seed: int = 7) -> np.ndarray:
+    """float32 waveforms [batch, n] at 16 kHz: a few seeded partials (80 Hz - 4 kHz,
+    decaying amplitudes, random phases) plus a little noise, peak about 0.5."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(n, dtype=np.float64) / 16000.0
+    out = np.empty((batch, n), dtype=np.float32)
+    for b in range(batch):
+        f = rng.uniform(80.0, 4000.0, 6)
+        a = rng.uniform(0.02, 0.12, 6)
+        ph = rng.uniform(0.0, 2 * np.pi, 6)
+        x = (a[:, None] * np.sin(2 * np.pi * f[:, None] * t[None, :] + ph[:, None])).sum(0)
+        out[b] = (x + rng.normal(0.0, 0.01, n)).astype(np.float32)
+    return out
 
 
 def make_latents(steps: int, T: int, latent_dim: int = 64, seed: int = 1, ar: float | None = None,

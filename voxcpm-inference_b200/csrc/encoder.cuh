@@ -2,10 +2,12 @@
 // residual-unit and GEMM kernels):
 //   enc_head_kernel      head conv k7 (pad 3) 1 -> E channels on the waveform
 //                        (encode_tensor, reference src/audio-vae.cpp:640-643).
-//   snake_im2col_kernel  [Snake ->] im2col of a strided causal conv, fp16,
+//   im2col_rows_kernel   im2col of a strided causal conv over its fp16 input
+//                        (the previous kernel's epilogue applied the Snake),
 //                        the B operand of the conv as one pointwise GEMM
 //                        (causal_conv1d + conv1d_mul_mat_impl, :476-493,
-//                        :218-234).
+//                        :218-234); permute_ck_kernel reorders the conv
+//                        weight to match once.
 //   latent_transpose_kernel  [B*T][L] -> [B][L][T] (ggml ne=[T, L]).
 #pragma once
 
@@ -15,78 +17,97 @@ namespace vxb {
 
 // x[b*L + t][c] = bias[c] + sum_k w[c][k] * a[b][t + k - 6], the waveform
 // sample rounded to fp16 first as the reference's F16 mul_mat rounds its
-// im2col rows (the weights are F16 values already).  One float4 of channels
-// per thread; C % 4 == 0.
+// im2col rows (the weights are F16 values already).  A block is C/4 channel
+// quads x G token groups (G = blockDim / (C/4)); a thread keeps its quad's 28
+// taps in registers and walks a run of kHeadRun consecutive tokens with the
+// 7 samples they need in a sliding register window (one new sample per
+// token, the same address for the whole group).  The group's C/4 float4
+// stores cover one contiguous token row.  C % 4 == 0, C / 4 <= blockDim.
+constexpr int kHeadRun = 32;
+
 __global__ void enc_head_kernel(const float* __restrict__ audio, const float* __restrict__ w /*[C][7]*/,
                                 const float* __restrict__ bias, float* __restrict__ x, int B, long long L,
                                 int C) {
     grid_dep_sync();
-    const int cq = C / 4;
-    const long long total = static_cast<long long>(B) * L * cq;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int c = static_cast<int>(i % cq) * 4;
-        const long long n = i / cq;
-        const long long t = n % L;
-        const float* a = audio + (n - t);  // this waveform
-        float4 acc = *reinterpret_cast<const float4*>(bias + c);
+    const int qn = C / 4;
+    const int G = blockDim.x / qn;
+    const int q = threadIdx.x % qn, g = threadIdx.x / qn;
+    if (g >= G) return;
+    const int c = q * 4;
+    float4 wk[7];
 #pragma unroll
-        for (int k = 0; k < 7; ++k) {
-            const long long src = t + k - 6;
-            if (src < 0) continue;
-            const float v = __half2float(__float2half_rn(a[src]));
-            acc.x = fmaf(w[(c + 0) * 7 + k], v, acc.x);
-            acc.y = fmaf(w[(c + 1) * 7 + k], v, acc.y);
-            acc.z = fmaf(w[(c + 2) * 7 + k], v, acc.z);
-            acc.w = fmaf(w[(c + 3) * 7 + k], v, acc.w);
+    for (int k = 0; k < 7; ++k)
+        wk[k] = make_float4(w[(c + 0) * 7 + k], w[(c + 1) * 7 + k], w[(c + 2) * 7 + k], w[(c + 3) * 7 + k]);
+    const float4 bb = *reinterpret_cast<const float4*>(bias + c);
+    const long long runs = (L + kHeadRun - 1) / kHeadRun;
+    for (long long r = static_cast<long long>(blockIdx.x) * G + g; r < B * runs;
+         r += static_cast<long long>(gridDim.x) * G) {
+        const long long b = r / runs;
+        const long long t0 = (r - b * runs) * kHeadRun;
+        const long long t1 = min(t0 + kHeadRun, L);
+        const float* a = audio + b * L;
+        float win[7];  // samples t - 6 .. t
+#pragma unroll
+        for (int k = 0; k < 6; ++k) {
+            const long long src = t0 + k - 6;
+            win[k + 1] = src >= 0 ? __half2float(__float2half_rn(a[src])) : 0.f;
         }
-        *reinterpret_cast<float4*>(x + n * C + c) = acc;
+        float* xo = x + (b * L + t0) * C + c;
+        for (long long t = t0; t < t1; ++t, xo += C) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) win[k] = win[k + 1];
+            win[6] = __half2float(__float2half_rn(a[t]));
+            float4 acc = bb;
+#pragma unroll
+            for (int k = 0; k < 7; ++k) {
+                acc.x = fmaf(wk[k].x, win[k], acc.x);
+                acc.y = fmaf(wk[k].y, win[k], acc.y);
+                acc.z = fmaf(wk[k].z, win[k], acc.z);
+                acc.w = fmaf(wk[k].w, win[k], acc.w);
+            }
+            *reinterpret_cast<float4*>(xo) = acc;
+        }
     }
 }
 
-// col[(b*Lout + t)][ci*K + k] = f(x[b*Lin + t*s + k - lpad][ci]), zero where
-// that row is before the sequence start (the causal left padding) or past
-// its end; f = Snake(alpha, inv) or the identity (alpha == nullptr).  The
-// column order ci*K + k (k fastest) is the memory order of the conv weight
-// ([K, Cin, Cout] F16 or folded [K*Cin, Cout] Q4_0), so the conv is the GEMM
-// y[n][co] = sum_j W[co][j] col[n][j] with the weight as stored.  One thread
-// per (row, ci): its K values are one contiguous run of the row.
-template <int K>
-__global__ void snake_im2col_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
-                                    const float* __restrict__ inv, __half* __restrict__ col, int B, int Lin,
-                                    int C, int s, int lpad, int Lout) {
+// col[(b*Lout + t)][k*C + c] = g[b*L + t*s + k - lpad][c] (zero where that
+// row is before the sequence start: the causal left padding): the im2col
+// operand of a strided causal conv over the fp16 (already Snake-activated)
+// input, in the column order k*C + c of the conv weight's [Cout][K][Cin]
+// copy, so each output row is K whole input rows.  One 16-byte chunk (8
+// channels) per thread; C % 8 == 0.
+__global__ void im2col_rows_kernel(const __half* __restrict__ g, __half* __restrict__ col, int B, int L, int C, int K,
+                                   int s, int lpad, int Lout) {
     grid_dep_sync();
-    const long long total = static_cast<long long>(B) * Lout * C;
+    const int c8n = C / 8;
+    const long long per_row = static_cast<long long>(K) * c8n;
+    const long long total = static_cast<long long>(B) * Lout * per_row;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int ci = static_cast<int>(i % C);
-        const long long n = i / C;
+        const long long n = i / per_row;
+        const int rem = static_cast<int>(i - n * per_row);
+        const int k = rem / c8n, c8 = rem - k * c8n;
         const int b = static_cast<int>(n / Lout);
         const int t = static_cast<int>(n - static_cast<long long>(b) * Lout);
-        const float* xb = x + static_cast<long long>(b) * Lin * C + ci;
-        const float al = alpha ? alpha[ci] : 0.f, iv = alpha ? inv[ci] : 0.f;
-        __half v[K];
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int src = t * s + k - lpad;
-            float u = 0.f;
-            if (src >= 0 && src < Lin) {
-                u = xb[static_cast<long long>(src) * C];
-                if (alpha) u = snake(u, al, iv);
-            }
-            v[k] = __float2half_rn(u);
-        }
-        __half* o = col + i * K;
-        if constexpr (K % 8 == 0) {
-#pragma unroll
-            for (int j = 0; j < K / 8; ++j) reinterpret_cast<uint4*>(o)[j] = reinterpret_cast<const uint4*>(v)[j];
-        } else if constexpr (K % 2 == 0) {
-#pragma unroll
-            for (int j = 0; j < K / 2; ++j) reinterpret_cast<__half2*>(o)[j] = __halves2half2(v[2 * j], v[2 * j + 1]);
-        } else {
-#pragma unroll
-            for (int k = 0; k < K; ++k) o[k] = v[k];
-        }
+        const int src = t * s + k - lpad;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (src >= 0 && src < L)
+            v = *reinterpret_cast<const uint4*>(g + (static_cast<long long>(b) * L + src) * C + c8 * 8);
+        reinterpret_cast<uint4*>(col)[i] = v;
+    }
+}
+
+// out[(co*K + k)*Cin + ci] = in[(co*Cin + ci)*K + k]: a conv weight's fp16
+// [Cout][Cin][K] -> [Cout][K][Cin] (once, when the encoder is bound).
+__global__ void permute_ck_kernel(const __half* __restrict__ in, __half* __restrict__ out, int Cout, int Cin, int K) {
+    const long long total = static_cast<long long>(Cout) * Cin * K;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int ci = static_cast<int>(i % Cin);
+        const long long r = i / Cin;
+        const int k = static_cast<int>(r % K);
+        const long long co = r / K;
+        out[i] = in[(co * Cin + ci) * K + k];
     }
 }
 

@@ -632,6 +632,7 @@ struct EncBlock {
     ResUnit ru[3];
     Vec alpha, bias;
     const DevTensor* conv = nullptr;  // [Cout][Cin][2s] in memory
+    __half* wperm = nullptr;          // its fp16 copy reordered [Cout][2s][Cin] (the im2col column order)
 };
 
 struct OpInfo {
@@ -648,7 +649,8 @@ struct DecodeBufs {
     float* xa = nullptr;       // fp32 residual stream (ping)
     float* xb = nullptr;       // fp32 residual stream (pong)
     __half* h16 = nullptr;     // fp16 pointwise B operand (prologue output, head output)
-    __half* s16 = nullptr;     // fp16 transposed-conv B operand
+    __half* s16 = nullptr;     // fp16 transposed-conv B operand (encoder: the im2col operand)
+    __half* g16 = nullptr;     // encoder: fp16 Snake output of a block's last residual unit
     int* status = nullptr;     // device status word
 };
 
@@ -699,6 +701,7 @@ struct vxb_ctx {
     Vec enc_b0, fc_b;
     std::vector<EncBlock> enc_blocks;
     const DevTensor* fc_mu = nullptr;
+    __half* fc_perm = nullptr;  // fc_mu weight [latent][3][C]
     std::unique_ptr<Plan> enc_plan;
     int* status = nullptr;         // device status word
     int* status_host = nullptr;    // pinned mirror
@@ -727,6 +730,7 @@ void free_plan(Plan* p) {
     cudaFree(p->bufs.xb);
     cudaFree(p->bufs.h16);
     cudaFree(p->bufs.s16);
+    cudaFree(p->bufs.g16);
 }
 
 const DevTensor* get(vxb_ctx* c, const std::string& name) {
@@ -1289,6 +1293,18 @@ int bind_encoder(vxb_ctx* c) {
     if (!(c->fc_mu->n_dims == 3 ? c->fc_mu->ne[0] == 3 && c->fc_mu->ne[1] == C : c->fc_mu->ne[0] == 3 * C))
         return fail(VXB_ERR_INVALID_FORMAT, "fc_mu.weight: expected [3, C, latent] or [3*C, latent]");
     if ((rc = derive_vec(c, p + "fc_mu.bias", Lt, false, &c->fc_b))) return rc;
+    // conv weights reordered to [Cout][K][Cin]: an im2col row is then K whole input rows
+    auto permute = [&](const DevTensor* t, int cout, int cin, int k, __half** out) {
+        CUDA_TRY(cudaMalloc(out, sizeof(__half) * size_t(cout) * cin * k));
+        c->derived_allocs.push_back(*out);
+        permute_ck_kernel<<<grid_1d(int64_t(cout) * cin * k, 256), 256, 0, c->stream>>>(
+            static_cast<const __half*>(t->gemm_view().p), *out, cout, cin, k);
+        CUDA_TRY(cudaGetLastError());
+        return VXB_OK;
+    };
+    for (EncBlock& b : c->enc_blocks)
+        if ((rc = permute(b.conv, b.cout, b.cin, 2 * b.s, &b.wperm))) return rc;
+    if ((rc = permute(c->fc_mu, Lt, C, 3, &c->fc_perm))) return rc;
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     c->enc_bound = true;
     return VXB_OK;
@@ -1310,28 +1326,22 @@ void enc_arena_sizes(const vxb_ctx* c, int B, int T, int64_t* max_x, int64_t* ma
     *max_col = std::max(*max_col, int64_t(B) * L * c->enc_blocks.back().cout * 3);
 }
 
-int launch_im2col(const float* x, const float* alpha, const float* inv, __half* col, int B, int Lin, int C, int K,
-                  int s, int lpad, int Lout, cudaStream_t st) {
-    const dim3 grid(grid_1d(int64_t(B) * Lout * C, 256)), block(256);
-    cudaError_t e;
-    switch (K) {
-        case 3: e = launch_pdl(snake_im2col_kernel<3>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
-        case 4: e = launch_pdl(snake_im2col_kernel<4>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
-        case 6: e = launch_pdl(snake_im2col_kernel<6>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
-        case 10: e = launch_pdl(snake_im2col_kernel<10>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
-        case 16: e = launch_pdl(snake_im2col_kernel<16>, grid, block, 0, st, x, alpha, inv, col, B, Lin, C, s, lpad, Lout); break;
-        default: return fail(VXB_ERR_INVALID_ARGUMENT, "encoder conv: kernel size must be 3, 4, 6, 10 or 16");
-    }
+int launch_im2col(const __half* g, __half* col, int B, int L, int C, int K, int s, int lpad, int Lout,
+                  cudaStream_t st) {
+    const cudaError_t e = launch_pdl(im2col_rows_kernel, dim3(grid_1d(int64_t(B) * Lout * K * (C / 8), 256)),
+                                     dim3(256), 0, st, g, col, B, L, C, K, s, lpad, Lout);
     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("im2col launch: ") + cudaGetErrorString(e));
 }
 
 // The launch sequence of one encode of B waveforms of T latent frames
 // (T * hop samples each; encode_tensor, src/audio-vae.cpp:640-650):
 //   head conv k7 -> per block: 3 residual units (the decoder's kernels: the
-//   fused unit up to 128 channels, else prologue + pointwise GEMM), Snake +
-//   im2col (k 2s, stride s, left pad 2 ceil(s/2)) -> the conv as one
-//   pointwise GEMM (K = 2s Cin) doubling the channels
-//   -> fc_mu: im2col (k 3, left pad 2) -> GEMM -> transpose to [B][L][T].
+//   fused unit up to 128 channels, else prologue + pointwise GEMM), the last
+//   one's epilogue applying the block's Snake and writing fp16 -> im2col
+//   rows (k 2s, stride s, left pad 2 ceil(s/2)) -> the conv as one pointwise
+//   GEMM (K = 2s Cin, weight in [Cout][2s][Cin] order) doubling the channels
+//   (fp32, or fp16 after the last block: fc_mu's input)
+//   -> fc_mu: im2col rows (k 3, left pad 2) -> GEMM -> transpose to [B][L][T].
 int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
     const int E = c->encoder_dim, Lt = c->latent_dim;
     const int sms = num_sms(c->device);
@@ -1342,10 +1352,12 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
         float* o = d.xa;
         const int64_t n = int64_t(B) * L;
         const long long Lq = L;
+        const int G = 256 / (E / 4);
+        const int64_t runs = int64_t(B) * ((L + kHeadRun - 1) / kHeadRun);
+        const int grid = static_cast<int>(std::min<int64_t>((runs + G - 1) / G, int64_t(sms) * 16));
         rc = sink.kernel(
             [=](cudaStream_t s) {
-                const cudaError_t e = launch_pdl(enc_head_kernel, dim3(grid_1d(n * E / 4, 256)), dim3(256), 0, s, a,
-                                                 w, bb, o, B, Lq, E);
+                const cudaError_t e = launch_pdl(enc_head_kernel, dim3(grid), dim3(256), 0, s, a, w, bb, o, B, Lq, E);
                 return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "encoder head launch");
             },
             {"enc_head", 14.0 * double(n) * E, double(n) * (4 + E * 4), "enc_head_kernel"});
@@ -1354,7 +1366,8 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
     float* cur = d.xa;
     float* nxt = d.xb;
     static const int kDil[3] = {1, 3, 9};
-    for (size_t bi = 0; bi < c->enc_blocks.size(); ++bi) {
+    const size_t nbk = c->enc_blocks.size();
+    for (size_t bi = 0; bi < nbk; ++bi) {
         const EncBlock& b = c->enc_blocks[bi];
         const int C = b.cin;
         const int Lb = static_cast<int>(L);
@@ -1364,17 +1377,21 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             const ResUnit& u = b.ru[r];
             const int dl = kDil[r];
             const std::string nm = tag + "u" + std::to_string(r);
+            // the last unit applies the block's Snake and writes fp16 (the conv's input)
+            const bool last = r == 2;
             if (resunit_fits(C)) {
                 ResUnitOp op;
-                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, nxt, kResPlain,
-                                        u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, u.pb.v, nullptr, nullptr, B,
-                                        Lb, sms, d.status)))
+                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur,
+                                        last ? static_cast<void*>(d.g16) : nxt, last ? kResSnakeF16 : kResPlain,
+                                        u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, u.pb.v,
+                                        last ? b.alpha.v : nullptr, last ? b.alpha.inv : nullptr, B, Lb, sms,
+                                        d.status)))
                     return rc;
                 rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
                                  {"resunit_" + nm, 2.0 * C * C * double(n) + 20.0 * double(n) * C,
-                                  u.pw->gemm_bytes() + double(n) * C * 8, op.kernel_name()});
+                                  u.pw->gemm_bytes() + double(n) * C * (last ? 6 : 8), op.kernel_name()});
                 if (rc) return rc;
-                std::swap(cur, nxt);
+                if (!last) std::swap(cur, nxt);
                 continue;
             }
             {
@@ -1390,55 +1407,54 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                 if (rc) return rc;
             }
             GemmOp op;
-            if ((rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, nullptr, nullptr, 0, nxt,
-                                      d.status)))
+            if ((rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, last ? b.alpha.v : nullptr,
+                                      last ? b.alpha.inv : nullptr, last ? 1 : 0,
+                                      last ? static_cast<void*>(d.g16) : nxt, d.status)))
                 return rc;
-            if ((rc = sink.gemm(op, {"pw_" + nm, 2.0 * C * C * double(n), u.pw->gemm_bytes() + double(n) * C * 10,
-                                     gemm_kernel_name(op)})))
+            if ((rc = sink.gemm(op, {"pw_" + nm, 2.0 * C * C * double(n),
+                                     u.pw->gemm_bytes() + double(n) * C * (last ? 8 : 10), gemm_kernel_name(op)})))
                 return rc;
-            std::swap(cur, nxt);
+            if (!last) std::swap(cur, nxt);
         }
-        // Snake + im2col, then the strided conv as one GEMM
+        // im2col rows of the Snake output, then the strided conv as one GEMM
         const int K = 2 * b.s, lpad = 2 * ((b.s + 1) / 2);
         const int Lo = static_cast<int>((L + lpad - K) / b.s + 1);
         const int64_t no = int64_t(B) * Lo;
         {
-            const float* x = cur;
+            const __half* g = d.g16;
             __half* col = d.s16;
-            const float *al = b.alpha.v, *iv = b.alpha.inv;
             const int s = b.s;
-            rc = sink.kernel(
-                [=](cudaStream_t st) { return launch_im2col(x, al, iv, col, B, Lb, C, K, s, lpad, Lo, st); },
-                {"im2col_" + tag, 20.0 * double(no) * C * K, double(n) * C * 4 + double(no) * C * K * 2,
-                 "snake_im2col_kernel<" + std::to_string(K) + ">"});
+            rc = sink.kernel([=](cudaStream_t st) { return launch_im2col(g, col, B, Lb, C, K, s, lpad, Lo, st); },
+                             {"im2col_" + tag, 0.0, double(n) * C * 2 + double(no) * C * K * 2, "im2col_rows_kernel"});
             if (rc) return rc;
         }
+        // the last block writes fp16: fc_mu's im2col reads it
+        const bool last_block = bi + 1 == nbk;
         GemmOp op;
-        if ((rc = setup_pointwise(&op, b.conv->gemm_view(), C * K, b.cout, d.s16, no, b.bias.v, nullptr, nullptr,
-                                  nullptr, 0, nxt, d.status)))
+        if ((rc = setup_pointwise(&op, WView{b.wperm, VXB_TYPE_F16, 0, nullptr, 0}, C * K, b.cout, d.s16, no,
+                                  b.bias.v, nullptr, nullptr, nullptr, last_block ? 1 : 0,
+                                  last_block ? static_cast<void*>(d.g16) : cur, d.status)))
             return rc;
         if ((rc = sink.gemm(op, {"conv_" + tag, 2.0 * b.cout * double(C) * K * double(no),
-                                 b.conv->gemm_bytes() + double(no) * C * K * 2 + double(no) * b.cout * 4,
+                                 b.conv->gemm_bytes() + double(no) * C * K * 2 + double(no) * b.cout * (last_block ? 2 : 4),
                                  gemm_kernel_name(op)})))
             return rc;
-        std::swap(cur, nxt);
         L = Lo;
     }
     // fc_mu: conv k3 (left pad 2) -> [B*T][Lt], then the latent layout [B][Lt][T]
     const int C = c->enc_blocks.back().cout;
     const int64_t n = int64_t(B) * L;
     {
-        const float* x = cur;
+        const __half* g = d.g16;
         __half* col = d.s16;
         const int Lb = static_cast<int>(L);
-        rc = sink.kernel(
-            [=](cudaStream_t st) { return launch_im2col(x, nullptr, nullptr, col, B, Lb, C, 3, 1, 2, Lb, st); },
-            {"im2col_fc_mu", 0.0, double(n) * C * 4 + double(n) * C * 3 * 2, "snake_im2col_kernel<3>"});
+        rc = sink.kernel([=](cudaStream_t st) { return launch_im2col(g, col, B, Lb, C, 3, 1, 2, Lb, st); },
+                         {"im2col_fc_mu", 0.0, double(n) * C * 2 + double(n) * C * 3 * 2, "im2col_rows_kernel"});
         if (rc) return rc;
     }
     GemmOp op;
-    if ((rc = setup_pointwise(&op, c->fc_mu->gemm_view(), C * 3, Lt, d.s16, n, c->fc_b.v, nullptr, nullptr, nullptr, 0,
-                              nxt, d.status)))
+    if ((rc = setup_pointwise(&op, WView{c->fc_perm, VXB_TYPE_F16, 0, nullptr, 0}, C * 3, Lt, d.s16, n, c->fc_b.v,
+                              nullptr, nullptr, nullptr, 0, nxt, d.status)))
         return rc;
     if ((rc = sink.gemm(op, {"conv_fc_mu", 2.0 * Lt * double(C) * 3 * double(n),
                              c->fc_mu->gemm_bytes() + double(n) * C * 3 * 2 + double(n) * Lt * 4, gemm_kernel_name(op)})))
@@ -1604,11 +1620,12 @@ extern "C" int vxb_build_encode_plan(vxb_ctx* c, int B, int T) {
     CUDA_TRY(cudaMalloc(&d.xb, sizeof(float) * max_x));
     CUDA_TRY(cudaMalloc(&d.h16, sizeof(__half) * max_x));
     CUDA_TRY(cudaMalloc(&d.s16, sizeof(__half) * max_col));
+    CUDA_TRY(cudaMalloc(&d.g16, sizeof(__half) * max_x));
     d.z = P.z;
     d.out = P.out;
     d.status = c->status;
     P.bytes = sizeof(float) * (int64_t(B) * T * hop + int64_t(B) * c->latent_dim * T + 2 * max_x) +
-              sizeof(__half) * (max_x + max_col);
+              sizeof(__half) * (2 * max_x + max_col);
     PlanSink sink(P);
     return emit_encode(c, d, B, T, sink);
 }

@@ -1,13 +1,14 @@
-"""The voxcpm C++ API over libvxb: a caller written like the reference's
-decode_waveform compiles, links and -- on a B200 -- decodes within the stated
-tolerance of the reference (golden L1 output)."""
+"""The voxcpm C++ API over libvxb: callers written like the reference's own
+(decode_waveform; AudioVAE::encode with last_input_tensor) compile, link and
+-- on a B200 -- decode / encode within the stated tolerances of the reference
+(golden outputs of its own code)."""
 import os
 import subprocess
 
 import numpy as np
 import pytest
 
-from cpp_api import build_api_decode
+from cpp_api import build_api_decode, build_api_encode
 from models import model_path
 
 G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -72,3 +73,32 @@ def test_cpp_load_from_store_rejects_missing_encoder_names(tmp_path):
     r = subprocess.run([exe, str(tmp_path / "m.gguf"), str(tmp_path / "z.f32"), "6", "1", str(tmp_path / "o.f32")],
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 3, (r.returncode, r.stderr)
+
+
+def test_cpp_encode_caller_compiles(tmp_path):
+    assert os.path.exists(build_api_encode(str(tmp_path)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,tol", [("f16_t6", 5e-3), ("q4_t6", 6e-2)])
+def test_cpp_caller_encodes_like_the_reference(tmp_path, name, tol):
+    """Relative to max|latent| (the encoder tolerances of test_gpu_encode.py)."""
+    import ast
+
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    exe = build_api_encode(str(tmp_path))
+    f = np.load(os.path.join(G, f"encode_{name}.npz"))
+    path, sha = model_path(**ast.literal_eval(str(f["model"])))
+    assert sha == str(f["sha"])
+    a = np.ascontiguousarray(f["audio"], dtype=np.float32)
+    steps, n = a.shape
+    a.tofile(tmp_path / "a.f32")
+    r = subprocess.run([exe, path, str(tmp_path / "a.f32"), str(n), str(steps), str(tmp_path / "o.f32")],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    got = np.fromfile(tmp_path / "o.f32", dtype=np.float32).reshape(f["latent"].shape)
+    ref = f["latent"]
+    assert np.abs(got - ref).max() <= tol * np.abs(ref).max()

@@ -165,7 +165,8 @@ VoxCPMBackend::~VoxCPMBackend() {
 
 VoxCPMBackend::VoxCPMBackend(VoxCPMBackend&& o) noexcept
     : type_(o.type_), n_threads_(o.n_threads_), ctx_(o.ctx_), description_(std::move(o.description_)),
-      staging_(std::move(o.staging_)), staging_bytes_(o.staging_bytes_), plan_b_(o.plan_b_), plan_t_(o.plan_t_) {
+      staging_(std::move(o.staging_)), staging_bytes_(o.staging_bytes_), plan_b_(o.plan_b_), plan_t_(o.plan_t_),
+      enc_plan_t_(o.enc_plan_t_) {
     o.ctx_ = nullptr;
 }
 
@@ -180,6 +181,7 @@ VoxCPMBackend& VoxCPMBackend::operator=(VoxCPMBackend&& o) noexcept {
         staging_bytes_ = o.staging_bytes_;
         plan_b_ = o.plan_b_;
         plan_t_ = o.plan_t_;
+        enc_plan_t_ = o.enc_plan_t_;
         o.ctx_ = nullptr;
     }
     return *this;
@@ -189,6 +191,14 @@ void VoxCPMBackend::reserve_compute_memory(ggml_cgraph* graph, const char* stage
     VOXCPM_UNUSED(stage);
     for (int i = 0; i < graph->n_nodes; ++i) {
         ggml_tensor* t = graph->nodes[i];
+        if (t->op == VOXCPM_OP_AUDIO_VAE_ENCODE) {
+            const int T = static_cast<int>(t->ne[0]);
+            if (T == enc_plan_t_) continue;
+            if (vxb_build_encode_plan(ctx_, 1, T) != VXB_OK)
+                throw Error(ErrorCode::BackendError, std::string("reserve_compute_memory: ") + vxb_last_error());
+            enc_plan_t_ = T;
+            continue;
+        }
         if (t->op != VOXCPM_OP_AUDIO_VAE_DECODE) continue;
         const ggml_tensor* z = t->src[0];
         const int T = static_cast<int>(z->ne[0]);
@@ -205,7 +215,8 @@ void VoxCPMBackend::alloc_graph(ggml_cgraph* graph, const char* stage) {
     VOXCPM_UNUSED(stage);
     for (int i = 0; i < graph->n_nodes; ++i) {
         ggml_tensor* t = graph->nodes[i];
-        const bool io = t->op == VOXCPM_OP_AUDIO_VAE_DECODE || (t->flags & GGML_TENSOR_FLAG_INPUT);
+        const bool io = t->op == VOXCPM_OP_AUDIO_VAE_DECODE || t->op == VOXCPM_OP_AUDIO_VAE_ENCODE ||
+                        (t->flags & GGML_TENSOR_FLAG_INPUT);
         if (!io || t->buffer) continue;
         auto buf = std::make_unique<std::vector<uint8_t>>(ggml_nbytes(t));
         t->data = buf->data();
@@ -218,6 +229,16 @@ void VoxCPMBackend::alloc_graph(ggml_cgraph* graph, const char* stage) {
 ggml_status VoxCPMBackend::compute(ggml_cgraph* graph) {
     for (int i = 0; i < graph->n_nodes; ++i) {
         ggml_tensor* t = graph->nodes[i];
+        if (t->op == VOXCPM_OP_AUDIO_VAE_ENCODE) {
+            const ggml_tensor* a = t->src[0];
+            if (!t->data || !a->data) return GGML_STATUS_ALLOC_FAILED;
+            if (static_cast<int>(t->ne[0]) != enc_plan_t_) reserve_compute_memory(graph);
+            if (vxb_encode(ctx_, static_cast<const float*>(a->data), static_cast<float*>(t->data)) != VXB_OK) {
+                std::fprintf(stderr, "[voxcpm] encode failed: %s\n", vxb_last_error());
+                return GGML_STATUS_FAILED;
+            }
+            continue;
+        }
         if (t->op != VOXCPM_OP_AUDIO_VAE_DECODE) continue;
         const ggml_tensor* z = t->src[0];
         if (!t->data || !z->data) return GGML_STATUS_ALLOC_FAILED;
@@ -401,6 +422,31 @@ ggml_tensor* AudioVAE::decode(VoxCPMContext& ctx, ggml_tensor* z) {
     y->src[0] = z;
     y->extra = this;
     std::snprintf(y->name, sizeof(y->name), "audio_vae.decode");
+    ggml_set_output(y);
+    return y;
+}
+
+std::vector<float> AudioVAE::preprocess(std::vector<float> audio_data, int sample_rate) const {
+    const int sr = sample_rate < 0 ? config_.sample_rate : sample_rate;
+    VOXCPM_ASSERT(sr == config_.sample_rate);
+    const size_t hop = static_cast<size_t>(config_.hop_length());
+    audio_data.resize((audio_data.size() + hop - 1) / hop * hop, 0.0f);
+    return audio_data;
+}
+
+ggml_tensor* AudioVAE::encode(VoxCPMContext& ctx, std::vector<float>& audio_data, int sample_rate) {
+    VOXCPM_ASSERT(derived_ready_ && "call ensure_derived_weights() before encode()");
+    last_preprocessed_audio_ = preprocess(audio_data, sample_rate);
+    const int64_t n = static_cast<int64_t>(last_preprocessed_audio_.size());
+    VOXCPM_ASSERT(n > 0);
+    last_input_tensor_ = ctx.new_tensor_3d(GGML_TYPE_F32, n, 1, 1);
+    ggml_set_input(last_input_tensor_);
+    const int64_t ne[3] = {n / config_.hop_length(), config_.latent_dim, 1};
+    ggml_tensor* y = ctx.new_node(GGML_TYPE_F32, 3, ne);
+    y->op = VOXCPM_OP_AUDIO_VAE_ENCODE;
+    y->src[0] = last_input_tensor_;
+    y->extra = this;
+    std::snprintf(y->name, sizeof(y->name), "audio_vae.encode");
     ggml_set_output(y);
     return y;
 }

@@ -64,6 +64,7 @@ private:
     std::vector<std::unique_ptr<std::vector<uint8_t>>> staging_;  // host buffers of graph tensors
     size_t staging_bytes_ = 0;
     int plan_b_ = 0, plan_t_ = 0;
+    int enc_plan_t_ = 0;  // frames of the encode plan (batch 1)
 };
 
 }  // namespace voxcpm

@@ -52,6 +52,7 @@ enum ggml_tensor_flag {
 enum voxcpm_op {
     VOXCPM_OP_NONE = 0,          // leaf (input or weight)
     VOXCPM_OP_AUDIO_VAE_DECODE,  // src[0] = latent ne=[T, latent_dim(, B)]
+    VOXCPM_OP_AUDIO_VAE_ENCODE,  // src[0] = waveform ne=[hop*T, 1, 1] -> latent ne=[T, latent_dim, 1]
 };
 
 struct ggml_context;

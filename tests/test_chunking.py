@@ -62,3 +62,39 @@ def test_halo_chunks_reproduce_full_decode(small_model):
             assert worst == 0.0, (halo, worst)
         else:
             assert worst > 0.0, halo
+
+
+class _OracleDecoder:
+    """The oracle behind the StreamingDecoder's duck-typed Decoder interface."""
+
+    def __init__(self, m):
+        self.m = m
+        self.hop = m.hop
+
+    def config(self):
+        return {"latent_dim": self.m.latent_dim, "rates": self.m.rates}
+
+    def decode(self, z):
+        return self.m.decode(z, O.MODE_EXACT)
+
+
+def test_streaming_decoder_equals_continuous_decode(small_model):
+    """Stateful streaming (history + new frames, halo >= the receptive field)
+    emits exactly the continuous decode of the whole stream, for any step
+    sizes; a halo below the receptive field is refused."""
+    import vxb
+
+    m, hop = small_model, 640
+    z = S.make_latents(1, 40, latent_dim=m.latent_dim, seed=12, ar=0.9)[0]  # [1, L, 40]
+    full = m.decode(z, O.MODE_EXACT)
+    sd = vxb.StreamingDecoder(_OracleDecoder(m), batch=1)
+    assert sd.halo == CH.min_halo(m.rates)
+    got, t = [], 0
+    for n in (6, 6, 1, 13, 6, 8):
+        got.append(sd.push(z[:, :, t:t + n]))
+        t += n
+    got = np.concatenate(got, axis=1)
+    assert got.shape == (1, 40 * hop)
+    assert np.array_equal(got, full)
+    with pytest.raises(ValueError):
+        vxb.StreamingDecoder(_OracleDecoder(m), batch=1, halo=CH.min_halo(m.rates) - 1)

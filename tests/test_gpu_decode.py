@@ -125,6 +125,23 @@ def test_chunked_decode_equals_full(vxb, quant):
     assert np.abs(got - full).max() <= 1e-5
 
 
+@pytest.mark.parametrize("quant", ["f16", "q4_0"])
+def test_streaming_decoder_equals_continuous_decode(vxb, quant):
+    """Opt-in stateful streaming: two streams pushed 6 frames at a time (then
+    an odd step) emit the continuous decode of each whole stream."""
+    d = decoder_for(vxb, quant=quant, seed=0)
+    z = S.make_latents(1, 45, seed=31, batch=2)[0]  # [2, 64, 45]
+    full = d.decode(z)
+    sd = vxb.StreamingDecoder(d, batch=2)
+    parts, t = [], 0
+    for n in (6,) * 7 + (3,):
+        parts.append(sd.push(z[:, :, t:t + n]))
+        t += n
+    got = np.concatenate(parts, axis=1)
+    assert got.shape == full.shape
+    assert np.abs(got - full).max() <= 1e-5
+
+
 def test_decode_rejects_bad_shapes(vxb):
     d = decoder_for(vxb, quant="f16", seed=0)
     with pytest.raises(vxb.VxbError) as e:

@@ -306,6 +306,56 @@ class Decoder:
         return out
 
 
+class StreamingDecoder:
+    """Opt-in stateful streaming over a Decoder.
+
+    The reference decodes every streaming window on its own, with zero left
+    context (vae_decode_mock.cpp:1337-1347), so consecutive windows do not
+    join up; this mode is NOT output-equivalent to it.  It keeps each
+    stream's last `halo` latent frames and decodes [history + new frames]
+    with the sequence start only at the true start of the stream: the
+    decoder is causal with a left receptive field of
+    chunking.receptive_field_frames(rates) frames (18.49 for VoxCPM), so with
+    halo >= chunking.min_halo(rates) every emitted sample equals the
+    continuous decode of the whole stream so far -- the quality check this
+    mode is tested against.  Each step decodes halo + n frames to emit n
+    (the history is re-decoded, not cached as activations); the window
+    length settles at halo + n once the stream is halo frames old.  Streams
+    of a batch advance together.
+    """
+
+    def __init__(self, decoder: "Decoder", batch: int = 1, halo: int | None = None):
+        import chunking
+
+        self.d = decoder
+        cfg = decoder.config()
+        self.latent_dim = cfg["latent_dim"]
+        need = chunking.min_halo(cfg["rates"])
+        self.halo = need if halo is None else int(halo)
+        if self.halo < need:
+            raise ValueError(f"halo {self.halo} < the decoder's receptive field ({need} frames)")
+        self.batch = batch
+        self.reset()
+
+    def reset(self):
+        """Forgets every stream's history (the next push starts new streams)."""
+        self.history = np.zeros((self.batch, self.latent_dim, 0), np.float32)
+
+    def push(self, z_new: np.ndarray) -> np.ndarray:
+        """New latent frames [batch, latent, n] (or [latent, n] for one stream)
+        -> their waveform [batch, n * hop]."""
+        z_new = np.asarray(z_new, dtype=np.float32)
+        if z_new.ndim == 2:
+            z_new = z_new[None]
+        if z_new.shape[:2] != (self.batch, self.latent_dim) or z_new.shape[2] < 1:
+            raise ValueError(f"expected [{self.batch}, {self.latent_dim}, n >= 1] frames, got {list(z_new.shape)}")
+        win = np.ascontiguousarray(np.concatenate([self.history, z_new], axis=2))
+        n, hop = z_new.shape[2], self.d.hop
+        y = self.d.decode(win)
+        self.history = win[:, :, -self.halo:].copy()
+        return y[:, -n * hop:].copy()
+
+
 # ---------------------------------------------------------- single kernels --
 
 def q4_0_dequant(blocks, n: int, out, stream=None):

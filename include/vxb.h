@@ -182,7 +182,7 @@ VXB_API int vxb_encoder_hop(const vxb_ctx* ctx);
  * waveforms of T * vxb_encoder_hop samples each.  Replaces the graph build +
  * gallocr reserve of AudioVAE::encode (src/audio-vae.cpp:652-664) for that
  * shape.  VXB_ERR_INVALID_FORMAT if the model's encoder tensors are
- * placeholders; encoder rates must be 2, 3, 5 or 8. */
+ * placeholders or an encoder width is not a multiple of 32. */
 VXB_API int vxb_build_encode_plan(vxb_ctx* ctx, int batch, int T);
 
 /* One encode of the planned shape: audio [batch][T*hop] (16 kHz samples;

@@ -1,5 +1,5 @@
 /*
- * vxb.h -- C ABI of the B200 AudioVAE decoder (libvxb.so).
+ * vxb.h -- C ABI of the B200 AudioVAE decoder and encoder (libvxb.so).
  *
  * This is the drop-in seam for the reference's decode path
  * (nowang6/voxcpm-inference): plain pointers, sizes and int status codes; no

@@ -122,6 +122,15 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def quiet_nccl_stdout():
+    """Rank 0 prints exactly one JSON line on stdout: NCCL writes its log
+    (the version banner included, at every level from VERSION up) to stdout
+    unless told otherwise, so send it to stderr and keep warnings only."""
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -285,9 +294,7 @@ def main():
 
         import torch.distributed as dist
 
-        # rank 0 prints exactly one JSON line on stdout: keep NCCL's version banner off it
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        quiet_nccl_stdout()
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -484,8 +491,7 @@ def main_encode(args):
 
         import torch.distributed as dist
 
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        quiet_nccl_stdout()
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import vxb

@@ -171,6 +171,11 @@ VXB_API int vxb_decode_static(vxb_ctx* ctx, const float* z_dev, float* out_dev, 
  * encoder_dim / encoder_rates (include/voxcpm/config.h:34-133). */
 VXB_API int vxb_set_encoder_config(vxb_ctx* ctx, int encoder_dim, const int* rates, int n_rates);
 
+/* Reads back the encoder config (vxb_set_encoder_config / vxb_load_gguf):
+ * *encoder_dim and up to max_rates downsampling rates, *n_rates = their
+ * count (0 and 0 without an encoder config). */
+VXB_API int vxb_get_encoder_config(const vxb_ctx* ctx, int* encoder_dim, int* rates, int max_rates, int* n_rates);
+
 /* Waveform samples per latent frame: the product of the encoder rates
  * (AudioVAEConfig::hop_length); 0 without an encoder config. */
 VXB_API int vxb_encoder_hop(const vxb_ctx* ctx);

@@ -98,3 +98,44 @@ def test_streaming_decoder_equals_continuous_decode(small_model):
     assert np.array_equal(got, full)
     with pytest.raises(ValueError):
         vxb.StreamingDecoder(_OracleDecoder(m), batch=1, halo=CH.min_halo(m.rates) - 1)
+
+
+def test_encoder_receptive_field_voxcpm():
+    """6 + sum_b r_b (78 + 2 ceil(s_b/2)) + 2 * 640 = 9274 samples = 14.49 frames for rates 2,5,8,8."""
+    assert abs(CH.encoder_receptive_field_frames((2, 5, 8, 8)) - 9274 / 640) < 1e-12
+    assert CH.min_encoder_halo((2, 5, 8, 8)) == 15
+
+
+class _OracleEncoder:
+    """The oracle behind the Decoder methods encode_chunked uses."""
+
+    def __init__(self, m, rates):
+        self.m, self.rates = m, rates
+        self.encoder_hop = int(np.prod(rates))
+
+    def encoder_config(self):
+        return {"encoder_dim": 0, "rates": list(self.rates)}
+
+    def encode(self, audio):
+        return self.m.encode(audio, O.MODE_EXACT)
+
+
+def test_chunked_encode_equals_full_encode():
+    """A waveform encoded in windows with the minimal halo (15 frames) equals
+    the one-shot encode; a 14-frame halo does not."""
+    import vxb
+
+    rates = (2, 5, 8, 8)
+    path, _ = model_path(quant="f16", seed=4, decoder_dim=128, encoder=True, encoder_dim=32)
+    m = O.OracleModel(path)
+    try:
+        a = S.make_audio(29 * 640 - 77, 1, seed=17)[0]
+        full = m.encode(a[None], O.MODE_EXACT)[0]
+        enc = _OracleEncoder(m, rates)
+        got = vxb.Decoder.encode_chunked(enc, a, chunk=10)
+        assert got.shape == full.shape == (64, 29)
+        assert np.array_equal(got, full)
+        short = vxb.Decoder.encode_chunked(enc, a, chunk=10, halo=14)
+        assert not np.array_equal(short, full)
+    finally:
+        m.close()

@@ -125,3 +125,15 @@ def test_encode_placeholder_encoder_is_an_error(vxb):
         assert e.value.code == vxb.ERR_INVALID_FORMAT
     finally:
         d.close()
+
+
+def test_chunked_encode_equals_full(vxb):
+    """A long waveform encoded in 8-frame windows with the minimal halo (15
+    frames for rates 2,5,8,8) equals the one-shot encode."""
+    d, _ = encoder_for(vxb, "f16")
+    assert d.encoder_config() == {"encoder_dim": 128, "rates": [2, 5, 8, 8]}
+    a = S.make_audio(40 * 640 - 123, 1, seed=27)[0]
+    full = d.encode(a[None])[0]
+    got = d.encode_chunked(a, chunk=8)
+    assert got.shape == full.shape
+    assert np.abs(got - full).max() <= 1e-5 * np.abs(full).max()

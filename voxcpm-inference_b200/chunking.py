@@ -51,6 +51,29 @@ def min_halo(rates=(8, 8, 5, 2)) -> int:
     return math.ceil(receptive_field_frames(rates))
 
 
+def encoder_receptive_field_frames(rates=(2, 5, 8, 8), kernel: int = KERNEL, dilations=DILATIONS) -> float:
+    """Left reach of one latent frame of the encoder (in latent frames): the
+    encoder is causal as well (reference encode_tensor / encoder_block_forward,
+    src/audio-vae.cpp:553-570, 640-650: every conv pads on the left only),
+    so a waveform window that starts this far before the frames it keeps
+    reproduces them.  In samples: the head conv reads 6 back; block b at r_b
+    samples per position (r_1 = 1) adds its three dilated residual units
+    (6 * (1+3+9) positions) and its strided conv's left pad (2 * ceil(s/2)
+    positions); fc_mu reads 2 frames back."""
+    reach = kernel - 1
+    r = 1
+    for s in rates:
+        reach += r * ((kernel - 1) * sum(dilations) + 2 * ((s + 1) // 2))
+        r *= s
+    reach += 2 * r
+    return reach / r
+
+
+def min_encoder_halo(rates=(2, 5, 8, 8)) -> int:
+    """Smallest whole number of halo frames that makes an encoder chunk exact."""
+    return math.ceil(encoder_receptive_field_frames(rates))
+
+
 @dataclass(frozen=True)
 class Chunk:
     start: int  # first latent frame decoded (window start, includes the halo)

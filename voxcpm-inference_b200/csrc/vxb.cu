@@ -888,6 +888,15 @@ int vxb_set_encoder_config(vxb_ctx* c, int encoder_dim, const int* rates, int n_
     return VXB_OK;
 }
 
+int vxb_get_encoder_config(const vxb_ctx* c, int* encoder_dim, int* rates, int max_rates, int* n_rates) {
+    if (!c || !encoder_dim || !n_rates || max_rates < 0 || (max_rates > 0 && !rates))
+        return fail(VXB_ERR_INVALID_ARGUMENT, "vxb_get_encoder_config: null argument");
+    *encoder_dim = c->encoder_dim;
+    *n_rates = static_cast<int>(c->enc_rates.size());
+    for (int i = 0; i < max_rates && i < *n_rates; ++i) rates[i] = c->enc_rates[i];
+    return VXB_OK;
+}
+
 int vxb_encoder_hop(const vxb_ctx* c) {
     if (!c || c->enc_rates.empty()) return 0;
     int h = 1;

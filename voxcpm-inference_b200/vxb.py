@@ -58,6 +58,7 @@ SIGNATURES = {
     "vxb_residual_unit": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "vxb_set_encoder_config": (_i, [_vp, _i, ctypes.POINTER(_i), _i]),
     "vxb_encoder_hop": (_i, [_vp]),
+    "vxb_get_encoder_config": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, ctypes.POINTER(_i)]),
     "vxb_build_encode_plan": (_i, [_vp, _i, _i]),
     "vxb_encode": (_i, [_vp, _vp, _vp]),
     "vxb_encode_device": (_i, [_vp, _vp, _vp, _vp]),
@@ -252,6 +253,13 @@ class Decoder:
     def encoder_hop(self) -> int:
         return lib().vxb_encoder_hop(self.h)
 
+    def encoder_config(self) -> dict:
+        """{encoder_dim, rates} of the loaded encoder (0 and [] without one)."""
+        dim, n = ctypes.c_int(), ctypes.c_int()
+        rates = (ctypes.c_int * 8)()
+        check(lib().vxb_get_encoder_config(self.h, ctypes.byref(dim), rates, 8, ctypes.byref(n)))
+        return {"encoder_dim": dim.value, "rates": list(rates[: n.value])}
+
     def build_encode_plan(self, batch: int, T: int):
         check(lib().vxb_build_encode_plan(self.h, batch, T))
         self.eB, self.eT = batch, T
@@ -275,6 +283,39 @@ class Decoder:
         if out is None:
             out = np.empty((B, self.config()["latent_dim"], T), np.float32)
         check(lib().vxb_encode(self.h, ptr(audio), ptr(out)))
+        return out
+
+    def encode_chunked(self, audio: np.ndarray, chunk: int, halo: int | None = None) -> np.ndarray:
+        """One waveform [n] (or [1, n]) -> latent [latent, T], encoded in windows
+        of at most chunk + halo frames (activation memory bounded by the window,
+        not the waveform).  Equal to encode(): the encoder is causal, every window
+        starts `halo` frames (>= chunking.min_encoder_halo(rates), 15 for
+        VoxCPM) before the frames it keeps, and is zero-padded at its end to one
+        plan size, which never reaches a kept frame."""
+        import chunking
+
+        a = np.asarray(audio, dtype=np.float32)
+        if a.ndim == 2:
+            if a.shape[0] != 1:
+                raise ValueError("encode_chunked encodes one waveform")
+            a = a[0]
+        hop = self.encoder_hop
+        if hop <= 0:
+            raise VxbError(ERR_NOT_READY, "no encoder config")
+        T = (a.size + hop - 1) // hop
+        a = np.concatenate([a, np.zeros(T * hop - a.size, np.float32)])
+        if halo is None:
+            halo = chunking.min_encoder_halo(self.encoder_config()["rates"])
+        W = min(T, chunk + halo)
+        win = np.zeros((1, W * hop), np.float32)
+        out = None
+        for c in chunking.chunks_of(T, chunk, halo):
+            win[0, : c.frames * hop] = a[c.start * hop:c.end * hop]
+            win[0, c.frames * hop:] = 0.0
+            z = self.encode(win)[0]
+            if out is None:
+                out = np.empty((z.shape[0], T), np.float32)
+            out[:, c.keep:c.end] = z[:, c.halo:c.halo + c.end - c.keep]
         return out
 
     def encode_host_ptrs(self, audio_ptr: int, latent_ptr: int):

@@ -111,3 +111,54 @@ def test_two_gloo_ranks_time_chunks_reproduce_one_utterance():
     got = np.concatenate([k for _, _, k in parts])
     assert parts[1][1] == 25 and got.size == full.size
     assert np.array_equal(got, full)
+
+
+def _enc_chunk_worker(rank, world, port, model, T, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+    import bench
+    import chunking
+    import oracle_lib as O
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ws, r, _ = bench.dist_env()
+    halo = chunking.min_encoder_halo((2, 5, 8, 8))
+    w = chunking.split(T, ws, halo)[r]
+    a = bench.S.make_audio(T * 640, 1, seed=2000)  # the waveform every rank shares
+    m = O.OracleModel(model)
+    z = m.encode(a[:, w.start * 640:w.end * 640], O.MODE_EXACT)[0]
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((r, w.keep, z[:, w.halo:]))
+
+
+@pytest.mark.timeout(300)
+def test_two_gloo_ranks_encode_time_chunks_of_one_waveform():
+    """The encoder over ranks: each rank encodes its time window (15-frame
+    halo) of one shared waveform with no exchange; the kept latent frames,
+    placed side by side, equal the one-shot encode (oracle, narrow encoder, CPU)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "voxcpm-inference_b200"))
+    import oracle_lib as O
+    import vxb_synth as S
+    from models import model_path
+
+    model, _ = model_path(quant="f16", seed=4, decoder_dim=128, encoder=True, encoder_dim=32)
+    T = 40
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + ((os.getpid() + 13) % 1000)
+    procs = [ctx.Process(target=_enc_chunk_worker, args=(r, 2, port, model, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    parts = sorted(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    a = S.make_audio(T * 640, 1, seed=2000)
+    full = O.OracleModel(model).encode(a, O.MODE_EXACT)[0]
+    got = np.concatenate([k for _, _, k in parts], axis=1)
+    assert parts[1][1] == 20 and got.shape == full.shape
+    assert np.array_equal(got, full)

@@ -49,6 +49,9 @@ ENCODE_CASES = {
     "f32_t2": (dict(quant="f32", seed=0, encoder=True), dict(n=2 * 640 - 37, batch=2, seed=11)),
     "f16_t6": (dict(quant="f16", seed=0, encoder=True), dict(n=6 * 640, batch=2, seed=7)),
     "q4_t6": (dict(quant="q4_0", seed=0, encoder=True), dict(n=6 * 640, batch=2, seed=7)),
+    # non-default config: width 64, encoder rates 3,2,5,4 (hop 120; strided-conv kernels 6, 4, 10, 8)
+    "q4_small_rates": (dict(quant="q4_0", seed=5, decoder_dim=512, rates=(4, 5, 2, 3), encoder=True, encoder_dim=64),
+                       dict(n=9 * 120 - 31, batch=2, seed=19)),
 }
 
 
@@ -176,7 +179,7 @@ def encode_fixture(L, name, mk, ak):
     sha = hashlib.sha256(data).hexdigest()
     audio = S.make_audio(**ak)
     B, n = audio.shape
-    hop = 640
+    hop = int(np.prod(mk.get("rates", S.DEFAULT_RATES)))
     T = (n + hop - 1) // hop
     lat = np.zeros((B, 64, T), np.float32)
     with tempfile.TemporaryDirectory() as td:

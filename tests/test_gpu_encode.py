@@ -42,27 +42,30 @@ def vxb():
 _ctx = {}
 
 
-def encoder_for(vxb, quant):
-    if quant not in _ctx:
-        path, _ = model_path(quant=quant, seed=0, encoder=True)
+def encoder_for(vxb, q, **mk):
+    """(Decoder, OracleModel) of the seed-0 encoder model of quant `q`, or of model kwargs mk."""
+    mk = mk or dict(quant=q, seed=0, encoder=True)
+    key = repr(sorted(mk.items()))
+    if key not in _ctx:
+        path, _ = model_path(**mk)
         d = vxb.Decoder(0)
         d.load_gguf(path)
         d.prepare()
-        _ctx[quant] = (d, O.OracleModel(path))
-    return _ctx[quant]
+        _ctx[key] = (d, O.OracleModel(path))
+    return _ctx[key]
 
 
 def rel_err(got, ref):
     return float(np.abs(got - ref).max() / np.abs(ref).max())
 
 
-@pytest.mark.parametrize("name", ["f16_t6", "q4_t6"])
+@pytest.mark.parametrize("name", ["f16_t6", "q4_t6", "q4_small_rates"])
 def test_encode_matches_reference(vxb, name):
     f = np.load(os.path.join(G, f"encode_{name}.npz"))
     mk = ast.literal_eval(str(f["model"]))
     _, sha = model_path(**mk)
     assert sha == str(f["sha"])
-    d, m = encoder_for(vxb, mk["quant"])
+    d, m = encoder_for(vxb, mk["quant"], **mk)
     got = d.encode(f["audio"])
     assert got.shape == f["latent"].shape
     err = rel_err(got, f["latent"])

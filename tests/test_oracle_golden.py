@@ -117,7 +117,7 @@ def test_decode_matches_reference_l1(name):
 ENCODE_TOL = {"f32": 1e-5, "f16": 3e-3, "q4_0": 5e-2}
 
 
-@pytest.mark.parametrize("name", ["f32_t2", "f16_t6", "q4_t6"])
+@pytest.mark.parametrize("name", ["f32_t2", "f16_t6", "q4_t6", "q4_small_rates"])
 def test_encode_matches_reference(name):
     f = load(f"encode_{name}.npz")
     mk = ast.literal_eval(str(f["model"]))

@@ -75,8 +75,18 @@ def test_cpp_load_from_store_rejects_missing_encoder_names(tmp_path):
     assert r.returncode == 3, (r.returncode, r.stderr)
 
 
-def test_cpp_encode_caller_compiles(tmp_path):
-    assert os.path.exists(build_api_encode(str(tmp_path)))
+def test_cpp_encode_caller_compiles_and_fails_loudly_without_gpu(tmp_path):
+    """Without a B200 the backend constructor throws voxcpm::Error (exit 7): no CPU fallback."""
+    import torch
+
+    exe = build_api_encode(str(tmp_path))
+    if torch.cuda.is_available():
+        return
+    np.zeros((1, 640), np.float32).tofile(tmp_path / "a.f32")
+    path, _ = model_path(quant="f16", seed=0)
+    r = subprocess.run([exe, path, str(tmp_path / "a.f32"), "640", "1", str(tmp_path / "o.f32")],
+                       capture_output=True, text=True)
+    assert r.returncode == 7 and "voxcpm::Error" in r.stderr
 
 
 @pytest.mark.gpu

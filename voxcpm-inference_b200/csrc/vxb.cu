@@ -1256,7 +1256,8 @@ struct PlanSink : OpSink {
 
 // Binds the encoder weights (audio_vae.encoder.*, the names and layouts
 // load_encoder_weights reads, src/audio-vae.cpp:331-363) and derives their
-// fp32 vectors / fp16 conv copies, once per vxb_prepare.
+// fp32 vectors, the fp16 copies of Q4_0 matrices and the strided convs' /
+// fc_mu's weights reordered to [Cout][K][Cin], once per vxb_prepare.
 int bind_encoder(vxb_ctx* c) {
     if (c->enc_bound) return VXB_OK;
     const int E = c->encoder_dim, nb = static_cast<int>(c->enc_rates.size());

@@ -1,21 +1,25 @@
 """Benchmark: AudioVAE decode on B200 (decoded audio-seconds per second).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c1|c3|c4|c5f|c5q|e1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c4|c2|c1|c3|c5f|c5q|e1]
                     [--impl ours|reference]
 
 Workloads (seeded synthetic weights in the reference's GGUF layout and seeded
 latents; the reference's own VoxCPM checkpoints and mock captures are not
 distributed):
-  c2  (default) streaming replay, Q4_0-mixed weights: each step decodes one
-      independent z=[1,64,6]; the last 640 samples (40 ms) are emitted.
+  c4  (default) batched streaming: 256 independent streams per step,
+      z=[256,64,6], Q4_0-mixed weights, split evenly over the ranks (strong
+      scaling); each stream-step emits its last 640 samples (40 ms).  The
+      line also carries the single-stream step latency (z=[1,64,6], one more
+      plan on the same weights, timed the same way) as
+      "stream_step_latency_ms".
+  c2  streaming replay, Q4_0-mixed: each step decodes one independent
+      z=[1,64,6] and emits its last 640 samples.
   c1  the same with F16 weights.
   c3  one 60 s utterance, z=[1,64,1500] (AR(1) 0.9), F16; a step = the decode.
       Over N ranks the utterance is cut into N time chunks, each decoded
       with a 20-frame left halo (the decoder's receptive field is 18.49
       frames, so every kept sample equals the one-shot decode's; strong
       scaling, no exchange).
-  c4  256 independent streams per step, z=[256,64,6], Q4_0-mixed, split
-      evenly over the ranks (strong scaling).
   c5f / c5q  64 utterances z=[64,64,750] (AR(1) 0.9), F16 / Q4_0-mixed, split
       evenly over the ranks (strong scaling).
   e1  the encoder: 16 waveforms of 30 s (seeded partials + noise) -> latents
@@ -25,12 +29,19 @@ A step is one decode of the per-rank batch.  For c2/c1 every rank replays its
 own stream (weak scaling).  Under torchrun each rank drives one GPU; nothing
 crosses GPUs on the data path (the path shards with no exchange).
 
-value = emitted audio seconds / device time of the K timed steps (max over
-ranks), CUDA events on the launching stream, L2 flushed (256 MiB memset)
-before every step and excluded from the timed events.  e2e = the same metric
-through vxb_decode() with pinned host buffers: host->device copy of the
-latent, decode, device->host copy of the waveform, per step (host clock,
-the call is blocking).
+value = decoded (emitted) audio seconds of the whole job / device time of the
+K timed steps (max over ranks), CUDA events on the launching stream, L2
+flushed (256 MiB memset) before every step and excluded from the timed
+events.  e2e = the same metric through vxb_decode() with pinned host buffers:
+host->device copy of the latents, decode, device->host copy of the waveforms,
+per step (host clock, the call is blocking).
+
+--impl reference times the reference's own CPU decoder (oracle/_ref, built
+from the reference's sources: HEAD AudioVAE::decode for Q4_0 models, its L1
+graph functions for F16, which HEAD's decode rejects) on all host cores, on
+the same workload, metric and unit: W warm-up and K timed steps, a step being
+one stream-step (streaming workloads) or one bounded window of an utterance
+(offline workloads), rank 0 only.
 """
 from __future__ import annotations
 
@@ -51,6 +62,10 @@ import vxb_synth as S  # noqa: E402
 
 SR = 16000
 HOP = 640
+# One metric string per workload family, printed byte-identically by both arms.
+METRIC_DECODE = "decoded audio-sec/sec"
+METRIC_ENCODE = "encoded audio-sec/sec"
+DEFAULT_WORKLOAD = "c4"
 WORKLOADS = {
     # name: (quant, streams per step (global), T, emitted samples per stream-step, scaling, ar)
     "c2": ("q4_0", 1, 6, 640, "weak", None),
@@ -61,10 +76,10 @@ WORKLOADS = {
     "c5q": ("q4_0", 64, 750, 750 * HOP, "strong", 0.9),
 }
 DESCR = {
-    "c2": "streaming replay z=[1,64,6] per step, Q4_0-mixed (17 decoder matrices Q4_0)",
-    "c1": "streaming replay z=[1,64,6] per step, F16",
+    "c2": "streaming replay z=[1,64,6] per step, Q4_0-mixed (17 decoder matrices Q4_0), 640-sample tail emitted",
+    "c1": "streaming replay z=[1,64,6] per step, F16, 640-sample tail emitted",
     "c3": "long-form z=[1,64,1500] (60 s) AR(1) 0.9, F16",
-    "c4": "batched streaming z=[256,64,6] per step, Q4_0-mixed",
+    "c4": "batched streaming z=[256,64,6] per step, Q4_0-mixed, 640-sample tail per stream emitted",
     "c5f": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, F16",
     "c5q": "offline 64 x z=[64,750] (30 s each) AR(1) 0.9, Q4_0-mixed",
 }
@@ -72,6 +87,9 @@ DESCR = {
 ENCODE_WORKLOADS = {"e1": ("q4_0", 16, 750)}
 DESCR["e1"] = "batched encode 16 x 30 s waveforms (16 kHz) -> z=[16,64,750], Q4_0-mixed encoder"
 FLUSH_BYTES = 256 << 20
+# The reference's CPU decoder on an offline workload: each step decodes one
+# window of this many frames (4 s) of the utterance on its own.
+REF_WINDOW_FRAMES = 100
 
 
 def peaks():
@@ -138,10 +156,7 @@ def dist_env():
     return ws, rank, local
 
 
-def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: float = 20.0):
-    """Times the reference's own CPU decode (oracle/_ref, built from its sources)
-    on all host cores over a bounded sample of the workload.  Returns
-    (seconds per stream-step, steps timed, path label, cores)."""
+def ref_lib():
     import ctypes
 
     so = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
@@ -153,6 +168,34 @@ def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: 
     L.ref_close.argtypes = [ctypes.c_void_p]
     for f in ("ref_decode_l1", "ref_decode_l2"):
         getattr(L, f).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    L.ref_encode.restype = ctypes.c_longlong
+    L.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p,
+                             ctypes.c_longlong]
+    return L
+
+
+def ref_samples(workload: str, n: int):
+    """The reference's CPU samples of a decode workload: n latents [64, frames]
+    (one stream-step each for streaming workloads; one REF_WINDOW_FRAMES
+    window of an utterance for offline ones) and the audio seconds each one
+    accounts for."""
+    quant, _, T, emit, _, ar = WORKLOADS[workload]
+    if emit == HOP:  # streaming: every stream-step is an independent z=[1,64,T]
+        z = S.make_latents(n, T, seed=1000, ar=ar, batch=1)[:, 0]
+        return z, emit / SR
+    Tw = min(T, REF_WINDOW_FRAMES)
+    z = S.make_latents(n, Tw, seed=1000, ar=ar, batch=1)[:, 0]
+    return z, Tw * HOP / SR
+
+
+def reference_run(workload: str, model_path: str, warmup: int, steps: int, budget_s: float | None = None):
+    """Times the reference's own CPU decode (oracle/_ref) on all host cores:
+    `warmup` untimed and up to `steps` timed samples of the workload (stops
+    early after budget_s seconds of timed work when given).  Returns
+    (per-sample seconds list, audio seconds per sample, path label, cores)."""
+    L = ref_lib()
+    if L is None:
+        return None
     cores = os.cpu_count() or 1
     h = L.ref_open(model_path.encode(), cores)
     quant = WORKLOADS[workload][0]
@@ -160,21 +203,23 @@ def reference_time(workload: str, model_path: str, z_all: np.ndarray, budget_s: 
     # reference's L1 graph functions.
     fn, label = (L.ref_decode_l2, "HEAD AudioVAE::decode (L2)") if quant == "q4_0" else \
         (L.ref_decode_l1, "L1 graph functions (HEAD decode aborts on F16)")
+    z_all, audio_s = ref_samples(workload, warmup + steps)
     T = z_all.shape[-1]
     out = np.zeros(T * HOP, np.float32)
-    z0 = np.ascontiguousarray(z_all[0])
-    fn(h, z0.ctypes.data, T, out.ctypes.data)  # warm-up
+    for i in range(warmup):
+        z = np.ascontiguousarray(z_all[steps + i])
+        fn(h, z.ctypes.data, T, out.ctypes.data)
     times = []
     t_start = time.perf_counter()
-    for i in range(z_all.shape[0]):
+    for i in range(steps):
         z = np.ascontiguousarray(z_all[i])
         t0 = time.perf_counter()
         fn(h, z.ctypes.data, T, out.ctypes.data)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
+        if budget_s is not None and time.perf_counter() - t_start > budget_s:
             break
     L.ref_close(h)
-    return statistics.median(times), len(times), label, cores, times
+    return times, audio_s, label, cores, T
 
 
 def roofline(ops, op_ms, hbm, tfl, peak_src, workload):
@@ -225,12 +270,28 @@ def build_inputs(workload: str, rank: int, per_rank: int, steps: int, window=Non
     return z  # [steps, per_rank, 64, T]
 
 
+def workload_config(workload, ws, per_rank, T_full):
+    quant, streams, T, emit, scaling, ar = WORKLOADS[workload]
+    cfg = {"workload": f"{workload}: {DESCR[workload]}", "weights": quant, "batch_per_gpu": per_rank,
+           "global_batch": streams if scaling == "strong" else ws * per_rank, "frames": T_full,
+           "emitted_samples_per_stream_step": emit, "sample_rate": SR,
+           "l2": "flushed before every step (256 MiB memset outside the timed events)",
+           "parallelism": f"dp{ws} (independent streams per GPU, no collective)"}
+    if workload == "c3" and ws > 1:
+        import chunking
+
+        w0 = chunking.split(T_full, ws, C3_HALO)[0]
+        cfg["parallelism"] = f"dp{ws} time chunks of one utterance ({C3_HALO}-frame left halo), no collective"
+        cfg["rank0_window"] = "frames [%d, %d), kept from %d" % (w0.start, w0.end, w0.keep)
+    return cfg
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + sorted(ENCODE_WORKLOADS))
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS) + sorted(ENCODE_WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args()
     if args.workload in ENCODE_WORKLOADS:
@@ -238,49 +299,39 @@ def main():
     ws, rank, local = dist_env()
     quant, streams, T, emit, scaling, ar = WORKLOADS[args.workload]
     per_rank = streams if scaling == "weak" else max(1, streams // ws)
+    K, W = args.steps, max(3, args.warmup)
     window = None
-    if args.workload == "c3":  # time chunks of one utterance
+    if args.workload == "c3" and ws > 1:  # time chunks of one utterance
         import chunking
 
-        per_rank = 1
-        window = chunking.split(T, ws, C3_HALO)[rank] if ws > 1 else None
+        window = chunking.split(T, ws, C3_HALO)[rank]
     audio_per_step = (streams * emit if scaling == "strong" else ws * per_rank * emit) / SR  # whole job
     T_full = T
     if window is not None:
         T = window.frames
-    hbm, tfl, peak_src = peaks()
+    cfg = workload_config(args.workload, ws, per_rank, T_full)
     tmpdir = tempfile.mkdtemp(prefix="vxb_bench_")
     model = os.path.join(tmpdir, f"{quant}.gguf")
-    S.write_model(model, quant=quant, seed=0)
-    cfg = {"workload": f"{args.workload}: {DESCR[args.workload]}", "weights": quant, "batch_per_gpu": per_rank,
-           "frames": T, "emitted_samples_per_stream_step": emit, "sample_rate": SR,
-           "l2": "flushed before every step (256 MiB memset outside the timed events)",
-           "parallelism": f"dp{ws} (independent streams per GPU, no collective)"}
-    cfg["frames"] = T_full
-    if window is not None:
-        cfg["parallelism"] = (f"dp{ws} time chunks of one utterance ({C3_HALO}-frame left halo), no collective")
-        cfg["rank0_window"] = "frames [%d, %d), kept from %d" % (
-            chunking.split(T_full, ws, C3_HALO)[0].start, chunking.split(T_full, ws, C3_HALO)[0].end,
-            chunking.split(T_full, ws, C3_HALO)[0].keep)
 
     if args.impl == "reference":
         if rank != 0:
             return
-        k = min(args.steps, 40)
-        z = build_inputs(args.workload, 0, 1, k)[:, 0]
-        r = reference_time(args.workload, model, z)
+        S.write_model(model, quant=quant, seed=0)
+        r = reference_run(args.workload, model, W, K)
         if r is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/liboracle_ref.so not built"}))
             return
-        sec, n, label, cores, times = r
-        val = (emit / SR) / sec
-        line = {"impl": "reference", "metric": "decoded audio-sec/sec (emitted)", "value": val,
-                "unit": "audio-s/s", "n_gpus": ws, "steps": n, "warmup": 1, "ms_per_step": sec * 1e3,
-                "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "config": cfg,
-                "latency_ms": {"p50": sec * 1e3, "p99": float(np.percentile(times, 99)) * 1e3},
+        times, audio_s, label, cores, Tw = r
+        val = audio_s * len(times) / sum(times)
+        sample = (f"{len(times)} stream-steps z=[1,64,{Tw}] of the workload's streams, one at a time"
+                  if emit == HOP else f"{len(times)} windows of {Tw} frames of the workload's utterances")
+        line = {"impl": "reference", "metric": METRIC_DECODE, "value": val, "unit": "audio-s/s", "n_gpus": ws,
+                "steps": K, "warmup": W, "ms_per_step": statistics.mean(times) * 1e3, "higher_is_better": True,
+                "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                "latency_ms": {"p50": float(np.percentile(times, 50)) * 1e3,
+                               "p99": float(np.percentile(times, 99)) * 1e3},
                 "cpu_baseline": {"value": val, "unit": "audio-s/s", "cores": cores, "kind": "reference",
-                                 "sample": f"{n} stream-steps of one stream, {label}, {cores} threads"},
+                                 "sample": f"{sample}, {label}, {cores} threads"},
                 "e2e": {"value": val, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
@@ -300,12 +351,13 @@ def main():
                                 device_id=torch.device("cuda", local))
     import vxb
 
+    S.write_model(model, quant=quant, seed=0)
+    hbm, tfl, peak_src = peaks()
     d = vxb.Decoder(local)
     d.load_gguf(model)
     d.prepare()
     d.build_plan(per_rank, T, graph=True)
     nops = len(d.ops())
-    K, W = args.steps, max(3, args.warmup)
     z_host = build_inputs(args.workload, rank, per_rank, K + W, window)
     z_dev = torch.from_numpy(z_host).cuda()
     out_dev = torch.empty((per_rank, T * HOP), dtype=torch.float32, device="cuda")
@@ -366,28 +418,56 @@ def main():
 
     # per-op device times (same plan, L2 flushed before each rep) -> roofline
     op_ms = d.time_ops(reps=10, flush=flush, flush_bytes=FLUSH_BYTES)
-    clk = clocks.stop()
     ops = d.ops()
     roof = roofline(ops, op_ms, hbm, tfl, peak_src, args.workload)
 
+    # single-stream step latency (z=[1,64,6], same weights, one more context
+    # and plan, timed the same way) next to a batched streaming workload
+    latency = None
+    if emit == HOP and per_rank > 1:
+        d1 = vxb.Decoder(local)
+        d1.load_gguf(model)
+        d1.prepare()
+        d1.build_plan(1, T, graph=True)
+        z1 = z_dev[:, 0:1].contiguous()
+        o1 = torch.empty((1, T * HOP), dtype=torch.float32, device="cuda")
+        for i in range(W):
+            d1.decode_device(z1[K + i], o1, stream)
+        d1.sync()
+        torch.cuda.synchronize()
+        for i in range(K):
+            flush.fill_(i & 0xFF)
+            ev0[i].record(stream)
+            d1.decode_device(z1[i], o1, stream)
+            ev1[i].record(stream)
+        torch.cuda.synchronize()
+        d1.sync()
+        lat = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+        latency = {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
+                   "workload": f"one stream z=[1,64,{T}], {quant} weights, L2 flushed before every step",
+                   "steps": K}
+        d1.close()
+    clk = clocks.stop()
+
     cpu = None
     if rank == 0 and ws == 1:
-        zc = build_inputs(args.workload, 0, 1, min(K, 40))[:, 0]
-        r = reference_time(args.workload, model, zc)
+        r = reference_run(args.workload, model, 1, min(K, 40), budget_s=20.0)
         if r is not None:
-            sec, n, label, cores, _ = r
-            cpu = {"value": (emit / SR) / sec, "unit": "audio-s/s", "cores": cores, "kind": "reference",
-                   "sample": f"{n} stream-steps of one stream, {label}, {cores} threads"}
+            times, audio_s, label, cores, Tw = r
+            sample = (f"{len(times)} stream-steps z=[1,64,{Tw}], one at a time" if emit == HOP
+                      else f"{len(times)} windows of {Tw} frames of the workload's utterances")
+            cpu = {"value": audio_s * len(times) / sum(times), "unit": "audio-s/s", "cores": cores,
+                   "kind": "reference", "sample": f"{sample}, {label}, {cores} threads"}
 
     if rank == 0:
         line = {
-            "metric": "decoded audio-sec/sec (emitted; streams x 640-sample tail per step)"
-            if WORKLOADS[args.workload][3] == 640 else "decoded audio-sec/sec",
+            "metric": METRIC_DECODE,
             "value": value, "unit": "audio-s/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f16", "data": "synthetic (seeded weights and latents)", "config": cfg,
             "latency_ms": {"p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
                            "e2e_p50": float(np.percentile(e2e_ms, 50))},
+            "stream_step_latency_ms": latency,
             "full_output_audio_s_per_s": value * (T_full * HOP) / emit,
             "e2e": {"value": e2e_value, "unit": "audio-s/s", "clock": "host (blocking call)",
                     "h2d_bytes_per_step": int(z_host[0].nbytes), "d2h_bytes_per_step": int(out_pin.nbytes)},
@@ -405,43 +485,38 @@ def main():
         dist.destroy_process_group()
 
 
-def reference_encode_time(model_path: str, audio: np.ndarray, budget_s: float = 20.0):
-    """Times the reference's own CPU encoder (AudioVAE::encode through
-    oracle/_ref) on all host cores, one waveform at a time, until budget_s.
-    Returns (seconds per waveform, waveforms timed, cores, times)."""
-    import ctypes
+# CPU sample of the encoder: waveforms of this many latent frames (0.24 s each;
+# the reference's encoder runs well below real time on the host cores)
+REF_ENCODE_FRAMES = 6
 
-    so = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
-    if not os.path.exists(so):
+
+def reference_encode_run(model_path: str, warmup: int, steps: int, budget_s: float | None = None):
+    """Times the reference's own CPU encoder (AudioVAE::encode through
+    oracle/_ref) on all host cores, one waveform of REF_ENCODE_FRAMES frames
+    per step: `warmup` untimed, up to `steps` timed.  Returns (per-waveform
+    seconds, cores)."""
+    L = ref_lib()
+    if L is None:
         return None
-    L = ctypes.CDLL(so)
-    L.ref_open.restype = ctypes.c_void_p
-    L.ref_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
-    L.ref_close.argtypes = [ctypes.c_void_p]
-    L.ref_encode.restype = ctypes.c_longlong
-    L.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_longlong]
     cores = os.cpu_count() or 1
     h = L.ref_open(model_path.encode(), cores)
+    audio = S.make_audio(REF_ENCODE_FRAMES * HOP, warmup + steps, seed=3000)
     n = audio.shape[1]
     out = np.zeros(64 * ((n + HOP - 1) // HOP), np.float32)
-    a0 = np.ascontiguousarray(audio[0])
-    L.ref_encode(h, a0.ctypes.data, n, out.ctypes.data, out.size)  # warm-up
+    for i in range(warmup):
+        a = np.ascontiguousarray(audio[steps + i])
+        L.ref_encode(h, a.ctypes.data, n, out.ctypes.data, out.size)
     times = []
     t_start = time.perf_counter()
-    for i in range(audio.shape[0]):
+    for i in range(steps):
         a = np.ascontiguousarray(audio[i])
         t0 = time.perf_counter()
         L.ref_encode(h, a.ctypes.data, n, out.ctypes.data, out.size)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
+        if budget_s is not None and time.perf_counter() - t_start > budget_s:
             break
     L.ref_close(h)
-    return statistics.median(times), len(times), cores, times
-
-
-# CPU sample of the encoder: waveforms of this many latent frames (0.24 s each;
-# the reference's encoder runs well below real time on the host cores)
-REF_ENCODE_FRAMES = 6
+    return times, cores
 
 
 def main_encode(args):
@@ -453,37 +528,39 @@ def main_encode(args):
     ws, rank, local = dist_env()
     quant, streams, T = ENCODE_WORKLOADS[args.workload]
     per_rank = max(1, streams // ws)
+    K, W = args.steps, max(3, args.warmup)
     audio_per_step = ws * per_rank * T * HOP / SR
-    hbm, tfl, peak_src = peaks()
     tmpdir = tempfile.mkdtemp(prefix="vxb_bench_")
     model = os.path.join(tmpdir, f"{quant}_enc.gguf")
     S.write_model(model, quant=quant, seed=0, encoder=True)
     cfg = {"workload": f"{args.workload}: {DESCR[args.workload]}", "weights": quant, "batch_per_gpu": per_rank,
-           "frames": T, "samples_per_waveform": T * HOP, "sample_rate": SR,
+           "global_batch": streams, "frames": T, "samples_per_waveform": T * HOP, "sample_rate": SR,
            "l2": "flushed before every step (256 MiB memset outside the timed events)",
            "parallelism": f"dp{ws} (independent waveforms per GPU, no collective)"}
+    ref_sample = lambda n, cores: (f"{n} waveforms of {REF_ENCODE_FRAMES} frames, AudioVAE::encode, "  # noqa: E731
+                                   f"{cores} threads")
     if args.impl == "reference":
         if rank != 0:
             return
-        a = S.make_audio(REF_ENCODE_FRAMES * HOP, min(args.steps, 40), seed=3000)
-        r = reference_encode_time(model, a)
+        r = reference_encode_run(model, W, K)
         if r is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/liboracle_ref.so not built"}))
             return
-        sec, n, cores, times = r
-        val = (REF_ENCODE_FRAMES * HOP / SR) / sec
-        sample = f"{n} waveforms of {REF_ENCODE_FRAMES} frames, AudioVAE::encode, {cores} threads"
-        print(json.dumps({"impl": "reference", "metric": "encoded audio-sec/sec", "value": val, "unit": "audio-s/s",
-                          "n_gpus": ws, "steps": n, "warmup": 1, "ms_per_step": sec * 1e3, "higher_is_better": True,
-                          "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                          "config": cfg, "cpu_baseline": {"value": val, "unit": "audio-s/s", "cores": cores,
-                                                          "kind": "reference", "sample": sample},
+        times, cores = r
+        val = (REF_ENCODE_FRAMES * HOP / SR) * len(times) / sum(times)
+        print(json.dumps({"impl": "reference", "metric": METRIC_ENCODE, "value": val, "unit": "audio-s/s",
+                          "n_gpus": ws, "steps": K, "warmup": W, "ms_per_step": statistics.mean(times) * 1e3,
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic", "config": cfg,
+                          "cpu_baseline": {"value": val, "unit": "audio-s/s", "cores": cores, "kind": "reference",
+                                           "sample": ref_sample(len(times), cores)},
                           "e2e": {"value": val, "unit": "audio-s/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
         return
 
     import torch
 
+    hbm, tfl, peak_src = peaks()
     torch.cuda.set_device(local)
     dist = None
     if ws > 1:
@@ -501,7 +578,6 @@ def main_encode(args):
     d.prepare()
     d.build_encode_plan(per_rank, T)
     nops = len(d.encode_ops())
-    K, W = args.steps, max(3, args.warmup)
     audio_host = S.make_audio(T * HOP, per_rank, seed=2000 + rank)
     a_dev = torch.from_numpy(audio_host).cuda()
     z_dev = torch.empty((per_rank, 64, T), dtype=torch.float32, device="cuda")
@@ -538,7 +614,8 @@ def main_encode(args):
 
     a_pin = torch.from_numpy(audio_host).pin_memory()
     z_pin = torch.empty((per_rank, 64, T), dtype=torch.float32).pin_memory()
-    d.encode_host_ptrs(a_pin.data_ptr(), z_pin.data_ptr())
+    for _ in range(W):
+        d.encode_host_ptrs(a_pin.data_ptr(), z_pin.data_ptr())
     e2e_ms = []
     for i in range(K):
         flush.fill_(i & 0xFF)
@@ -559,15 +636,14 @@ def main_encode(args):
     roof = roofline(ops, op_ms, hbm, tfl, peak_src, args.workload)
     cpu = None
     if rank == 0 and ws == 1:
-        r = reference_encode_time(model, S.make_audio(REF_ENCODE_FRAMES * HOP, 40, seed=3000))
+        r = reference_encode_run(model, 1, 40, budget_s=20.0)
         if r is not None:
-            sec, n, cores, _ = r
-            cpu = {"value": (REF_ENCODE_FRAMES * HOP / SR) / sec, "unit": "audio-s/s", "cores": cores,
-                   "kind": "reference",
-                   "sample": f"{n} waveforms of {REF_ENCODE_FRAMES} frames, AudioVAE::encode, {cores} threads"}
+            times, cores = r
+            cpu = {"value": (REF_ENCODE_FRAMES * HOP / SR) * len(times) / sum(times), "unit": "audio-s/s",
+                   "cores": cores, "kind": "reference", "sample": ref_sample(len(times), cores)}
     if rank == 0:
         print(json.dumps({
-            "metric": "encoded audio-sec/sec", "value": value, "unit": "audio-s/s", "n_gpus": ws, "steps": K,
+            "metric": METRIC_ENCODE, "value": value, "unit": "audio-s/s", "n_gpus": ws, "steps": K,
             "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded weights and waveforms)", "config": cfg,
             "latency_ms": {"p50": float(np.percentile(step_ms, 50)), "e2e_p50": float(np.percentile(e2e_ms, 50))},

@@ -135,7 +135,9 @@ def test_chunked_encode_equals_full_encode():
         got = vxb.Decoder.encode_chunked(enc, a, chunk=10)
         assert got.shape == full.shape == (64, 29)
         assert np.array_equal(got, full)
-        short = vxb.Decoder.encode_chunked(enc, a, chunk=10, halo=14)
+        with pytest.raises(ValueError):
+            vxb.Decoder.encode_chunked(enc, a, chunk=10, halo=14)
+        short = vxb.Decoder._encode_windows(enc, a, 10, 14)  # the window loop without the check
         assert not np.array_equal(short, full)
     finally:
         m.close()

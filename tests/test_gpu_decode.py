@@ -165,3 +165,18 @@ def test_missing_tensor_reported(vxb, tmp_path):
         d.load_gguf(str(tmp_path / "absent.gguf"))
     assert e.value.code == vxb.ERR_FILE_NOT_FOUND
     d.close()
+
+
+def test_sample_rate_conditioning_refused(vxb):
+    """A model carrying the reference's optional sample-rate conditioning
+    tensors (src/audio-vae.cpp:389-396) is refused at prepare, not decoded
+    without the conditioning."""
+    path, _ = model_path(quant="f16", seed=0)
+    d = vxb.Decoder(0)
+    d.load_gguf(path)
+    d.upload("audio_vae.decoder.sr_cond_model.2.scale_embed.weight", vxb.TYPE_F32, [4, 768],
+             np.zeros(4 * 768, np.float32).tobytes())
+    with pytest.raises(vxb.VxbError) as e:
+        d.prepare()
+    assert e.value.code == vxb.ERR_INVALID_FORMAT
+    d.close()

@@ -13,6 +13,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -989,6 +990,12 @@ extern "C" int vxb_prepare(vxb_ctx* c) {
                                  "audio_vae.encoder.fc_mu.weight", "audio_vae.encoder.fc_mu.bias"};
     for (const char* n : kEnc)
         if (!get(c, n)) return fail(VXB_ERR_MISSING_TENSOR, std::string("missing tensor ") + n);
+    // Sample-rate conditioning (audio_vae.decoder.sr_cond_model.<i>.*, optional
+    // in the reference, src/audio-vae.cpp:389-396) is not implemented: a model
+    // that carries it is refused rather than decoded without it.
+    for (const auto& kv : c->tensors)
+        if (kv.first.rfind("audio_vae.decoder.sr_cond_model.", 0) == 0)
+            return fail(VXB_ERR_INVALID_FORMAT, "sample-rate conditioning tensors are not supported: " + kv.first);
     const std::string p = "audio_vae.decoder.model.";
     const int L = c->latent_dim, D = c->decoder_dim;
     int rc;
@@ -1267,6 +1274,8 @@ int bind_encoder(vxb_ctx* c) {
     if (!w0) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + p + "block.0.weight");
     if (w0->nelem() != int64_t(7) * E)
         return fail(VXB_ERR_INVALID_FORMAT, "the model carries no encoder weights (placeholder encoder tensors)");
+    // the head conv kernel gives each thread a quad of channels, 256 threads per block
+    if (E % 32 || E > 1024) return fail(VXB_ERR_INVALID_FORMAT, "encoder width must be a multiple of 32 and <= 1024");
     int rc;
     if ((rc = derive_taps(c, p + "block.0.weight", E, &c->enc_w0))) return rc;
     if ((rc = derive_vec(c, p + "block.0.bias", E, false, &c->enc_b0))) return rc;
@@ -1963,17 +1972,24 @@ constexpr size_t kStaticActFloats = size_t(61440) * kStaticFrames;  // largest s
 constexpr size_t kStaticBytes = 2 * kStaticActFloats * sizeof(float) + 2 * kStaticActFloats * sizeof(__half) + 256;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticBytes];
 
-// Device address of g_static_scratch per device, looked up once.  In host
+// Device address of g_static_scratch per device, looked up once (with that
+// device current) under a per-device once_flag, so host threads that make
+// their first call on one device at the same time do not race.  In host
 // code the symbol is only a host-side stand-in, never a device pointer.
 uint8_t* g_static_ptr[64] = {};
+cudaError_t g_static_err[64] = {};
+std::once_flag g_static_once[64];
 
 int static_scratch(int dev, uint8_t** out) {
     if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
-    if (!g_static_ptr[dev]) {
+    std::call_once(g_static_once[dev], [dev] {
         void* p = nullptr;
-        CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));
-        g_static_ptr[dev] = static_cast<uint8_t*>(p);
-    }
+        g_static_err[dev] = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (g_static_err[dev] == cudaSuccess) g_static_ptr[dev] = static_cast<uint8_t*>(p);
+    });
+    if (g_static_err[dev] != cudaSuccess)
+        return fail(VXB_ERR_BACKEND, std::string("cudaGetSymbolAddress(static scratch): ") +
+                                         cudaGetErrorString(g_static_err[dev]));
     *out = g_static_ptr[dev];
     return VXB_OK;
 }

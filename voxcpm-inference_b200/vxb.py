@@ -302,10 +302,19 @@ class Decoder:
         hop = self.encoder_hop
         if hop <= 0:
             raise VxbError(ERR_NOT_READY, "no encoder config")
+        need = chunking.min_encoder_halo(self.encoder_config()["rates"])
+        halo = need if halo is None else int(halo)
+        if halo < need:
+            raise ValueError(f"halo {halo} < the encoder's receptive field ({need} frames)")
+        return Decoder._encode_windows(self, a, chunk, halo)
+
+    def _encode_windows(self, a: np.ndarray, chunk: int, halo: int) -> np.ndarray:
+        """encode_chunked's window loop, without the halo check."""
+        import chunking
+
+        hop = self.encoder_hop
         T = (a.size + hop - 1) // hop
         a = np.concatenate([a, np.zeros(T * hop - a.size, np.float32)])
-        if halo is None:
-            halo = chunking.min_encoder_halo(self.encoder_config()["rates"])
         W = min(T, chunk + halo)
         win = np.zeros((1, W * hop), np.float32)
         out = None

@@ -10,7 +10,10 @@ reference's own code (oracle/_ref/liboracle_ref.so): ggml's fp16 and Q4_0
 conversions, HEAD's fused Snake callback, ggml mul_mat, whole decodes
 through the reference's L1 graph functions and (for Q4_0 models) through
 HEAD's AudioVAE::decode, and whole encodes through AudioVAE::encode
-(``python tests/golden/make_golden.py encode_f16_t6`` regenerates one case).  Models are not stored: they are regenerated
+(``python tests/golden/make_golden.py encode_f16_t6`` regenerates one case), and
+the "big_decode_*" fixtures at the benchmark configurations' shapes (a 60 s
+utterance, two 30 s utterances of the offline batch, 8 streams of a
+256-stream streaming step).  Models are not stored: they are regenerated
 bit-identically from their seeds by vxb_synth.make_model, and each fixture
 records the sha256 of the model bytes it was made from.
 """
@@ -41,6 +44,21 @@ DECODE_CASES = {
                        dict(steps=2, T=8, seed=6), True),
     "f16_small_t3": (dict(quant="f16", seed=7, decoder_dim=256, rates=(2, 2, 2, 2)),
                      dict(steps=3, T=3, seed=8), False),
+}
+
+
+# Decode fixtures at the benchmark configurations' own shapes ("big_decode_*"):
+# name -> (model kwargs, latent kwargs, run L2 too, stream indices kept).
+# The latents of a batched case are the whole batch (regenerated from the
+# seed); `keep` names the streams whose reference outputs are stored.
+BIG_DECODE_CASES = {
+    # 60 s utterance, F16 (z=[1,64,1500], AR(1) 0.9)
+    "f16_c3_t1500": (dict(quant="f16", seed=0), dict(steps=1, T=1500, seed=1000, ar=0.9), False, None),
+    # two 30 s utterances of the offline batch, Q4_0-mixed (z=[2,64,750], AR(1) 0.9)
+    "q4_c5_t750x2": (dict(quant="q4_0", seed=0), dict(steps=1, T=750, seed=1000, ar=0.9, batch=2), True, None),
+    # 8 of the 256 streams of one batched streaming step, Q4_0-mixed (z=[256,64,6])
+    "q4_c4_b256": (dict(quant="q4_0", seed=0), dict(steps=1, T=6, seed=1000, batch=256), True,
+                   (0, 1, 37, 100, 128, 191, 254, 255)),
 }
 
 
@@ -173,6 +191,39 @@ def decode_fixture(L, name, mk, lk, do_l2):
           ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
 
 
+def big_decode_fixture(L, name, mk, lk, do_l2, keep):
+    """Reference L1 (and HEAD-L2 for Q4_0) outputs of the kept streams of a
+    benchmark-shaped batch.  L2 is stored as its difference from L1 in fp16
+    (differences of order 1e-3, stored to ~1e-6), keeping the fixture small."""
+    data = S.make_model(**mk)
+    sha = hashlib.sha256(data).hexdigest()
+    z = S.make_latents(**lk)[0]  # [batch, 64, T]
+    keep = list(range(z.shape[0])) if keep is None else list(keep)
+    T = lk["T"]
+    hop = int(np.prod(mk.get("rates", S.DEFAULT_RATES)))
+    l1 = np.zeros((len(keep), hop * T), np.float32)
+    l2 = np.zeros_like(l1)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "m.gguf")
+        with open(path, "wb") as f:
+            f.write(data)
+        h = L.ref_open(path.encode(), os.cpu_count() or 4)
+        assert h, "reference failed to open the model"
+        for i, b in enumerate(keep):
+            zs = np.ascontiguousarray(z[b])
+            assert L.ref_decode_l1(h, P(zs), T, P(l1[i])) == hop * T
+            if do_l2:
+                assert L.ref_decode_l2(h, P(zs), T, P(l2[i])) == hop * T
+        L.ref_close(h)
+    arrs = dict(keep=np.array(keep), z=z[keep], l1=l1, sha=np.array(sha), model=np.array(repr(mk)),
+                latents=np.array(repr(lk)))
+    if do_l2:
+        arrs["l2_minus_l1"] = (l2 - l1).astype(np.float16)
+    np.savez_compressed(os.path.join(HERE, f"big_decode_{name}.npz"), **arrs)
+    print("big", name, sha[:12], "max|y| %.3f" % np.abs(l1).max(),
+          ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
+
+
 def encode_fixture(L, name, mk, ak):
     """The reference's own AudioVAE::encode on each waveform of a seeded batch."""
     data = S.make_model(**mk)
@@ -208,6 +259,9 @@ def main():
     for name, (mk, lk, do_l2) in DECODE_CASES.items():
         if not only or name in only:
             decode_fixture(L, name, mk, lk, do_l2)
+    for name, (mk, lk, do_l2, keep) in BIG_DECODE_CASES.items():
+        if not only or "big_decode_" + name in only:
+            big_decode_fixture(L, name, mk, lk, do_l2, keep)
     for name, (mk, ak) in ENCODE_CASES.items():
         if not only or "encode_" + name in only:
             encode_fixture(L, name, mk, ak)

@@ -104,6 +104,20 @@ def test_decode_matches_reference_l1(name):
         assert np.abs(got - f["l2"]).max() <= 1e-2
 
 
+def test_decode_batched_streaming_sample_matches_reference_l1():
+    """The oracle on 8 streams of a 256-stream batched streaming step (the
+    benchmark-shaped fixture; the longer ones are checked on the GPU only)."""
+    f = load("big_decode_q4_c4_b256.npz")
+    mk = ast.literal_eval(str(f["model"]))
+    path, sha = model_path(**mk)
+    assert sha == str(f["sha"]), "seeded model generator drifted from the fixture"
+    lk = ast.literal_eval(str(f["latents"]))
+    assert np.array_equal(S.make_latents(**lk)[0][f["keep"]], f["z"]), "latent generator drifted"
+    got = O.OracleModel(path).decode(f["z"][:4], O.MODE_REF)
+    err = np.abs(got - f["l1"][:4]).max()
+    assert err <= 2e-3, f"oracle vs reference L1: max|d| {err:.3e}"
+
+
 # Encoder: the oracle's restatement against the reference's own
 # AudioVAE::encode.  With F32 weights nothing is rounded to fp16 and only
 # the fp32 summation order differs (the restatement of every layer is pinned

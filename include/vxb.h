@@ -85,8 +85,22 @@ VXB_API int vxb_load_gguf(vxb_ctx* ctx, const char* path);
  * AudioVAE::ensure_derived_weights (src/audio-vae.cpp:365-419, :839-1003);
  * a missing tensor gives VXB_ERR_MISSING_TENSOR, as load_from_store returns
  * false.  Unlike the reference (which asserts Q4_0 convT weights at :739),
- * F16 (2-D folded or 3-D) and Q4_0 are both accepted. */
+ * F16 (2-D folded or 3-D) and Q4_0 are both accepted.
+ * Q4_0 conv weights stay Q4_0: besides the uploaded blocks, prepare lays the
+ * same nibbles and scales out once as 16-byte aligned rows (the same 4.5
+ * bits per value; +15.1 MB of HBM for the VoxCPM decoder), which the plan's
+ * GEMMs load by TMA and dequantise to fp16 in shared memory inside their
+ * mainloop; the fused residual-unit kernels dequantise the uploaded blocks
+ * once per CTA.  With vxb_set_q4_fp16_cache(ctx, 1) prepare instead makes an
+ * fp16 copy of each Q4_0 conv weight (+53.7 MB for the VoxCPM decoder) that the GEMMs
+ * read directly: the same operand values and results, traded for HBM. */
 VXB_API int vxb_prepare(vxb_ctx* ctx);
+
+/* Opt-in (enable != 0) or out of the fp16 copies of Q4_0 conv weights that
+ * vxb_prepare makes for the decode and encode plans' GEMMs (see vxb_prepare);
+ * takes effect at the next vxb_prepare.  Off by default.  No counterpart in
+ * the reference, whose CPU path dots Q4_0 blocks directly. */
+VXB_API int vxb_set_q4_fp16_cache(vxb_ctx* ctx, int enable);
 
 /* Allocates the activation arena for `batch` independent latents of `T` frames
  * and captures the whole decode as one CUDA graph (use_graph != 0) or keeps

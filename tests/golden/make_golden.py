@@ -48,18 +48,33 @@ DECODE_CASES = {
 
 
 # Decode fixtures at the benchmark configurations' own shapes ("big_decode_*"):
-# name -> (model kwargs, latent kwargs, run L2 too, stream indices kept).
-# The latents of a batched case are the whole batch (regenerated from the
-# seed); `keep` names the streams whose reference outputs are stored.
+# name -> (model kwargs, latent kwargs, run L2 too, stream indices kept,
+# exact-arithmetic decode too).  The latents of a batched case are the whole
+# batch (regenerated from the seed); `keep` names the streams whose outputs
+# are stored.  "Exact" is the C oracle's fp32 decode with the same weights
+# and no activation rounding (oracle/vae_oracle.c, pinned to the reference
+# by the other fixtures): it measures how far the reference's Q4_0 path,
+# which quantises every pointwise conv's input to Q8_0 blocks, is from the
+# arithmetic it approximates at this length.
 BIG_DECODE_CASES = {
     # 60 s utterance, F16 (z=[1,64,1500], AR(1) 0.9)
-    "f16_c3_t1500": (dict(quant="f16", seed=0), dict(steps=1, T=1500, seed=1000, ar=0.9), False, None),
+    "f16_c3_t1500": (dict(quant="f16", seed=0), dict(steps=1, T=1500, seed=1000, ar=0.9), False, None, False),
     # two 30 s utterances of the offline batch, Q4_0-mixed (z=[2,64,750], AR(1) 0.9)
-    "q4_c5_t750x2": (dict(quant="q4_0", seed=0), dict(steps=1, T=750, seed=1000, ar=0.9, batch=2), True, None),
+    "q4_c5_t750x2": (dict(quant="q4_0", seed=0), dict(steps=1, T=750, seed=1000, ar=0.9, batch=2), True, None,
+                     True),
     # 8 of the 256 streams of one batched streaming step, Q4_0-mixed (z=[256,64,6])
     "q4_c4_b256": (dict(quant="q4_0", seed=0), dict(steps=1, T=6, seed=1000, batch=256), True,
-                   (0, 1, 37, 100, 128, 191, 254, 255)),
+                   (0, 1, 37, 100, 128, 191, 254, 255), False),
 }
+
+
+def _oracle_exact(args):
+    """One exact-arithmetic oracle decode (run in a spawned worker)."""
+    path, z = args
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+
+    return O.OracleModel(path).decode(z[None], O.MODE_EXACT)[0]
 
 
 # Encode fixtures: name -> (model kwargs, audio kwargs)
@@ -191,7 +206,7 @@ def decode_fixture(L, name, mk, lk, do_l2):
           ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
 
 
-def big_decode_fixture(L, name, mk, lk, do_l2, keep):
+def big_decode_fixture(L, name, mk, lk, do_l2, keep, do_exact):
     """Reference L1 (and HEAD-L2 for Q4_0) outputs of the kept streams of a
     benchmark-shaped batch.  L2 is stored as its difference from L1 in fp16
     (differences of order 1e-3, stored to ~1e-6), keeping the fixture small."""
@@ -215,13 +230,22 @@ def big_decode_fixture(L, name, mk, lk, do_l2, keep):
             if do_l2:
                 assert L.ref_decode_l2(h, P(zs), T, P(l2[i])) == hop * T
         L.ref_close(h)
+        exact = None
+        if do_exact:
+            import multiprocessing as mp
+
+            with mp.get_context("spawn").Pool(len(keep)) as pool:
+                exact = np.stack(pool.map(_oracle_exact, [(path, np.ascontiguousarray(z[b])) for b in keep]))
     arrs = dict(keep=np.array(keep), z=z[keep], l1=l1, sha=np.array(sha), model=np.array(repr(mk)),
                 latents=np.array(repr(lk)))
     if do_l2:
         arrs["l2_minus_l1"] = (l2 - l1).astype(np.float16)
+    if exact is not None:
+        arrs["exact_minus_l1"] = (exact - l1).astype(np.float16)
     np.savez_compressed(os.path.join(HERE, f"big_decode_{name}.npz"), **arrs)
     print("big", name, sha[:12], "max|y| %.3f" % np.abs(l1).max(),
-          ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "")
+          ("L1 vs L2 %.2e" % np.abs(l1 - l2).max()) if do_l2 else "",
+          ("L1 vs exact %.2e" % np.abs(l1 - exact).max()) if exact is not None else "")
 
 
 def encode_fixture(L, name, mk, ak):
@@ -259,9 +283,9 @@ def main():
     for name, (mk, lk, do_l2) in DECODE_CASES.items():
         if not only or name in only:
             decode_fixture(L, name, mk, lk, do_l2)
-    for name, (mk, lk, do_l2, keep) in BIG_DECODE_CASES.items():
+    for name, (mk, lk, do_l2, keep, do_exact) in BIG_DECODE_CASES.items():
         if not only or "big_decode_" + name in only:
-            big_decode_fixture(L, name, mk, lk, do_l2, keep)
+            big_decode_fixture(L, name, mk, lk, do_l2, keep, do_exact)
     for name, (mk, ak) in ENCODE_CASES.items():
         if not only or "encode_" + name in only:
             encode_fixture(L, name, mk, ak)

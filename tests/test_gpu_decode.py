@@ -146,20 +146,34 @@ def test_long_utterance_matches_reference(vxb):
 
 def test_offline_batch_matches_reference(vxb):
     """Two 30 s utterances of the offline workload (z=[2,64,750], AR(1) 0.9,
-    Q4_0-mixed), decoded as one batch, against the reference's exact-Q4_0 L1
-    decode (5e-3).  The reference's HEAD decode re-quantises the transposed
-    convs' weights to Q8_0 and differs from its own L1 by up to 7e-3 here;
-    the GPU must stay within that distance plus 5e-3 of it."""
+    Q4_0-mixed), decoded as one batch.
+
+    The reference's Q4_0 path quantises the input of every pointwise conv to
+    Q8_0 blocks (8-bit, one scale per 32 values); at this length that alone
+    moves its waveform up to 5.6e-3 away from the exact fp32 arithmetic with
+    the same Q4_0 weights (the fixture stores that exact decode, made by the
+    oracle), more than the 5e-3 the reference comparison allows.  So the GPU
+    (fp16 operands) is held to the exact decode at 5e-4, and to the
+    reference at 5e-3 or, where the reference's own distance from the exact
+    decode exceeds that, at that distance plus 5e-4.  The reference's HEAD
+    decode (transposed-conv weights re-quantised to Q8_0 as well) is held the
+    same way."""
     f, mk = big("q4_c5_t750x2")
     d = decoder_for(vxb, **mk)
     got = d.decode(f["z"])
     l1 = f["l1"]
     l2 = l1 + f["l2_minus_l1"].astype(np.float32)
-    err = float(np.abs(got - l1).max())
-    assert err <= 5e-3, f"batch of 2 x 750 frames vs reference L1 max|d| {err:.3e}"
-    err2 = float(np.abs(got - l2).max())
-    assert err2 <= float(np.abs(l2 - l1).max()) + 5e-3, f"vs reference HEAD (L2) max|d| {err2:.3e}"
-    print(f"offline batch 2 x 750: vs L1 {err:.2e}, vs HEAD L2 {err2:.2e}")
+    exact = l1 + f["exact_minus_l1"].astype(np.float32)
+    e_exact = float(np.abs(got - exact).max())
+    assert e_exact <= 5e-4, f"vs exact fp32 arithmetic max|d| {e_exact:.3e}"
+    own_l1 = float(np.abs(l1 - exact).max())
+    e_l1 = float(np.abs(got - l1).max())
+    assert e_l1 <= max(5e-3, own_l1 + 5e-4), f"vs reference L1 max|d| {e_l1:.3e} (L1 vs exact {own_l1:.3e})"
+    own_l2 = float(np.abs(l2 - exact).max())
+    e_l2 = float(np.abs(got - l2).max())
+    assert e_l2 <= max(5e-3, own_l2 + 5e-4), f"vs reference HEAD max|d| {e_l2:.3e} (HEAD vs exact {own_l2:.3e})"
+    print(f"offline batch 2 x 750: vs exact {e_exact:.2e}; vs L1 {e_l1:.2e} (L1 vs exact {own_l1:.2e}); "
+          f"vs HEAD {e_l2:.2e} (HEAD vs exact {own_l2:.2e})")
 
 
 def test_batched_streaming_step_matches_reference(vxb):
@@ -241,3 +255,20 @@ def test_sample_rate_conditioning_refused(vxb):
         d.prepare()
     assert e.value.code == vxb.ERR_INVALID_FORMAT
     d.close()
+
+
+def test_q4_fp16_cache_gives_the_same_decode(vxb):
+    """The opt-in fp16 copies of Q4_0 weights hold the values the GEMMs'
+    in-kernel dequantisation produces, so the decode is bit-identical."""
+    path, _ = model_path(quant="q4_0", seed=0)
+    d = vxb.Decoder(0)
+    d.load_gguf(path)
+    d.prepare()
+    z = S.make_latents(1, 6, seed=41, batch=3)[0]
+    a = d.decode(z)
+    d.set_q4_fp16_cache(True)
+    d.prepare()
+    d.build_plan(3, 6)
+    b = d.decode(z)
+    d.close()
+    assert np.array_equal(a, b)

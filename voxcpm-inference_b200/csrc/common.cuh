@@ -333,6 +333,32 @@ __device__ __forceinline__ uint4 q4_dequant8(uint32_t w0, uint32_t w1, bool hi, 
     return out;
 }
 
+// The nibble order of the GEMMs' split Q4_0 weights: one 32-bit word holds
+// the 8 values v0..v7 of a 16-byte smem chunk with v(i) in nibble slot
+// kQ4Slot[i] (slot n = bits 4n..4n+3), so that masking the word shifted by
+// 4j with 0x000F000F picks the pair (v2j, v2j+1) into the two halves.
+__host__ __device__ constexpr int q4_slot(int i) { return (i & 1) * 4 + (i >> 1); }
+
+// One word of the split layout -> eight fp16 (one 16-byte smem chunk),
+// (q - 8) * d: each pair's nibbles are OR-ed into the fp16 pattern of 1024
+// (0x6400) in one lop3, giving 1024 + q exactly; subtracting 1032 gives
+// q - 8 exactly and one fp16 multiply by d rounds the exact product once --
+// the same value as rounding the fp32 product (q - 8) * d to fp16.
+__device__ __forceinline__ uint4 q4_dequant8_split(uint32_t w, __half2 d2) {
+    const __half2 k1032 = __float2half2_rn(1032.0f);
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t bits;
+        asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(bits) : "r"(w >> (4 * j)), "r"(0x000F000Fu), "r"(0x64006400u));
+        __half2 h = *reinterpret_cast<const __half2*>(&bits);
+        h = __hmul2(__hsub2(h, k1032), d2);
+        o[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return out;
+}
+
 // Snake activation (reference audio-vae.cpp:278-289 / :1443-1479):
 // x + sin(alpha*x)^2 * inv, inv = 1 / (alpha + 1e-9).
 __device__ __forceinline__ float snake(float x, float alpha, float inv) {

@@ -97,9 +97,12 @@ __global__ void im2col_rows_kernel(const __half* __restrict__ g, __half* __restr
     }
 }
 
-// out[(co*K + k)*Cin + ci] = in[(co*Cin + ci)*K + k]: a conv weight's fp16
-// [Cout][Cin][K] -> [Cout][K][Cin] (once, when the encoder is bound).
-__global__ void permute_ck_kernel(const __half* __restrict__ in, __half* __restrict__ out, int Cout, int Cin, int K) {
+// out[(co*K + k)*Cin + ci] = in[(co*Cin + ci)*K + k]: a conv weight's
+// [Cout][Cin][K] -> fp16 [Cout][K][Cin] (once, when the encoder is bound).
+// `in` holds fp16 values, or Q4_0 blocks (in_q4) along that same element
+// order, each value (q - 8) * d rounded once to fp16.
+__global__ void permute_ck_kernel(const void* __restrict__ in, int in_q4, __half* __restrict__ out, int Cout,
+                                  int Cin, int K) {
     const long long total = static_cast<long long>(Cout) * Cin * K;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -107,7 +110,16 @@ __global__ void permute_ck_kernel(const __half* __restrict__ in, __half* __restr
         const long long r = i / Cin;
         const int k = static_cast<int>(r % K);
         const long long co = r / K;
-        out[i] = in[(co * Cin + ci) * K + k];
+        const long long e = (co * Cin + ci) * K + k;
+        if (in_q4) {
+            const uint8_t* blk = static_cast<const uint8_t*>(in) + (e >> 5) * 18;
+            const int j = static_cast<int>(e & 31);
+            const float d = half_bits_to_float(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+            const int q = j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4);
+            out[i] = __float2half_rn(static_cast<float>(q - 8) * d);
+        } else {
+            out[i] = static_cast<const __half*>(in)[e];
+        }
     }
 }
 

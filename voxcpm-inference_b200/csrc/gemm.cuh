@@ -53,7 +53,8 @@ struct GemmArgs {
 };
 
 // Q4_0 weights are staged per k step from their split form (nibbles
-// [rows][blocks][16 B] and fp16 scales [rows][...], see vxb_prepare):
+// [rows][blocks][16 B], each block's 32 values as four words of 8 in the
+// q4_slot order, and fp16 scales [rows][...], made by q4_split_kernel):
 //   K-major (pointwise): 128 rows x 2 blocks -> nibbles 128 x 32 B, scales
 //     128 x 8 (the aligned group of 8 holding the step's 2 scales);
 //   MN-major (transposed conv): 64 k rows x the up to 5 blocks covering a
@@ -99,13 +100,14 @@ struct GemmCfg {
     static constexpr int kAccStride = BN < 32 ? 32 : BN;
     static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
     static_assert((4 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
-    static constexpr int kThreads = Q4 ? 512 : 384;
+    static constexpr int kDqWarps = 4;                           // Q4_0: dequantiser warps (one per SM sub-partition)
+    static constexpr int kThreads = Q4 ? 384 + 32 * kDqWarps : 384;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
     static_assert(kStages >= 2, "pipeline needs two stages");
 };
 
 template <int AK, int BN, int EPI>
-__global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
+__global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, EPI>::kDqWarps : 384, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_res, const __grid_constant__ CUtensorMap tmap_out,
                 const __grid_constant__ CUtensorMap tmap_scale, const GemmArgs args) {
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full_bar[i], 1);
-            mbar_init(&ready_bar[i], 4);
+            mbar_init(&ready_bar[i], Cfg::kDqWarps);
             mbar_init(&empty_bar[i], 1);
             mbar_init(&raw_bar[i], 1);
         }
@@ -302,7 +304,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
         }
     } else if (kQ4 && warp >= 12) {
         // ------------------------------------------- Q4_0 dequantisers ------
-        const int t = threadIdx.x - 384;  // 0..127
+        constexpr int kDqThreads = 32 * Cfg::kDqWarps;
+        const int t = threadIdx.x - 384;  // 0..kDqThreads-1
         int it = 0;
         for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
             const int m0 = (tile % args.m_tiles) * rows_per_tile;
@@ -317,48 +320,46 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 512 : 384, 1)
                 const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
                 const int k0 = kb * Cfg::kBK;
                 if (AK == kAQ4K) {
-                    // thread t -> row m0 + t: the step's two blocks (k0..k0+63),
-                    // nibbles 32 B, scales at positions (2 kb) & 7 of the row's 8
-                    const int m = m0 + t;
-                    const uint4* nib = reinterpret_cast<const uint4*>(raw + t * kQ4KNibBox);
-                    const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + t * kQ4KScaleBox + ((2 * kb) & 7);
+                    // item i -> row m0 + (i & 127), block hb = i >> 7 of the
+                    // step's two (k0..k0+63): nibbles 16 B, the scale at
+                    // position (2 kb + hb) & 7 of the row's 8
 #pragma unroll
-                    for (int hb = 0; hb < 2; ++hb) {
+                    for (int i = t; i < 256; i += kDqThreads) {
+                        const int r = i & 127, hb = i >> 7;
+                        const int m = m0 + r;
                         const bool valid = m < args.M && k0 + hb * 32 < args.K;
-                        const __half2 d2 = __half2half2(valid ? sc[hb] : __float2half_rn(0.f));
-                        const uint4 q = nib[hb];
+                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + r * kQ4KScaleBox;
+                        const __half2 d2 = __half2half2(valid ? sc[(2 * kb + hb) & 7] : __float2half_rn(0.f));
+                        const uint4 q = reinterpret_cast<const uint4*>(raw + r * kQ4KNibBox)[hb];
+                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            // chunk c: elements 8c..8c+7 = low nibbles of bytes 0-7 / 8-15, then high nibbles
-                            *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(t, hb * 32 + c * 8)) =
-                                q4_dequant8((c & 1) ? q.z : q.x, (c & 1) ? q.w : q.y, c >= 2, d2);
-                        }
+                        for (int c = 0; c < 4; ++c)  // word c: elements 8c..8c+7 of the block
+                            *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(r, hb * 32 + c * 8)) =
+                                q4_dequant8_split(qw[c], d2);
                     }
                 } else {
-                    // thread t -> k row kl = t % 64 and blocks h, h + 2, h + 4 (h = t / 64)
-                    // of the up to five that intersect [m0, m0 + 128); m0 is a
+                    // item i -> k row kl = i % 64 and block bi = i / 64 of the
+                    // up to five that intersect [m0, m0 + 128); m0 is a
                     // multiple of 8, so a block lands on four aligned 16-byte
                     // chunks of the MN-major tile
                     const int b_first = m0 >> 5;
                     const int nblk = ((m0 + 127) >> 5) - b_first + 1;
-                    const int kl = t & 63, h = t >> 6;
-                    const __half* sc = reinterpret_cast<const __half*>(raw + kQ4MNScaleOff) + kl * kQ4MNScaleBox + (b_first & 7);
-#pragma unroll
-                    for (int j = 0; j < 3; ++j) {
-                        const int bi = h + 2 * j;
-                        if (bi >= nblk) break;
+#pragma unroll 1
+                    for (int i = t; i < 64 * nblk; i += kDqThreads) {
+                        const int kl = i & 63, bi = i >> 6;
+                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4MNScaleOff) + kl * kQ4MNScaleBox + (b_first & 7);
                         const int blk = b_first + bi;
                         const bool valid = k0 + kl < args.K && blk * 32 < args.M;
                         const __half2 d2 = __half2half2(valid ? sc[bi] : __float2half_rn(0.f));
                         const uint4 q = *reinterpret_cast<const uint4*>(raw + kl * kQ4MNNibBox + bi * 16);
+                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
+                        for (int c = 0; c < 4; ++c) {  // word c: elements 8c..8c+7 of the block
                             const int ml = blk * 32 + c * 8 - m0;
                             if (ml < 0 || ml >= 128) continue;
                             const int hh = ml >> 6, mc = (ml & 63) >> 3;
                             const uint32_t off = hh * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
-                            *reinterpret_cast<uint4*>(a_dst + off) =
-                                q4_dequant8((c & 1) ? q.z : q.x, (c & 1) ? q.w : q.y, c >= 2, d2);
+                            *reinterpret_cast<uint4*>(a_dst + off) = q4_dequant8_split(qw[c], d2);
                         }
                     }
                 }

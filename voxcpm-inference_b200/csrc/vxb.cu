@@ -132,8 +132,8 @@ int num_sms(int dev) {
 }
 
 // A conv weight as a GEMM operand: fp16 bytes, or Q4_0 blocks split into
-// their 16 nibble bytes (p: [rows][blocks][16 B], row pitch `pitch` =
-// 16 * blocks) and their fp16 scales (s: [rows][spitch bytes], spitch a
+// their 16 nibble bytes (p: [rows][pitch bytes], block b at 16 * b, pitch
+// >= 16 * blocks) and their fp16 scales (s: [rows][spitch bytes], spitch a
 // multiple of 16) -- both 16-byte aligned for TMA, the values unchanged.
 struct WView {
     const void* p = nullptr;
@@ -143,22 +143,25 @@ struct WView {
     int spitch = 0;
 };
 
-// Q4_0 rows [rows][nblk x 18 B] -> nibbles [rows][nblk][16 B] + scales
-// [rows][spitch / 2] fp16, one thread per block (the bytes are copied, not
-// re-quantised).
+// Q4_0 rows [rows][nblk x 18 B] -> nibbles [rows][pitch B] (block bi at
+// bi * 16, its values 8w..8w+7 in word w in the q4_slot order) + scales
+// [rows][spitch / 2] fp16, one thread per block (the nibbles and scales are
+// moved, not re-quantised).
 __global__ void q4_split_kernel(const uint8_t* __restrict__ src, int64_t rows, int nblk, uint8_t* __restrict__ q,
-                                uint8_t* __restrict__ sc, int spitch) {
+                                int pitch, uint8_t* __restrict__ sc, int spitch) {
     const int64_t total = rows * nblk;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         const int64_t r = i / nblk;
         const int bi = static_cast<int>(i - r * nblk);
         const uint8_t* blk = src + i * 18;
-        uint32_t w[4];
+        // value e of the block: low nibble of byte e (e < 16), high nibble of byte e - 16
+        uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            w[j] = uint32_t(blk[2 + 4 * j]) | (uint32_t(blk[3 + 4 * j]) << 8) | (uint32_t(blk[4 + 4 * j]) << 16) |
-                   (uint32_t(blk[5 + 4 * j]) << 24);
-        *reinterpret_cast<uint4*>(q + i * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int e = 0; e < 32; ++e) {
+            const uint32_t v = e < 16 ? (blk[2 + e] & 15u) : (blk[2 + e - 16] >> 4);
+            w[e >> 3] |= v << (4 * q4_slot(e & 7));
+        }
+        *reinterpret_cast<uint4*>(q + r * pitch + bi * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         sc[r * spitch + bi * 2] = blk[0];
         sc[r * spitch + bi * 2 + 1] = blk[1];
     }
@@ -194,8 +197,10 @@ struct SplitQ4 {
 int split_q4(const void* w, int64_t inner, int64_t rows, cudaStream_t st, bool async_alloc, SplitQ4* out) {
     if (inner % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 rows must hold whole blocks");
     const int nblk = static_cast<int>(inner / 32);
-    out->pitch = nblk * 16;
-    out->spitch = (nblk * 2 + 15) / 16 * 16;
+    // rows at least as wide as the GEMMs' widest TMA boxes (80 nibble bytes,
+    // 16 scales); the padding is zero and lies past the matrix
+    out->pitch = std::max(nblk * 16, kQ4MNNibBox);
+    out->spitch = std::max((nblk * 2 + 15) / 16 * 16, 2 * kQ4MNScaleBox);
     const size_t qb = size_t(out->pitch) * rows, sb = size_t(out->spitch) * rows;
     if (async_alloc) {
         CUDA_TRY(cudaMallocAsync(&out->q, qb, st));
@@ -205,16 +210,17 @@ int split_q4(const void* w, int64_t inner, int64_t rows, cudaStream_t st, bool a
         CUDA_TRY(cudaMalloc(&out->s, sb));
     }
     CUDA_TRY(cudaMemsetAsync(out->s, 0, sb, st));
+    if (out->pitch != nblk * 16) CUDA_TRY(cudaMemsetAsync(out->q, 0, qb, st));
     const int64_t total = rows * nblk;
     const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
     q4_split_kernel<<<std::max(grid, 1), 256, 0, st>>>(static_cast<const uint8_t*>(w), rows, nblk,
-                                                        static_cast<uint8_t*>(out->q), static_cast<uint8_t*>(out->s),
-                                                        out->spitch);
+                                                        static_cast<uint8_t*>(out->q), out->pitch,
+                                                        static_cast<uint8_t*>(out->s), out->spitch);
     CUDA_TRY(cudaGetLastError());
     return VXB_OK;
 }
 
-// The exact fp16 copy of a Q4_0 weight of `nelem` values (synchronous allocation).
+// The fp16 copy of a Q4_0 weight of `nelem` values (synchronous allocation).
 int q4_make_f16(const void* w, int64_t nelem, cudaStream_t st, void** out) {
     CUDA_TRY(cudaMalloc(out, size_t(nelem) * 2));
     const int64_t nblk = nelem / 32;
@@ -597,17 +603,29 @@ struct DevTensor {
     int64_t ne[4] = {1, 1, 1, 1};
     void* dev = nullptr;     // the GGUF bytes, unchanged
     size_t nbytes = 0;
-    void* f16 = nullptr;     // Q4_0 conv weights: the exact fp16 copy (made by vxb_prepare)
+    SplitQ4 split;           // Q4_0 conv weights: the same blocks as 16-byte nibble rows + fp16 scales (vxb_prepare)
+    void* f16 = nullptr;     // Q4_0 conv weights, opt-in (vxb_set_q4_fp16_cache): the values rounded once to fp16
     int64_t nelem() const { return ne[0] * ne[1] * ne[2] * ne[3]; }
-    // The operand the decode plan's kernels read: a Q4_0 weight's exact fp16
-    // copy (made at prepare; the same values the in-kernel dequantiser
-    // produces, so the same results).  Measured on B200, streaming included
-    // (weights cold in HBM every step), reading 16 bits per value beats
-    // dequantising 4.5 bits per value inside the GEMM, which sits on each
-    // k step's critical path and is repeated for every token tile.
-    WView gemm_view() const { return WView{type == VXB_TYPE_Q4_0 ? f16 : dev, VXB_TYPE_F16, 0, nullptr, 0}; }
-    // Weight bytes one pass over gemm_view() reads.
-    double gemm_bytes() const { return double(nelem()) * 2; }
+    // The operand the plan's GEMMs read: fp16 values, or a Q4_0 weight's
+    // blocks in their split form (16-byte aligned for TMA), dequantised to
+    // fp16 in shared memory inside the GEMM mainloop (or, when the context
+    // keeps fp16 copies of Q4_0 weights, that copy: the same operand values).
+    WView gemm_view() const {
+        if (type == VXB_TYPE_Q4_0 && f16) return WView{f16, VXB_TYPE_F16, 0, nullptr, 0};
+        if (type == VXB_TYPE_Q4_0) return WView{split.q, VXB_TYPE_Q4_0, split.pitch, split.s, split.spitch};
+        return WView{dev, VXB_TYPE_F16, 0, nullptr, 0};
+    }
+    // Weight bytes one pass over gemm_view() reads (4.5 bits per Q4_0 value).
+    double gemm_bytes() const {
+        return type == VXB_TYPE_Q4_0 && !f16 ? double(nelem()) / 32 * 18 : double(nelem()) * 2;
+    }
+    void free_split() {
+        cudaFree(split.q);
+        cudaFree(split.s);
+        cudaFree(f16);
+        split = SplitQ4{};
+        f16 = nullptr;
+    }
 };
 
 struct Vec {  // derived fp32 vector (+ inverse for Snake alphas)
@@ -706,6 +724,7 @@ struct vxb_ctx {
     std::unique_ptr<Plan> enc_plan;
     int* status = nullptr;         // device status word
     int* status_host = nullptr;    // pinned mirror
+    bool q4_fp16_cache = false;    // vxb_set_q4_fp16_cache: plan GEMMs read fp16 copies of Q4_0 weights
 };
 
 namespace {
@@ -774,13 +793,22 @@ int vxb_close(vxb_ctx* c) {
     if (c->enc_plan) free_plan(c->enc_plan.get());
     for (auto& kv : c->tensors) {
         cudaFree(kv.second.dev);
-        cudaFree(kv.second.f16);
+        kv.second.free_split();
     }
     for (void* p : c->derived_allocs) cudaFree(p);
     cudaFree(c->status);
     cudaFreeHost(c->status_host);
     cudaStreamDestroy(c->stream);
     delete c;
+    return VXB_OK;
+}
+
+int vxb_set_q4_fp16_cache(vxb_ctx* c, int enable) {
+    if (!c) return fail(VXB_ERR_INVALID_ARGUMENT, "null ctx");
+    if (c->q4_fp16_cache != (enable != 0)) {
+        c->q4_fp16_cache = enable != 0;
+        c->prepared = false;  // the next vxb_prepare lays the weights out again
+    }
     return VXB_OK;
 }
 
@@ -822,7 +850,7 @@ int vxb_upload_tensor(vxb_ctx* c, const char* name, int type, const int64_t* ne,
     auto it = c->tensors.find(t.name);
     if (it != c->tensors.end()) {
         cudaFree(it->second.dev);
-        cudaFree(it->second.f16);
+        it->second.free_split();
     }
     c->tensors[t.name] = t;
     c->prepared = false;
@@ -949,7 +977,8 @@ int derive_taps(vxb_ctx* c, const std::string& name, int C, float** out) {
 }
 
 // Binds a conv weight used as a GEMM operand ([outer rows][inner]); for Q4_0
-// it also makes the exact fp16 copy that the decode plan's kernels read.
+// it also lays the same blocks out in their split form (nibble rows and
+// scale rows, each 16-byte aligned) for the GEMMs' TMA loads.
 int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t outer, const DevTensor** out) {
     auto it = c->tensors.find(name);
     if (it == c->tensors.end()) return fail(VXB_ERR_MISSING_TENSOR, "missing tensor " + name);
@@ -959,9 +988,12 @@ int check_matrix(vxb_ctx* c, const std::string& name, int64_t inner, int64_t out
     if (t->nelem() != inner * outer) return fail(VXB_ERR_INVALID_FORMAT, "unexpected shape for " + name);
     if (t->type == VXB_TYPE_Q4_0) {
         if (inner % 32) return fail(VXB_ERR_INVALID_FORMAT, name + ": Q4_0 rows must hold whole blocks");
-        cudaFree(t->f16);
-        t->f16 = nullptr;
-        if (int rc = q4_make_f16(t->dev, t->nelem(), c->stream, &t->f16)) return rc;
+        t->free_split();
+        if (c->q4_fp16_cache) {
+            if (int rc = q4_make_f16(t->dev, t->nelem(), c->stream, &t->f16)) return rc;
+        } else if (int rc = split_q4(t->dev, inner, outer, c->stream, false, &t->split)) {
+            return rc;
+        }
     }
     *out = t;
     return VXB_OK;
@@ -1145,7 +1177,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
                 }
-                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status)))
                     return rc;
                 rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
@@ -1188,7 +1220,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
                 }
-                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
+                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status, d.h16)))
                     return rc;
                 rc = sink.kernel([op](cudaStream_t s) { return op.launch(s); },
@@ -1317,7 +1349,7 @@ int bind_encoder(vxb_ctx* c) {
         CUDA_TRY(cudaMalloc(out, sizeof(__half) * size_t(cout) * cin * k));
         c->derived_allocs.push_back(*out);
         permute_ck_kernel<<<grid_1d(int64_t(cout) * cin * k, 256), 256, 0, c->stream>>>(
-            static_cast<const __half*>(t->gemm_view().p), *out, cout, cin, k);
+            t->dev, t->type == VXB_TYPE_Q4_0 ? 1 : 0, *out, cout, cin, k);
         CUDA_TRY(cudaGetLastError());
         return VXB_OK;
     };
@@ -1400,7 +1432,7 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             const bool last = r == 2;
             if (resunit_fits(C)) {
                 ResUnitOp op;
-                if ((rc = setup_resunit(&op, u.pw->gemm_view().p, u.pw->gemm_view().type, C, dl, cur,
+                if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur,
                                         last ? static_cast<void*>(d.g16) : nxt, last ? kResSnakeF16 : kResPlain,
                                         u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, u.pb.v,
                                         last ? b.alpha.v : nullptr, last ? b.alpha.inv : nullptr, B, Lb, sms,

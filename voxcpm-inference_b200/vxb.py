@@ -39,6 +39,7 @@ SIGNATURES = {
     "vxb_upload_tensor": (_i, [_vp, ctypes.c_char_p, _i, ctypes.POINTER(_i64), _i, _vp, _sz]),
     "vxb_load_gguf": (_i, [_vp, ctypes.c_char_p]),
     "vxb_prepare": (_i, [_vp]),
+    "vxb_set_q4_fp16_cache": (_i, [_vp, _i]),
     "vxb_build_plan": (_i, [_vp, _i, _i, _i]),
     "vxb_hop": (_i, [_vp]),
     "vxb_get_config": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i), _i, ctypes.POINTER(_i)]),
@@ -160,6 +161,10 @@ class Decoder:
 
     def prepare(self):
         check(lib().vxb_prepare(self.h))
+
+    def set_q4_fp16_cache(self, enable: bool):
+        """Opt-in fp16 copies of Q4_0 conv weights for the plans' GEMMs (next prepare)."""
+        check(lib().vxb_set_q4_fp16_cache(self.h, 1 if enable else 0))
 
     def build_plan(self, batch: int, T: int, graph: bool = True):
         check(lib().vxb_build_plan(self.h, batch, T, 1 if graph else 0))

@@ -136,6 +136,18 @@ VXB_API int vxb_decode_device(vxb_ctx* ctx, const float* z_dev, float* out_dev, 
  * reported a failed bounded wait. */
 VXB_API int vxb_sync(vxb_ctx* ctx, int timeout_ms);
 
+/* Failure-detection probe: launches one kernel whose thread waits on an
+ * mbarrier that nothing arrives on, through the bounded wait every decode
+ * kernel uses, with the limit shortened to limit_us microseconds
+ * (1..2000000).  The wait gives up, the kernel records a failed wait in the
+ * context's device status word and returns -- no fault, no trap -- so the
+ * next vxb_sync returns VXB_ERR_DEVICE_STATUS and the context stays usable
+ * (the next decode clears the status word).  Enqueued on `stream` (NULL =
+ * the context's stream).  No counterpart in the reference, whose CPU graph
+ * has no device waits; its error convention is voxcpm::Error / ErrorCode
+ * (include/voxcpm/common.h:42-88). */
+VXB_API int vxb_debug_wait_probe(vxb_ctx* ctx, int limit_us, void* stream);
+
 /* Copies the fp32 activation after plan stage `stage` (2+4b: transposed conv
  * of block b; 3+4b, 4+4b: residual units 0 and 1 of block b) of the last
  * decode to host memory [batch*frames][channels]; n = capacity in floats.

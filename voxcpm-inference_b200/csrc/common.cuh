@@ -93,6 +93,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// The same bounded wait with the limit given in nanoseconds (the failure
+// probe waits on a barrier nothing arrives on, with a short limit).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                              int code, unsigned long long limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            *abort = 1;
+            set_status(status, code);
+            return false;
+        }
+    }
+}
+
 // ------------------------------------------------ programmatic launches --
 // Every decode kernel is launched with programmatic stream serialisation:
 // it may start (and run its setup) while the previous kernel finishes, and

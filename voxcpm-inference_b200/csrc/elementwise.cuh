@@ -235,6 +235,20 @@ __global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s,
     if ((lane & 3) == 0 && t < T) y[static_cast<long long>(b) * T + t] = tanhf(sum + bias);
 }
 
+// Failure probe: one thread waits on an mbarrier that nothing ever arrives
+// on, through the same bounded wait every decode kernel uses, with a limit
+// of limit_ns; the wait gives up, records kErrWaitFull in the status word
+// and the kernel returns.  No fault, no trap: the context stays usable.
+__global__ void wait_probe_kernel(int* status, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    mbar_wait_for(&bar, 0, &abort_flag, status, kErrWaitFull, limit_ns);
+}
+
 // y[n][c] = snake(x[n][c]) for an fp32 [N][C] tensor.
 __global__ void snake_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
                              const float* __restrict__ inv, float* __restrict__ y, int C, long long total) {

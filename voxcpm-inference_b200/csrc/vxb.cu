@@ -1755,6 +1755,17 @@ extern "C" int vxb_debug_stage(vxb_ctx* c, int stage, float* host_out, size_t n)
     return check_status(c);
 }
 
+extern "C" int vxb_debug_wait_probe(vxb_ctx* c, int limit_us, void* stream) {
+    if (!c || limit_us < 1 || limit_us > 2000000) return fail(VXB_ERR_INVALID_ARGUMENT, "wait probe: bad limit");
+    DeviceGuard g(c->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), s));
+    wait_probe_kernel<<<1, 32, 0, s>>>(c->status, static_cast<unsigned long long>(limit_us) * 1000ull);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return VXB_OK;
+}
+
 // ------------------------------------------------------ single-kernel APIs --
 
 extern "C" int vxb_q4_0_dequant(const void* blocks, int64_t n, float* out, void* stream) {

@@ -47,6 +47,7 @@ SIGNATURES = {
     "vxb_decode_device": (_i, [_vp, _vp, _vp, _vp]),
     "vxb_sync": (_i, [_vp, _i]),
     "vxb_debug_stage": (_i, [_vp, _i, _vp, _sz]),
+    "vxb_debug_wait_probe": (_i, [_vp, _i, _vp]),
     "vxb_decode_static": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "vxb_plan_num_ops": (_i, [_vp]),
     "vxb_plan_op_info": (_i, [_vp, _i, ctypes.c_char_p, _i, ctypes.c_char_p, _i, ctypes.POINTER(ctypes.c_double),
@@ -231,6 +232,11 @@ class Decoder:
     def decode_static(self, z_dev, out_dev, batch: int, T: int, stream=None):
         """Allocation-free decode (device buffers, static scratch, batch*T <= 8)."""
         check(lib().vxb_decode_static(self.h, ptr(z_dev), ptr(out_dev), batch, T, _stream(stream)))
+
+    def wait_probe(self, limit_us: int, stream=None):
+        """Runs a device wait that nothing satisfies, bounded at limit_us: the
+        next sync() raises VxbError(ERR_DEVICE_STATUS)."""
+        check(lib().vxb_debug_wait_probe(self.h, limit_us, _stream(stream) if stream is not None else None))
 
     def sync(self, timeout_ms: int = 60000):
         check(lib().vxb_sync(self.h, timeout_ms))

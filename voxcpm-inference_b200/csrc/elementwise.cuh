@@ -40,104 +40,104 @@ __global__ void head_kernel(const float* __restrict__ z, const float* __restrict
     }
 }
 
-// Residual-unit prologue.  A block covers CT channels (CT/4 threads x
-// float4) and `tt` (<= kPreTT) time steps of one sequence.  The input rows
-// [t0 - 6d, t0 + tt) are copied into shared memory with 16-byte cp.async
-// (zero-filled before the sequence start: causal padding, snake(0) == 0) and
-// Snake-activated (snake1) in place by the thread that copied them; every
-// output then applies the 7 dilated causal taps, bias and snake2 and is
-// stored as fp16.  CT = 64 when C is a multiple of 64, else 32 (C = 96 keeps
-// every thread busy).  Requires C % 4 == 0.
-constexpr int kPreTT = 128;
-
-__host__ __device__ constexpr size_t res_pre_smem(int d, int tt = kPreTT, int ct = 64) {
-    return sizeof(float) * (tt + 6 * d) * ct;
+// Residual-unit prologue: snake1 -> causal depthwise k7 conv, dilation d
+// (+ bias) -> snake2 -> fp16 [N][C], the B operand of the unit's pointwise
+// GEMM.  Every thread owns one channel pair and a run of `run` outputs (a
+// multiple of 7) of one sequence along one phase of the dilation
+// (t = phase + j*d), and walks it with the 7 inputs its current output needs
+// in a register window: each input row is read (8 bytes, a warp's pairs
+// contiguous) and Snake-activated once, plus 6 warm-up rows per run -- the
+// same overhead at every dilation -- and the next 7 rows are loaded while
+// the current 7 are computed.  Rows before the sequence start are zero
+// (causal padding; snake(0) == 0).  No shared memory.  The arithmetic per
+// output is that of the reference unit (audio-vae.cpp:1481-1518): taps in
+// order from the bias, one fma per tap and lane.  Requires C % 2 == 0.
+__host__ __device__ inline long long res_pre_threads(int C, int T, int B, int d, int run) {
+    const long long J = (T + d - 1) / d;  // outputs per phase (at most)
+    return static_cast<long long>(C / 2) * B * d * ((J + run - 1) / run);
 }
 
-template <int CT>
+// Run length: the longest of 56, 28, 14, 7 outputs that still gives every
+// SM two blocks' worth of threads (short sequences get short runs).
+inline int res_pre_run(int C, int T, int B, int d, int sms) {
+    for (int run = 56; run > 7; run /= 2)
+        if (res_pre_threads(C, T, B, d, run) >= 2LL * 256 * sms) return run;
+    return 7;
+}
+
 __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
                                                       const float* __restrict__ i1,
                                                       const float* __restrict__ w /*[C][7]*/,
                                                       const float* __restrict__ bias,
                                                       const float* __restrict__ a2,
                                                       const float* __restrict__ i2, __half* __restrict__ out,
-                                                      int C, int T, int d, int tt) {
-    constexpr int CG = CT / 4;    // threads across channels
-    constexpr int RG = 256 / CG;  // threads across rows
-    extern __shared__ float4 sh4[];  // [(tt + 6d)][CG]
-    const int cx = threadIdx.x % CG, ry = threadIdx.x / CG;
-    const int c = blockIdx.x * CT + cx * 4;
-    const int t0 = blockIdx.y * tt;
-    const int b = blockIdx.z;
-    const int halo = 6 * d;
-    const int rows = min(tt, T - t0) + halo;
-    const bool cv = c < C;
-    const float* xb = x + static_cast<long long>(b) * T * C;
-    {
-        // the per-channel parameters are not written by earlier kernels: pull
-        // this block's lines into L2 while the previous kernel finishes
-        const int c0 = blockIdx.x * CT, nc = min(CT, C - c0), i = threadIdx.x;
-        if (i < 10) {
-            const float* v = i < 2 ? a1 : i < 4 ? i1 : i < 6 ? bias : i < 8 ? a2 : i2;
-            if ((i & 1) * 32 < nc) prefetch_l2(v + c0 + (i & 1) * 32);
-        } else if (i < 10 + 2 * CT * 7 / 64) {
-            if ((i - 10) * 32 < nc * 7) prefetch_l2(w + c0 * 7 + (i - 10) * 32);
-        }
-    }
+                                                      int C, int T, int B, int d, int run) {
+    const int Q = C >> 1;
+    const int J = (T + d - 1) / d;
+    const int R = (J + run - 1) / run;
+    const long long total = static_cast<long long>(Q) * B * d * R;
+    const long long i = blockIdx.x * 256LL + threadIdx.x;
+    const bool active = i < total;
+    const int q = active ? static_cast<int>(i % Q) : 0;
+    long long r = i / Q;
+    const int jr = static_cast<int>(r % R);
+    r /= R;
+    const int phase = static_cast<int>(r % d);
+    const int b = static_cast<int>(r / d);
+    const int c = 2 * q;
+    // per-channel constants are not written by earlier kernels: loaded
+    // before the grid dependency wait, while the previous kernel finishes
+    float2 wk[7];
+#pragma unroll
+    for (int k = 0; k < 7; ++k) wk[k] = make_float2(w[c * 7 + k], w[(c + 1) * 7 + k]);
+    const float2 al1 = *reinterpret_cast<const float2*>(a1 + c);
+    const float2 iv1 = *reinterpret_cast<const float2*>(i1 + c);
+    const float2 bb = *reinterpret_cast<const float2*>(bias + c);
+    const float2 al2 = *reinterpret_cast<const float2*>(a2 + c);
+    const float2 iv2 = *reinterpret_cast<const float2*>(i2 + c);
     grid_dep_sync();
-    for (int r = ry; r < rows; r += RG) {
-        const int t = t0 - halo + r;
-        const bool ok = cv && t >= 0;
-        cp_async16(&sh4[r * CG + cx], ok ? xb + static_cast<long long>(t) * C + c : xb, ok ? 16u : 0u);
-    }
-    cp_async_wait_all();
-    if (cv) {
-        const float4 al1 = *reinterpret_cast<const float4*>(a1 + c);
-        const float4 iv1 = *reinterpret_cast<const float4*>(i1 + c);
-        for (int r = ry; r < rows; r += RG) sh4[r * CG + cx] = snake4(sh4[r * CG + cx], al1, iv1);
-    }
-    __syncthreads();
-    if (!cv) return;
-    float2 wlo[7], whi[7];
+    if (!active) return;
+    const float* xb = x + static_cast<long long>(b) * T * C + c;
+    __half* ob = out + static_cast<long long>(b) * T * C + c;
+    const int t_first = phase + (jr * run - 6) * d;  // row m of the run is t_first + m*d
+    auto load = [&](int t) {
+        return (t >= 0 && t < T) ? __ldg(reinterpret_cast<const float2*>(xb + static_cast<long long>(t) * C))
+                                 : make_float2(0.f, 0.f);
+    };
+    // window slot of row m is m % 7; rows 0..5 are the warm-up (before the first output)
+    float2 win[7];
 #pragma unroll
-    for (int k = 0; k < 7; ++k) {
-        wlo[k] = make_float2(w[(c + 0) * 7 + k], w[(c + 1) * 7 + k]);
-        whi[k] = make_float2(w[(c + 2) * 7 + k], w[(c + 3) * 7 + k]);
-    }
-    const float4 bb = *reinterpret_cast<const float4*>(bias + c);
-    const float4 al2 = *reinterpret_cast<const float4*>(a2 + c);
-    const float4 iv2 = *reinterpret_cast<const float4*>(i2 + c);
-    __half* ob = out + static_cast<long long>(b) * T * C;
-    for (int q = ry; q < tt; q += RG) {
-        const int t = t0 + q;
-        if (t >= T) break;
-        float2 lo = make_float2(bb.x, bb.y), hi = make_float2(bb.z, bb.w);
+    for (int m = 0; m < 6; ++m) win[m] = load(t_first + m * d);
+    float2 nxt[7];
 #pragma unroll
-        for (int k = 0; k < 7; ++k) {  // taps in order, one fma per tap and lane
-            const float4 u = sh4[(q + k * d) * CG + cx];
-            lo = ffma2(make_float2(u.x, u.y), wlo[k], lo);
-            hi = ffma2(make_float2(u.z, u.w), whi[k], hi);
+    for (int s = 0; s < 7; ++s) nxt[s] = load(t_first + (6 + s) * d);
+#pragma unroll
+    for (int m = 0; m < 6; ++m) win[m] = snake2(win[m], al1, iv1);
+#pragma unroll 1
+    for (int g = 0; g < run; g += 7) {
+        const int tg = t_first + (6 + g) * d;  // the group's first output row
+        if (tg >= T) break;
+        float2 cur[7];
+#pragma unroll
+        for (int s = 0; s < 7; ++s) cur[s] = nxt[s];
+        if (g + 7 < run) {  // the next group's rows, loaded while this one computes
+#pragma unroll
+            for (int s = 0; s < 7; ++s) nxt[s] = load(tg + (7 + s) * d);
         }
-        const float4 y = snake4(make_float4(lo.x, lo.y, hi.x, hi.y), al2, iv2);
-        const __half2 h01 = __floats2half2_rn(y.x, y.y);
-        const __half2 h23 = __floats2half2_rn(y.z, y.w);
-        uint2 pk;
-        pk.x = *reinterpret_cast<const uint32_t*>(&h01);
-        pk.y = *reinterpret_cast<const uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(ob + static_cast<long long>(t) * C + c) = pk;
+#pragma unroll
+        for (int s = 0; s < 7; ++s) {
+            // newest row m = 6 + g + s (slot (6 + s) % 7); tap k reads row m - 6 + k (slot (s + k) % 7)
+            win[(6 + s) % 7] = snake2(cur[s], al1, iv1);
+            float2 acc = bb;
+#pragma unroll
+            for (int k = 0; k < 7; ++k) acc = ffma2(win[(s + k) % 7], wk[k], acc);  // taps in order
+            const int t = tg + s * d;
+            if (t < T) {
+                const float2 y = snake2(acc, al2, iv2);
+                *reinterpret_cast<__half2*>(ob + static_cast<long long>(t) * C) = __floats2half2_rn(y.x, y.y);
+            }
+        }
     }
-}
-
-// Channel tile of res_pre_kernel for C channels.
-inline int res_pre_ct(int C) { return C % 64 == 0 ? 64 : 32; }
-
-// Time tile of res_pre_kernel: the largest of 128/64/32 that still gives at
-// least two blocks per SM.
-inline int res_pre_tt(int C, int T, int B, int sms) {
-    const long long ct = (C + res_pre_ct(C) - 1) / res_pre_ct(C);
-    for (int tt = kPreTT; tt > 32; tt /= 2)
-        if (ct * ((T + tt - 1) / tt) * B >= 2LL * sms) return tt;
-    return 32;
 }
 
 // Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c])

@@ -569,11 +569,12 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
 // Residual-unit prologue over x [B][T][C] -> h fp16, dilation d.
 int launch_res_pre(const float* x, const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
                    const float* i2, __half* h, int C, int B, int T, int d, int sms, cudaStream_t s) {
-    const int tt = res_pre_tt(C, T, B, sms);
-    const int ct = res_pre_ct(C);
-    dim3 grid((C + ct - 1) / ct, (T + tt - 1) / tt, B);
-    const cudaError_t e = launch_pdl(ct == 64 ? res_pre_kernel<64> : res_pre_kernel<32>, grid, dim3(256),
-                                     res_pre_smem(d, tt, ct), s, x, a1, i1, dw, db, a2, i2, h, C, T, d, tt);
+    if (C % 2) return fail(VXB_ERR_INVALID_ARGUMENT, "prologue: C must be even");
+    const int run = res_pre_run(C, T, B, d, sms);
+    const long long threads = res_pre_threads(C, T, B, d, run);
+    if (threads > (1LL << 40)) return fail(VXB_ERR_INVALID_ARGUMENT, "prologue: too many threads");
+    const cudaError_t e = launch_pdl(res_pre_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
+                                     s, x, a1, i1, dw, db, a2, i2, h, C, T, B, d, run);
     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("prologue launch: ") + cudaGetErrorString(e));
 }
 
@@ -1199,7 +1200,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                               sms, s);
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
-                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel<" + std::to_string(res_pre_ct(C)) + ">"});
+                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
                 if (rc) return rc;
             }
             if (resunit_hg_fits(C) && int64_t(B) * ((Tb + kRuTT - 1) / kRuTT) >= sms) {
@@ -1454,7 +1455,7 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                               sms, s);
                     },
                     {"res_pre_" + nm, double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4,
-                     "res_pre_kernel<" + std::to_string(res_pre_ct(C)) + ">"});
+                     "res_pre_kernel"});
                 if (rc) return rc;
             }
             GemmOp op;

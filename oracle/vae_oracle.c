@@ -31,8 +31,8 @@
  *                   input is rounded to fp16 too.
  *   VO_MODE_GPU   : the arithmetic the CUDA kernels use: every tensor-core
  *                   operand rounded to fp16 (activations, and Q4_0 weights
- *                   after exact dequantisation), fp32 accumulation, the final
- *                   conv in fp32.
+ *                   after exact dequantisation), fp32 accumulation; the final
+ *                   conv's input rounded to fp16 as in VO_MODE_REF.
  */
 #include <math.h>
 #include <stdint.h>
@@ -531,7 +531,7 @@ void vo_final(const float* x, const float* w /*[C][7]*/, float bias, int C, int 
                 if (st < 0) continue;
                 const float* xr = x + ((int64_t)bb * T + st) * C;
                 for (int c = 0; c < C; ++c) {
-                    const float v = mode == VO_MODE_REF ? r16(xr[c]) : xr[c];
+                    const float v = mode == VO_MODE_EXACT ? xr[c] : r16(xr[c]);
                     acc += (double)w[c * 7 + k] * v;
                 }
             }

@@ -141,40 +141,49 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
 }
 
 // Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c])
-// over the (already Snake-activated) last stage.  A block covers kFinTT time
-// steps of one sequence: rows [t0 - 6, t0 + kFinTT) are staged in shared
-// memory with 16-byte loads.  Each warp then computes 8 consecutive outputs
+// over the (already Snake-activated) last stage, held in fp16 (the reference
+// rounds this conv's input to fp16 in its im2col + F16 mul_mat,
+// audio-vae.cpp:218-234).  A block covers kFinTT time steps of one
+// sequence: rows [t0 - 6, t0 + kFinTT) are staged in shared memory as fp32
+// from 16-byte loads.  Each warp then computes 8 consecutive outputs
 // at once: lane = channel quad, the 14 rows they read are loaded once, every
 // lane accumulates its channels' share of all 8 sums, and one exchange of
 // halves (xor 16, 8, 4) followed by xor 2, 1 leaves each sum complete on four
-// lanes (9 shuffles for 8 outputs).  Requires C % 4 == 0 and C <= 128.
+// lanes (9 shuffles for 8 outputs).  Requires C % 8 == 0 and C <= 128.
 constexpr int kFinTT = 64;
 
-__global__ void __launch_bounds__(256) final_kernel(const float* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
+__global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
                                                     float bias, float* __restrict__ y, int C, int T) {
     extern __shared__ float4 fsh4[];  // [(kFinTT + 6)][C/4]
     const int c4n = C / 4;
     const int t0 = blockIdx.x * kFinTT;
     const int b = blockIdx.y;
     const int rows = min(kFinTT, T - t0) + 6;
-    const float* sb = s + static_cast<long long>(b) * T * C;
+    const __half* sb = s + static_cast<long long>(b) * T * C;
     if (threadIdx.x * 32 < C * 7) prefetch_l2(w + threadIdx.x * 32);  // taps: constant, into L2 before the wait
     grid_dep_sync();
-    constexpr int kMaxLd = ((kFinTT + 6) * 32 + 255) / 256;  // float4 per thread for C <= 128
-    float4 v[kMaxLd];
+    // 16-byte loads of 8 fp16 channels, widened to two float4 in shared memory
+    const int c8n = C / 8;
+    constexpr int kMaxLd = ((kFinTT + 6) * 16 + 255) / 256;  // 8-channel groups per thread for C <= 128
+    uint4 v[kMaxLd];
 #pragma unroll
     for (int j = 0; j < kMaxLd; ++j) {  // every load issued before any is stored
         const int i = threadIdx.x + j * 256;
-        const int r = i / c4n, cq = i - r * c4n;
+        const int r = i / c8n, cq = i - r * c8n;
         const int t = t0 - 6 + r;
-        v[j] = (i < rows * c4n && t >= 0)
-                   ? __ldg(reinterpret_cast<const float4*>(sb + static_cast<long long>(t) * C) + cq)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[j] = (i < rows * c8n && t >= 0) ? __ldg(reinterpret_cast<const uint4*>(sb + static_cast<long long>(t) * C) + cq)
+                                         : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int j = 0; j < kMaxLd; ++j) {
         const int i = threadIdx.x + j * 256;
-        if (i < rows * c4n) fsh4[i] = v[j];
+        if (i < rows * c8n) {
+            const __half2* h = reinterpret_cast<const __half2*>(&v[j]);
+            const float2 a = __half22float2(h[0]), b2 = __half22float2(h[1]);
+            const float2 c2 = __half22float2(h[2]), d2 = __half22float2(h[3]);
+            fsh4[2 * i] = make_float4(a.x, a.y, b2.x, b2.y);
+            fsh4[2 * i + 1] = make_float4(c2.x, c2.y, d2.x, d2.y);
+        }
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

@@ -1174,9 +1174,13 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     y = d.s16;
                     out_bytes = 2;
                 } else if (r == 2) {
-                    epi = kResSnakeF32;
+                    // the final Snake, fp16 (the final conv's input, rounded as the
+                    // reference's im2col + F16 mul_mat rounds it) into the fp32
+                    // buffer's memory
+                    epi = kResSnakeF16;
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
+                    out_bytes = 2;
                 }
                 if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status)))
@@ -1217,9 +1221,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                     y = d.s16;
                     out_bytes = 2;
                 } else if (r == 2) {
-                    epi = kResSnakeF32;
+                    epi = kResSnakeF16;  // the final Snake, fp16 (the final conv's input)
                     sa = c->final_alpha.v;
                     si = c->final_alpha.inv;
+                    out_bytes = 2;
                 }
                 if ((rc = setup_resunit(&op, u.pw->dev, u.pw->type, C, dl, cur, y, epi, u.a1.v, u.a1.inv, u.dw,
                                         u.db.v, u.a2.v, u.a2.inv, u.pb.v, sa, si, B, Tb, sms, d.status, d.h16)))
@@ -1244,9 +1249,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                      d.s16, d.status);
                 out_bytes = 2;
             } else {
+                // the final Snake, fp16 (the final conv's input)
                 rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, d.h16, n, u.pb.v, cur, c->final_alpha.v,
-                                     c->final_alpha.inv, 0, nxt, d.status);
-                out_bytes = 4;
+                                     c->final_alpha.inv, 1, nxt, d.status);
+                out_bytes = 2;
             }
             if (rc) return rc;
             if ((rc = sink.gemm(op, {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(n),
@@ -1256,8 +1262,8 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             std::swap(cur, nxt);
         }
         if (last_block) {
-            // final conv over snake(x) (held in `cur` after the swap)
-            const float* sx = cur;
+            // final conv over snake(x) (fp16, in `cur` after the swap)
+            const __half* sx = reinterpret_cast<const __half*>(cur);
             float* o = d.out;
             const float* w = c->final_w;
             const float fb = c->final_bias;
@@ -1269,7 +1275,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                                      s, sx, w, fb, o, C, Tq);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
-                {"final_conv", 14.0 * C * double(n), double(n) * C * 4 + double(n) * 4, "final_kernel"});
+                {"final_conv", 14.0 * C * double(n), double(n) * C * 2 + double(n) * 4, "final_kernel"});
             if (rc) return rc;
         }
     }

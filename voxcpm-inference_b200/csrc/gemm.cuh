@@ -135,11 +135,14 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
     const int num_kb = (args.K + Cfg::kBK - 1) / Cfg::kBK;
     const int num_tiles = args.m_tiles * args.n_tiles;
     const int rows_per_tile = EPI == kEpiConvT ? 2 * args.s * args.cpt : Cfg::kBM;
+    // at most one tile per CTA: the epilogue warpgroups help dequantise (Q4_0)
+    const bool dq_help = kQ4 && num_tiles <= static_cast<int>(gridDim.x);
+    const int dq_threads = 32 * Cfg::kDqWarps + (dq_help ? 256 : 0);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full_bar[i], 1);
-            mbar_init(&ready_bar[i], Cfg::kDqWarps);
+            mbar_init(&ready_bar[i], dq_threads / 32);
             mbar_init(&empty_bar[i], 1);
             mbar_init(&raw_bar[i], 1);
         }
@@ -237,6 +240,102 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
     }
     if (warp == 0 || (warp >= 4 && warp < 12)) grid_dep_sync();
 
+    // ------------------------------------------- Q4_0 dequantisers ------
+    // Thread t of nthr dequantisers.  The dedicated warps (12..) always run
+    // it; when every CTA has at most one tile (short GEMMs: streaming
+    // steps), the epilogue warpgroups, idle until that tile's accumulator is
+    // complete, run it too, tripling the dequantisation rate of the CTA's
+    // only mainloop.
+    constexpr int kDqThreads = 32 * Cfg::kDqWarps;
+    auto dequant = [&](const int t, const int nthr) {
+        // MN-major: item i -> k row kl = i % 64 and block bi = i / 64 of the
+        // up to five that intersect [m0, m0 + 128); m0 is a multiple of 8, so
+        // a block lands on four aligned 16-byte chunks of the MN-major tile.
+        // The smem offsets of a thread's items depend on the tile only: they
+        // are computed once per tile, not per k step.
+        constexpr int kMnItems = (64 * 5 + kDqThreads - 1) / kDqThreads;
+        constexpr uint32_t kNone = 0xFFFFFFFFu;
+        uint32_t mn_src[kMnItems], mn_dst[kMnItems][4];
+        int mn_kl[kMnItems], mn_bi[kMnItems];
+        bool mn_mv[kMnItems];
+        int it = 0, m0_prev = -1;
+        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+            const int m0 = (tile % args.m_tiles) * rows_per_tile;
+            if (AK == kAQ4MN && m0 != m0_prev) {
+                m0_prev = m0;
+                const int b_first = m0 >> 5;
+                const int nblk = ((m0 + 127) >> 5) - b_first + 1;
+#pragma unroll
+                for (int j = 0; j < kMnItems; ++j) {
+                    const int i = t + j * nthr;
+                    const int kl = i & 63, bi = i >> 6;
+                    const int blk = b_first + bi;
+                    mn_kl[j] = kl;
+                    mn_bi[j] = bi + (b_first & 7);  // scale position in the row's box of 16
+                    mn_mv[j] = blk * 32 < args.M;
+                    mn_src[j] = bi < nblk ? static_cast<uint32_t>(kl * kQ4MNNibBox + bi * 16) : kNone;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {  // word c: elements 8c..8c+7 of the block
+                        const int ml = blk * 32 + c * 8 - m0;
+                        const int hh = ml >> 6, mc = (ml & 63) >> 3;
+                        mn_dst[j][c] = (bi < nblk && ml >= 0 && ml < 128)
+                                           ? static_cast<uint32_t>(hh * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 +
+                                                                   (((mc ^ kl) & 7) << 4))
+                                           : kNone;
+                    }
+                }
+            }
+            bool ok = true;
+            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                const int st = it % S;
+                if (!mbar_wait(&raw_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* a_dst = smem + st * Cfg::kStageBytes;
+                const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
+                const int k0 = kb * Cfg::kBK;
+                if (AK == kAQ4K) {
+                    // item i -> row m0 + (i & 127), block hb = i >> 7 of the
+                    // step's two (k0..k0+63): nibbles 16 B, the scale at
+                    // position (2 kb + hb) & 7 of the row's 8
+#pragma unroll
+                    for (int i = t; i < 256; i += nthr) {
+                        const int r = i & 127, hb = i >> 7;
+                        const int m = m0 + r;
+                        const bool valid = m < args.M && k0 + hb * 32 < args.K;
+                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + r * kQ4KScaleBox;
+                        const __half2 d2 = __half2half2(valid ? sc[(2 * kb + hb) & 7] : __float2half_rn(0.f));
+                        const uint4 q = reinterpret_cast<const uint4*>(raw + r * kQ4KNibBox)[hb];
+                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)  // word c: elements 8c..8c+7 of the block
+                            *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(r, hb * 32 + c * 8)) =
+                                q4_dequant8_split(qw[c], d2);
+                    }
+                } else {
+                    const __half* sc = reinterpret_cast<const __half*>(raw + kQ4MNScaleOff);
+#pragma unroll
+                    for (int j = 0; j < kMnItems; ++j) {
+                        if (mn_src[j] == kNone) continue;
+                        const int kl = mn_kl[j];
+                        const bool valid = mn_mv[j] && k0 + kl < args.K;
+                        const __half2 d2 = __half2half2(valid ? sc[kl * kQ4MNScaleBox + mn_bi[j]] : __float2half_rn(0.f));
+                        const uint4 q = *reinterpret_cast<const uint4*>(raw + mn_src[j]);
+                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            if (mn_dst[j][c] != kNone)
+                                *reinterpret_cast<uint4*>(a_dst + mn_dst[j][c]) = q4_dequant8_split(qw[c], d2);
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready_bar[st]);
+            }
+            if (!ok) break;
+        }
+    };
     if (warp == 0) {
         if (lane == 0) {
             // ------------------------------------------------ TMA producer --
@@ -303,72 +402,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
             }
         }
     } else if (kQ4 && warp >= 12) {
-        // ------------------------------------------- Q4_0 dequantisers ------
-        constexpr int kDqThreads = 32 * Cfg::kDqWarps;
-        const int t = threadIdx.x - 384;  // 0..kDqThreads-1
-        int it = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-            const int m0 = (tile % args.m_tiles) * rows_per_tile;
-            bool ok = true;
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
-                const int st = it % S;
-                if (!mbar_wait(&raw_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-                const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
-                const int k0 = kb * Cfg::kBK;
-                if (AK == kAQ4K) {
-                    // item i -> row m0 + (i & 127), block hb = i >> 7 of the
-                    // step's two (k0..k0+63): nibbles 16 B, the scale at
-                    // position (2 kb + hb) & 7 of the row's 8
-#pragma unroll
-                    for (int i = t; i < 256; i += kDqThreads) {
-                        const int r = i & 127, hb = i >> 7;
-                        const int m = m0 + r;
-                        const bool valid = m < args.M && k0 + hb * 32 < args.K;
-                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + r * kQ4KScaleBox;
-                        const __half2 d2 = __half2half2(valid ? sc[(2 * kb + hb) & 7] : __float2half_rn(0.f));
-                        const uint4 q = reinterpret_cast<const uint4*>(raw + r * kQ4KNibBox)[hb];
-                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)  // word c: elements 8c..8c+7 of the block
-                            *reinterpret_cast<uint4*>(a_dst + sw128_kmajor_off(r, hb * 32 + c * 8)) =
-                                q4_dequant8_split(qw[c], d2);
-                    }
-                } else {
-                    // item i -> k row kl = i % 64 and block bi = i / 64 of the
-                    // up to five that intersect [m0, m0 + 128); m0 is a
-                    // multiple of 8, so a block lands on four aligned 16-byte
-                    // chunks of the MN-major tile
-                    const int b_first = m0 >> 5;
-                    const int nblk = ((m0 + 127) >> 5) - b_first + 1;
-#pragma unroll 1
-                    for (int i = t; i < 64 * nblk; i += kDqThreads) {
-                        const int kl = i & 63, bi = i >> 6;
-                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4MNScaleOff) + kl * kQ4MNScaleBox + (b_first & 7);
-                        const int blk = b_first + bi;
-                        const bool valid = k0 + kl < args.K && blk * 32 < args.M;
-                        const __half2 d2 = __half2half2(valid ? sc[bi] : __float2half_rn(0.f));
-                        const uint4 q = *reinterpret_cast<const uint4*>(raw + kl * kQ4MNNibBox + bi * 16);
-                        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {  // word c: elements 8c..8c+7 of the block
-                            const int ml = blk * 32 + c * 8 - m0;
-                            if (ml < 0 || ml >= 128) continue;
-                            const int hh = ml >> 6, mc = (ml & 63) >> 3;
-                            const uint32_t off = hh * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 + (((mc ^ kl) & 7) << 4);
-                            *reinterpret_cast<uint4*>(a_dst + off) = q4_dequant8_split(qw[c], d2);
-                        }
-                    }
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ready_bar[st]);
-            }
-            if (!ok) break;
-        }
+        dequant(threadIdx.x - 384, dq_threads);
     } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------ epilogue --
         const int eg = (warp - 4) >> 2;          // epilogue warpgroup == accumulator it drains
@@ -398,6 +432,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         if (EPI == kEpiPW && args.res != nullptr && et == 0) {
             for (int l = 0; l < Cfg::kEpiAhead; ++l) issue_res(l);
         }
+        if (kQ4 && dq_help) dequant(kDqThreads + threadIdx.x - 128, dq_threads);
         for (int tile = blockIdx.x + eg * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, tl += 2) {
             const int acc = eg;
             // the tile's parameters are loaded first, then the accumulator awaited

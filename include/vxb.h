@@ -189,6 +189,36 @@ VXB_API int vxb_time_ops(vxb_ctx* ctx, int reps, void* flush, size_t flush_bytes
  * always allocates its compute arena (src/backend.cpp:241-287). */
 VXB_API int vxb_decode_static(vxb_ctx* ctx, const float* z_dev, float* out_dev, int batch, int T, void* stream);
 
+/* ---- opt-in stateful streaming ---- */
+
+/* One latent stream decoded n frames per push, carrying every causal layer's
+ * left context from push to push (6 latent frames for model.0, 1 input row
+ * per transposed conv, 6*d rows per residual unit's dilated conv, 6 rows for
+ * the final conv) instead of re-decoding earlier frames: the pushes of a
+ * stream emit exactly the continuous decode of all its frames so far.  This
+ * is NOT the reference's streaming behaviour, which decodes every window of
+ * vae_decode_mock.cpp alone with zero left context (vae_decode_mock.cpp:13-15,
+ * :1337-1347); it has no counterpart there.  A stream object owns its
+ * windows (two sets of a few MB for n = 6) and two CUDA graphs; it shares the
+ * context's weights, device, stream and status word, so pushes of several
+ * streams of one context must not overlap.  Requires vxb_prepare. */
+typedef struct vxb_stream vxb_stream;
+
+VXB_API int vxb_stream_open(vxb_ctx* ctx, int n_frames, vxb_stream** out);
+
+/* Decodes the next n_frames of the stream: z [latent_dim][n_frames] (t
+ * fastest) -> out [hop * n_frames], HOST pointers, blocking (60 s bound). */
+VXB_API int vxb_stream_push(vxb_stream* s, const float* z_host, float* out_host);
+
+/* Same with DEVICE pointers, enqueued on `stream` (NULL = the context's
+ * stream) without waiting; completion via vxb_sync on the context. */
+VXB_API int vxb_stream_push_device(vxb_stream* s, const float* z_dev, float* out_dev, void* stream);
+
+/* Forgets the stream's history: the next push starts a new stream. */
+VXB_API int vxb_stream_reset(vxb_stream* s);
+
+VXB_API int vxb_stream_close(vxb_stream* s);
+
 /* ---- encoder: waveform -> latent ---- */
 
 /* Sets the encoder config for callers that upload tensors themselves

@@ -272,3 +272,40 @@ def test_q4_fp16_cache_gives_the_same_decode(vxb):
     b = d.decode(z)
     d.close()
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("quant", ["f16", "q4_0"])
+def test_layer_state_stream_equals_continuous_decode(vxb, quant):
+    """Stateful streaming with per-layer carried context: a stream pushed 6
+    frames at a time emits the continuous decode of the whole stream (the
+    GPU's one-shot decode to 1e-5, the oracle to 5e-4); after a reset the
+    next pushes start a new stream."""
+    mk = dict(quant=quant, seed=0)
+    d = decoder_for(vxb, **mk)
+    z = S.make_latents(1, 30, seed=33)[0, 0]  # [64, 30]
+    full = d.decode(z[None])[0]
+    st = vxb.LayerStateStream(d, 6)
+    got = np.concatenate([st.push(z[:, t:t + 6]) for t in range(0, 30, 6)])
+    assert got.shape == full.shape
+    err = float(np.abs(got - full).max())
+    assert err <= 1e-5, f"stream vs one-shot decode max|d| {err:.3e}"
+    path, _ = model_path(**mk)
+    ref = O.OracleModel(path).decode(z[None, :, :], O.MODE_GPU)[0]
+    assert float(np.abs(got - ref).max()) <= 5e-4
+    st.reset()
+    again = np.concatenate([st.push(z[:, t:t + 6]) for t in range(0, 12, 6)])
+    assert np.array_equal(again, got[: again.size])
+    st.close()
+
+
+def test_layer_state_stream_long_utterance_matches_reference(vxb):
+    """The 60 s utterance pushed 6 frames at a time through the stateful
+    stream stays within 2e-3 of the reference's continuous L1 decode."""
+    f, mk = big("f16_c3_t1500")
+    d = decoder_for(vxb, **mk)
+    z = f["z"][0]
+    st = vxb.LayerStateStream(d, 6)
+    got = np.concatenate([st.push(z[:, t:t + 6]) for t in range(0, 1500, 6)])
+    st.close()
+    err = float(np.abs(got - f["l1"][0]).max())
+    assert err <= 2e-3, f"stateful stream vs reference L1 max|d| {err:.3e}"

@@ -19,16 +19,20 @@ namespace vxb {
 // y[b*T + t][c] = b0[c] + sum_k w[c][k] * z[b][c][t + k - 6]   (reference
 // depthwise_conv_l2_custom / depthwise_conv_custom with stride 1, dilation 1,
 // padding 3: src = t + k*d - 2*pad).
+// t_off: the first t_off frames of each z sequence are a streaming window's
+// history: outputs start at frame t_off (out holds T - t_off frames per sequence).
 __global__ void head_kernel(const float* __restrict__ z, const float* __restrict__ w /*[L][7]*/,
-                            const float* __restrict__ bias, __half* __restrict__ out, int B, int L, int T) {
+                            const float* __restrict__ bias, __half* __restrict__ out, int B, int L, int T,
+                            int t_off) {
     grid_dep_sync();
-    const long long total = static_cast<long long>(B) * T * L;
+    const int To = T - t_off;
+    const long long total = static_cast<long long>(B) * To * L;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const int c = static_cast<int>(i % L);
         const long long n = i / L;
-        const int t = static_cast<int>(n % T);
-        const int b = static_cast<int>(n / T);
+        const int t = static_cast<int>(n % To) + t_off;
+        const int b = static_cast<int>(n / To);
         const float* zc = z + (static_cast<long long>(b) * L + c) * T;
         float acc = bias[c];
 #pragma unroll
@@ -71,7 +75,10 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
                                                       const float* __restrict__ bias,
                                                       const float* __restrict__ a2,
                                                       const float* __restrict__ i2, __half* __restrict__ out,
-                                                      int C, int T, int B, int d, int run) {
+                                                      int C, int T, int B, int d, int run, int t_off) {
+    // T outputs per sequence; x holds T + t_off rows per sequence, the first
+    // t_off of them a streaming window's history (output t reads row t + t_off)
+    const int Tx = T + t_off;
     const int Q = C >> 1;
     const int J = (T + d - 1) / d;
     const int R = (J + run - 1) / run;
@@ -97,12 +104,12 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
     const float2 iv2 = *reinterpret_cast<const float2*>(i2 + c);
     grid_dep_sync();
     if (!active) return;
-    const float* xb = x + static_cast<long long>(b) * T * C + c;
+    const float* xb = x + static_cast<long long>(b) * Tx * C + static_cast<long long>(t_off) * C + c;
     __half* ob = out + static_cast<long long>(b) * T * C + c;
     const int t_first = phase + (jr * run - 6) * d;  // row m of the run is t_first + m*d
     auto load = [&](int t) {
-        return (t >= 0 && t < T) ? __ldg(reinterpret_cast<const float2*>(xb + static_cast<long long>(t) * C))
-                                 : make_float2(0.f, 0.f);
+        return (t >= -t_off && t < T) ? __ldg(reinterpret_cast<const float2*>(xb + static_cast<long long>(t) * C))
+                                      : make_float2(0.f, 0.f);
     };
     // window slot of row m is m % 7; rows 0..5 are the warm-up (before the first output)
     float2 win[7];
@@ -152,14 +159,16 @@ __global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ 
 // lanes (9 shuffles for 8 outputs).  Requires C % 8 == 0 and C <= 128.
 constexpr int kFinTT = 64;
 
+// t_off: s holds T + t_off rows per sequence, the first t_off a streaming
+// window's history; y holds T outputs per sequence (output t reads rows up to t + t_off).
 __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
-                                                    float bias, float* __restrict__ y, int C, int T) {
+                                                    float bias, float* __restrict__ y, int C, int T, int t_off) {
     extern __shared__ float4 fsh4[];  // [(kFinTT + 6)][C/4]
     const int c4n = C / 4;
     const int t0 = blockIdx.x * kFinTT;
     const int b = blockIdx.y;
     const int rows = min(kFinTT, T - t0) + 6;
-    const __half* sb = s + static_cast<long long>(b) * T * C;
+    const __half* sb = s + static_cast<long long>(b) * (T + t_off) * C + static_cast<long long>(t_off) * C;
     if (threadIdx.x * 32 < C * 7) prefetch_l2(w + threadIdx.x * 32);  // taps: constant, into L2 before the wait
     grid_dep_sync();
     // 16-byte loads of 8 fp16 channels, widened to two float4 in shared memory
@@ -171,7 +180,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
         const int i = threadIdx.x + j * 256;
         const int r = i / c8n, cq = i - r * c8n;
         const int t = t0 - 6 + r;
-        v[j] = (i < rows * c8n && t >= 0) ? __ldg(reinterpret_cast<const uint4*>(sb + static_cast<long long>(t) * C) + cq)
+        v[j] = (i < rows * c8n && t >= -t_off) ? __ldg(reinterpret_cast<const uint4*>(sb + static_cast<long long>(t) * C) + cq)
                                          : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll

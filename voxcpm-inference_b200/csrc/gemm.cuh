@@ -49,6 +49,8 @@ struct GemmArgs {
     void* out;                // fp32 or fp16 [N][M] (PW); fp32 [N*s][Cout] (ConvT)
     int out_f16;              // PW: 1 = fp16 output
     int s, cout, cpt, seq_len;  // ConvT: stride, Cout, couts per tile, frames per sequence
+    int skip;                 // ConvT: leading input frames per sequence whose outputs are not written
+                              // (a streaming window's history row); output rows shift down by skip*s
     int* status;              // device status word (bounded-wait failures)
 };
 
@@ -545,9 +547,11 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                     epi_bar(bar_id);
                     const int c = c0 + lane;
                     const int n = n_start + c;
-                    if (c >= 1 && c < BN && n < args.N) {
-                        const bool seq_start = (n % args.seq_len) == 0;
-                        float* orow = out + static_cast<size_t>(n) * s * args.cout + co_lo;  // y row (n*s + 0)
+                    const int nl = n % args.seq_len;  // frame within its sequence
+                    if (c >= 1 && c < BN && n < args.N && nl >= args.skip) {
+                        const bool seq_start = nl == 0;
+                        const size_t orow_n = static_cast<size_t>(n / args.seq_len) * (args.seq_len - args.skip) + (nl - args.skip);
+                        float* orow = out + orow_n * s * args.cout + co_lo;  // y row (n*s + 0)
                         const float* sgl = sG + 4 + lane;
                         const int rs = 2 * s * Cfg::kEpiLD;                                  // next cout
 #pragma unroll

@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <array>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -394,8 +395,9 @@ int convt_cpt(int s) {
 // Transposed conv GEMM: W folded [Cin rows][2s*Cout] (F16, or Q4_0 rows padded
 // to w.pitch), x fp16 [B*T][Cin].
 int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, int B, int T, const float* bias,
-                float* y, int* status) {
+                float* y, int* status, int skip = 0) {
     const int64_t N = int64_t(B) * T;
+    if (skip < 0 || skip >= T) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad skip");
     if (Cin <= 0 || Cout <= 0 || s <= 0 || s > 32 || N <= 0 || N * s > (int64_t(1) << 31) - 1)
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: bad extents");
     if (Cin % 8) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: Cin must be a multiple of 8");
@@ -422,6 +424,7 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     a.cout = Cout;
     a.cpt = cpt;
     a.seq_len = T;
+    a.skip = skip;
     a.status = status;
     if (w.type == VXB_TYPE_F16) {
         if ((uint64_t(M) * 2) % 16) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: 2s*Cout must be a multiple of 8");
@@ -583,13 +586,13 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
 
 // Residual-unit prologue over x [B][T][C] -> h fp16, dilation d.
 int launch_res_pre(const float* x, const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
-                   const float* i2, __half* h, int C, int B, int T, int d, int sms, cudaStream_t s) {
+                   const float* i2, __half* h, int C, int B, int T, int d, int sms, cudaStream_t s, int t_off = 0) {
     if (C % 2) return fail(VXB_ERR_INVALID_ARGUMENT, "prologue: C must be even");
     const int run = res_pre_run(C, T, B, d, sms);
     const long long threads = res_pre_threads(C, T, B, d, run);
     if (threads > (1LL << 40)) return fail(VXB_ERR_INVALID_ARGUMENT, "prologue: too many threads");
     const cudaError_t e = launch_pdl(res_pre_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
-                                     s, x, a1, i1, dw, db, a2, i2, h, C, T, B, d, run);
+                                     s, x, a1, i1, dw, db, a2, i2, h, C, T, B, d, run, t_off);
     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("prologue launch: ") + cudaGetErrorString(e));
 }
 
@@ -1132,7 +1135,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
         rc = sink.kernel(
             [=](cudaStream_t s) {
                 const cudaError_t e =
-                    launch_pdl(head_kernel, dim3(grid_1d(int64_t(B) * T * L, 256)), dim3(256), 0, s, z, w, bb, o, B, L, T);
+                    launch_pdl(head_kernel, dim3(grid_1d(int64_t(B) * T * L, 256)), dim3(256), 0, s, z, w, bb, o, B, L, T, 0);
                 return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
             },
             {"head_dw", 14.0 * n0 * L, n0 * L * (4 + 2) + L * 8 * 4, "head_kernel"});
@@ -1287,7 +1290,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                 [=](cudaStream_t s) {
                     dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
                     const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), sizeof(float) * (kFinTT + 6) * C,
-                                                     s, sx, w, fb, o, C, Tq);
+                                                     s, sx, w, fb, o, C, Tq, 0);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
                 {"final_conv", 14.0 * C * double(n), double(n) * C * 2 + double(n) * 4, "final_kernel"});
@@ -2113,5 +2116,351 @@ extern "C" int vxb_decode_static(vxb_ctx* c, const float* z_dev, float* out_dev,
     if ((rc = emit_decode(c, d, B, T, sink))) return rc;
     // report a failed bounded wait through vxb_sync (pinned word made at vxb_open)
     CUDA_TRY(cudaMemcpyAsync(c->status_host, d.status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    return VXB_OK;
+}
+
+// ------------------------------------------------------- stateful streaming --
+//
+// A vxb_stream decodes one latent stream n frames per push and carries every
+// causal layer's left context from push to push: each layer reads a window
+// [history rows | this push's rows] of its own input -- 6 latent frames for
+// model.0, 1 input row for each transposed conv, 6*d rows for each residual
+// unit's dilated conv, 6 rows for the final conv -- and computes only the
+// new rows.  The history of a fresh stream is zero, which is exactly the
+// causal zero padding of a sequence start, so the pushes together emit the
+// continuous decode of the whole stream.  Two window sets alternate between
+// pushes (one CUDA graph each); the end of a push copies the tail of every
+// window of the set in use into the head of the other set's window.
+
+namespace {
+
+// One strided copy of the shift: `count` segments of `words` 32-bit words.
+struct ShiftSeg {
+    const uint32_t* src;
+    uint32_t* dst;
+    int count, words;
+    int src_stride, dst_stride;  // in words
+};
+
+__global__ void shift_history_kernel(const ShiftSeg* __restrict__ segs, int nseg) {
+    for (int g = blockIdx.x; g < nseg; g += gridDim.x) {
+        const ShiftSeg sg = segs[g];
+        const int total = sg.count * sg.words;
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int k = i / sg.words, w = i - k * sg.words;
+            sg.dst[k * sg.dst_stride + w] = sg.src[k * sg.src_stride + w];
+        }
+    }
+}
+
+// The windows of one set.
+struct StreamSet {
+    float* z = nullptr;                 // [L][6 + n]: the latent window, t fastest per channel
+    std::vector<__half*> wc;            // per block: transposed-conv input [1 + n_b][Cin] (fp16, Snake applied)
+    std::vector<std::array<float*, 3>> wx;  // per block and unit: residual-stream window [6d + m_b][Cout] (fp32)
+    __half* wf = nullptr;               // final conv input [6 + m_last][C_last] (fp16, final Snake applied)
+    ShiftSeg* segs = nullptr;           // device copy of the shift into the other set
+    int nseg = 0;
+    Plan plan;                          // ops + graph of a push on this set
+};
+
+}  // namespace
+
+struct vxb_stream {
+    vxb_ctx* c = nullptr;
+    int n = 0;                          // latent frames per push
+    int parity = 0;                     // set used by the next push
+    StreamSet set[2];
+    __half* h0 = nullptr;               // model.0 output [n][L]
+    __half* h = nullptr;                // prologue output [m_max][C_max]
+    float* out = nullptr;               // [n * hop]
+    std::vector<void*> allocs;
+    std::vector<std::pair<void*, size_t>> wins;  // every window of both sets (zeroed by a reset)
+};
+
+namespace {
+
+int stream_alloc(vxb_stream* st, size_t bytes, void** p) {
+    CUDA_TRY(cudaMalloc(p, std::max<size_t>(bytes, 16)));
+    st->allocs.push_back(*p);
+    return VXB_OK;
+}
+
+// The launches of one push on window set p (and the shift into set 1 - p).
+int emit_stream_push(vxb_stream* st, int p, OpSink& sink) {
+    vxb_ctx* c = st->c;
+    StreamSet& S = st->set[p];
+    StreamSet& O = st->set[1 - p];
+    const int L = c->latent_dim, D = c->decoder_dim, n = st->n;
+    int* status = c->status;
+    static const int kDil[3] = {1, 3, 9};
+    const int sms = num_sms(c->device);
+    int rc;
+    std::vector<ShiftSeg> segs;
+    auto seg_rows = [&](const void* src_win, void* dst_win, int64_t hist_row0, int64_t rows, int64_t cols, int elem) {
+        const int64_t words = rows * cols * elem / 4;
+        segs.push_back({static_cast<const uint32_t*>(src_win) + hist_row0 * cols * elem / 4,
+                        static_cast<uint32_t*>(dst_win), 1, static_cast<int>(words), 0, 0});
+    };
+    {   // model.0 over the latent window (6 history frames), model.1 into block 0's window (row 1)
+        const float* z = S.z;
+        const float *w = c->dw0, *bb = c->b0.v;
+        __half* o = st->h0;
+        rc = sink.kernel(
+            [=](cudaStream_t s) {
+                const cudaError_t e = launch_pdl(head_kernel, dim3(grid_1d(int64_t(n) * L, 256)), dim3(256), 0, s, z, w,
+                                                 bb, o, 1, L, n + 6, 6);
+                return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "head launch");
+            },
+            {"head_dw", 14.0 * n * L, double(n) * L * 6, "head_kernel"});
+        if (rc) return rc;
+        segs.push_back({reinterpret_cast<const uint32_t*>(S.z) + n, reinterpret_cast<uint32_t*>(O.z), L, 6, n + 6, n + 6});
+        GemmOp op;
+        const Block& b0 = c->blocks[0];
+        if ((rc = setup_pointwise(&op, c->pw1->gemm_view(), L, D, st->h0, n, c->b1.v, nullptr, b0.alpha.v,
+                                  b0.alpha.inv, 1, S.wc[0] + D, status)))
+            return rc;
+        if ((rc = sink.gemm(op, {"pw_model1", 2.0 * D * L * n, c->pw1->gemm_bytes(), gemm_kernel_name(op)}))) return rc;
+    }
+    int64_t nb = n;  // this push's input frames of the block
+    const size_t nblk = c->blocks.size();
+    for (size_t bi = 0; bi < nblk; ++bi) {
+        const Block& b = c->blocks[bi];
+        const bool last_block = bi + 1 == nblk;
+        const int C = b.cout;
+        const int64_t m = nb * b.s;  // this push's output rows of the block
+        {
+            GemmOp op;
+            if ((rc = setup_convt(&op, b.convt->gemm_view(), b.cin, C, b.s, S.wc[bi], 1, static_cast<int>(1 + nb),
+                                  b.bias.v, S.wx[bi][0] + 6 * int64_t(C), status, 1)))
+                return rc;
+            if ((rc = sink.gemm(op, {"convt_b" + std::to_string(bi), 2.0 * (2.0 * b.s * C) * b.cin * double(nb),
+                                     b.convt->gemm_bytes(), gemm_kernel_name(op)})))
+                return rc;
+            seg_rows(S.wc[bi], O.wc[bi], nb, 1, b.cin, 2);
+        }
+        for (int r = 0; r < 3; ++r) {
+            const ResUnit& u = b.ru[r];
+            const int dl = kDil[r];
+            float* x = S.wx[bi][r];  // [6 dl + m][C]
+            {
+                __half* hh = st->h;
+                const int mq = static_cast<int>(m);
+                rc = sink.kernel(
+                    [=](cudaStream_t s) {
+                        return launch_res_pre(x, u.a1.v, u.a1.inv, u.dw, u.db.v, u.a2.v, u.a2.inv, hh, C, 1, mq, dl,
+                                              sms, s, 6 * dl);
+                    },
+                    {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(m) * C * 20.0,
+                     double(m) * C * 6, "res_pre_kernel"});
+                if (rc) return rc;
+            }
+            GemmOp op;
+            const float* res = x + 6 * dl * int64_t(C);
+            if (r < 2) {
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, st->h, m, u.pb.v, res, nullptr, nullptr, 0,
+                                     S.wx[bi][r + 1] + 6 * kDil[r + 1] * int64_t(C), status);
+            } else if (!last_block) {
+                const Block& nbk = c->blocks[bi + 1];
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, st->h, m, u.pb.v, res, nbk.alpha.v, nbk.alpha.inv, 1,
+                                     S.wc[bi + 1] + C, status);
+            } else {
+                rc = setup_pointwise(&op, u.pw->gemm_view(), C, C, st->h, m, u.pb.v, res, c->final_alpha.v,
+                                     c->final_alpha.inv, 1, S.wf + 6 * int64_t(C), status);
+            }
+            if (rc) return rc;
+            if ((rc = sink.gemm(op, {"pw_b" + std::to_string(bi) + "u" + std::to_string(r), 2.0 * C * C * double(m),
+                                     u.pw->gemm_bytes(), gemm_kernel_name(op)})))
+                return rc;
+            seg_rows(x, O.wx[bi][r], m, 6 * dl, C, 4);
+        }
+        if (last_block) {
+            const __half* sx = S.wf;
+            float* o = st->out;
+            const float* w = c->final_w;
+            const float fb = c->final_bias;
+            const int Tq = static_cast<int>(m);
+            rc = sink.kernel(
+                [=](cudaStream_t s) {
+                    dim3 grid((Tq + kFinTT - 1) / kFinTT, 1);
+                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), sizeof(float) * (kFinTT + 6) * C, s,
+                                                     sx, w, fb, o, C, Tq, 6);
+                    return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
+                },
+                {"final_conv", 14.0 * C * double(m), double(m) * C * 2, "final_kernel"});
+            if (rc) return rc;
+            seg_rows(S.wf, O.wf, m, 6, C, 2);
+        }
+        nb = m;
+    }
+    // the shift: every window's tail -> the other set's head
+    S.nseg = static_cast<int>(segs.size());
+    CUDA_TRY(cudaMalloc(&S.segs, sizeof(ShiftSeg) * segs.size()));
+    st->allocs.push_back(S.segs);
+    CUDA_TRY(cudaMemcpy(S.segs, segs.data(), sizeof(ShiftSeg) * segs.size(), cudaMemcpyHostToDevice));
+    const ShiftSeg* sg = S.segs;
+    const int ns = S.nseg;
+    return sink.kernel(
+        [=](cudaStream_t s) {
+            shift_history_kernel<<<ns, 256, 0, s>>>(sg, ns);
+            const cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "history shift launch");
+        },
+        {"shift_history", 0.0, 0.0, "shift_history_kernel"});
+}
+
+void free_stream(vxb_stream* st) {
+    for (int p = 0; p < 2; ++p) {
+        if (st->set[p].plan.exec) cudaGraphExecDestroy(st->set[p].plan.exec);
+        if (st->set[p].plan.graph) cudaGraphDestroy(st->set[p].plan.graph);
+    }
+    for (void* q : st->allocs) cudaFree(q);
+    st->allocs.clear();
+}
+
+// A fresh stream: every window of both sets zero (the causal zero padding of a
+// sequence start), the next push on set 0.
+int stream_zero(vxb_stream* st, cudaStream_t s) {
+    for (auto& w : st->wins) CUDA_TRY(cudaMemsetAsync(w.first, 0, w.second, s));
+    st->parity = 0;
+    return VXB_OK;
+}
+
+}  // namespace
+
+extern "C" int vxb_stream_open(vxb_ctx* c, int n, vxb_stream** out) {
+    if (!c || !out || n <= 0 || n > 4096) return fail(VXB_ERR_INVALID_ARGUMENT, "vxb_stream_open: bad arguments");
+    *out = nullptr;
+    if (!c->prepared) return fail(VXB_ERR_NOT_READY, "call vxb_prepare before vxb_stream_open");
+    DeviceGuard g(c->device);
+    auto st = std::make_unique<vxb_stream>();
+    st->c = c;
+    st->n = n;
+    const int L = c->latent_dim, nb_blocks = static_cast<int>(c->blocks.size());
+    static const int kDil[3] = {1, 3, 9};
+    int rc;
+    auto& wins = st->wins;
+    int64_t m_max = 1, cmax = 1;
+    for (int p = 0; p < 2; ++p) {
+        StreamSet& S = st->set[p];
+        void* q = nullptr;
+        if ((rc = stream_alloc(st.get(), sizeof(float) * L * (6 + n), &q))) { free_stream(st.get()); return rc; }
+        S.z = static_cast<float*>(q);
+        wins.push_back({q, sizeof(float) * L * (6 + n)});
+        int64_t nb = n;
+        S.wc.resize(nb_blocks);
+        S.wx.resize(nb_blocks);
+        for (int bi = 0; bi < nb_blocks; ++bi) {
+            const Block& b = c->blocks[bi];
+            const size_t wcb = sizeof(__half) * (1 + nb) * b.cin;
+            if ((rc = stream_alloc(st.get(), wcb, &q))) { free_stream(st.get()); return rc; }
+            S.wc[bi] = static_cast<__half*>(q);
+            wins.push_back({q, wcb});
+            const int64_t m = nb * b.s;
+            for (int r = 0; r < 3; ++r) {
+                const size_t wxb = sizeof(float) * (6 * kDil[r] + m) * b.cout;
+                if ((rc = stream_alloc(st.get(), wxb, &q))) { free_stream(st.get()); return rc; }
+                S.wx[bi][r] = static_cast<float*>(q);
+                wins.push_back({q, wxb});
+            }
+            m_max = std::max(m_max, m);
+            cmax = std::max<int64_t>(cmax, b.cout);
+            nb = m;
+        }
+        const size_t wfb = sizeof(__half) * (6 + nb) * c->blocks.back().cout;
+        if ((rc = stream_alloc(st.get(), wfb, &q))) { free_stream(st.get()); return rc; }
+        S.wf = static_cast<__half*>(q);
+        wins.push_back({q, wfb});
+    }
+    void* q = nullptr;
+    if ((rc = stream_alloc(st.get(), sizeof(__half) * n * L, &q))) { free_stream(st.get()); return rc; }
+    st->h0 = static_cast<__half*>(q);
+    if ((rc = stream_alloc(st.get(), sizeof(__half) * m_max * cmax, &q))) { free_stream(st.get()); return rc; }
+    st->h = static_cast<__half*>(q);
+    if ((rc = stream_alloc(st.get(), sizeof(float) * n * vxb_hop(c), &q))) { free_stream(st.get()); return rc; }
+    st->out = static_cast<float*>(q);
+    if ((rc = stream_zero(st.get(), c->stream))) { free_stream(st.get()); return rc; }
+    for (int p = 0; p < 2; ++p) {
+        Plan& P = st->set[p].plan;
+        PlanSink sink(P);
+        if ((rc = emit_stream_push(st.get(), p, sink))) { free_stream(st.get()); return rc; }
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        int orc = VXB_OK;
+        for (auto& op : P.ops)
+            if ((orc = op(c->stream))) break;
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        if (orc || e != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            free_stream(st.get());
+            return orc ? orc : fail(VXB_ERR_BACKEND, std::string("stream graph capture: ") + cudaGetErrorString(e));
+        }
+        P.graph = graph;
+        if (cudaGraphInstantiate(&P.exec, P.graph, 0) != cudaSuccess) {
+            free_stream(st.get());
+            return fail(VXB_ERR_BACKEND, "stream graph instantiate");
+        }
+    }
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        free_stream(st.get());
+        return fail(VXB_ERR_BACKEND, "vxb_stream_open: device error");
+    }
+    *out = st.release();
+    return VXB_OK;
+}
+
+extern "C" int vxb_stream_push_device(vxb_stream* st, const float* z_dev, float* out_dev, void* stream) {
+    if (!st || !z_dev || !out_dev) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    vxb_ctx* c = st->c;
+    DeviceGuard g(c->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    StreamSet& S = st->set[st->parity];
+    const int n = st->n, L = c->latent_dim;
+    // this push's frames into the latent window after its 6 history frames, channel by channel
+    CUDA_TRY(cudaMemcpy2DAsync(S.z + 6, sizeof(float) * (6 + n), z_dev, sizeof(float) * n, sizeof(float) * n, L,
+                               cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), s));
+    CUDA_TRY(cudaGraphLaunch(S.plan.exec, s));
+    CUDA_TRY(cudaMemcpyAsync(out_dev, st->out, sizeof(float) * n * vxb_hop(c), cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    st->parity ^= 1;
+    return VXB_OK;
+}
+
+extern "C" int vxb_stream_push(vxb_stream* st, const float* z_host, float* out_host) {
+    if (!st || !z_host || !out_host) return fail(VXB_ERR_INVALID_ARGUMENT, "null argument");
+    vxb_ctx* c = st->c;
+    DeviceGuard g(c->device);
+    StreamSet& S = st->set[st->parity];
+    const int n = st->n, L = c->latent_dim;
+    CUDA_TRY(cudaMemcpy2DAsync(S.z + 6, sizeof(float) * (6 + n), z_host, sizeof(float) * n, sizeof(float) * n, L,
+                               cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemsetAsync(c->status, 0, sizeof(int), c->stream));
+    CUDA_TRY(cudaGraphLaunch(S.plan.exec, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(out_host, st->out, sizeof(float) * n * vxb_hop(c), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->status_host, c->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    st->parity ^= 1;
+    int rc = wait_stream(c->stream, 60000);
+    if (rc) return rc;
+    return check_status(c);
+}
+
+extern "C" int vxb_stream_reset(vxb_stream* st) {
+    if (!st) return fail(VXB_ERR_INVALID_ARGUMENT, "null stream");
+    DeviceGuard g(st->c->device);
+    CUDA_TRY(cudaStreamSynchronize(st->c->stream));
+    int rc = stream_zero(st, st->c->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(st->c->stream));
+    return VXB_OK;
+}
+
+extern "C" int vxb_stream_close(vxb_stream* st) {
+    if (!st) return VXB_OK;
+    DeviceGuard g(st->c->device);
+    cudaStreamSynchronize(st->c->stream);
+    free_stream(st);
+    delete st;
     return VXB_OK;
 }

@@ -58,6 +58,11 @@ SIGNATURES = {
     "vxb_pointwise": (_i, [_vp, _i, _i, _i, _vp, _i64, _vp, _vp, _vp, _i, _vp, _vp]),
     "vxb_convt": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
     "vxb_residual_unit": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
+    "vxb_stream_open": (_i, [_vp, _i, ctypes.POINTER(_vp)]),
+    "vxb_stream_push": (_i, [_vp, _vp, _vp]),
+    "vxb_stream_push_device": (_i, [_vp, _vp, _vp, _vp]),
+    "vxb_stream_reset": (_i, [_vp]),
+    "vxb_stream_close": (_i, [_vp]),
     "vxb_set_encoder_config": (_i, [_vp, _i, ctypes.POINTER(_i), _i]),
     "vxb_encoder_hop": (_i, [_vp]),
     "vxb_get_encoder_config": (_i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), _i, ctypes.POINTER(_i)]),
@@ -365,6 +370,43 @@ class Decoder:
         out = np.empty(n, np.float32)
         check(lib().vxb_debug_stage(self.h, stage, ptr(out), n))
         return out
+
+
+class LayerStateStream:
+    """One latent stream decoded n frames per push with every causal layer's
+    left context carried from push to push on the device (vxb_stream_*): the
+    pushes emit exactly the continuous decode of the stream.  Not the
+    reference's streaming behaviour (every window decoded alone)."""
+
+    def __init__(self, decoder: "Decoder", n_frames: int):
+        h = ctypes.c_void_p()
+        check(lib().vxb_stream_open(decoder.h, n_frames, ctypes.byref(h)))
+        self.h, self.n, self.d = h, n_frames, decoder
+        self.latent_dim = decoder.config()["latent_dim"]
+
+    def push(self, z_new: np.ndarray) -> np.ndarray:
+        """z_new [latent, n] (or [1, latent, n]) -> waveform [n * hop]."""
+        z = np.ascontiguousarray(np.asarray(z_new, dtype=np.float32).reshape(self.latent_dim, self.n))
+        out = np.empty(self.n * self.d.hop, np.float32)
+        check(lib().vxb_stream_push(self.h, ptr(z), ptr(out)))
+        return out
+
+    def push_device(self, z_dev, out_dev, stream=None):
+        check(lib().vxb_stream_push_device(self.h, ptr(z_dev), ptr(out_dev), _stream(stream)))
+
+    def reset(self):
+        check(lib().vxb_stream_reset(self.h))
+
+    def close(self):
+        if self.h:
+            lib().vxb_stream_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class StreamingDecoder:

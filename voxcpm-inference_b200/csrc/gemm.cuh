@@ -54,20 +54,23 @@ struct GemmArgs {
     int* status;              // device status word (bounded-wait failures)
 };
 
-// Q4_0 weights are staged per k step from their split form (nibbles
-// [rows][blocks][16 B], each block's 32 values as four words of 8 in the
-// q4_slot order, and fp16 scales [rows][...], made by q4_split_kernel):
+// Q4_0 weights are staged per k step from their split form (made by
+// q4_split_kernel): nibbles [rows][blocks][16 B], each block's 32 values as
+// four words of 8 in the q4_slot order, and the fp16 scales transposed,
+// [blocks][rows], so that consecutive rows' scales are consecutive halves:
 //   K-major (pointwise): 128 rows x 2 blocks -> nibbles 128 x 32 B, scales
-//     128 x 8 (the aligned group of 8 holding the step's 2 scales);
+//     2 block rows x 128 (box {128, 2});
 //   MN-major (transposed conv): 64 k rows x the up to 5 blocks covering a
-//     128-wide m range -> nibbles 64 x 80 B, scales 64 x 16 (from the aligned
-//     group of 8 holding the first block's scale: the 5 fit in 16).
+//     128-wide m range -> nibbles 64 x 80 B, scales 5 block rows x 64 k
+//     (box {64, 5}).
 constexpr int kQ4KNibBox = 32;     // bytes
-constexpr int kQ4KScaleBox = 8;    // fp16 values
+constexpr int kQ4KScaleRows = 2;   // block rows of the scale box
 constexpr int kQ4MNNibBox = 80;    // bytes
-constexpr int kQ4MNScaleBox = 16;  // fp16 values
+constexpr int kQ4MNScaleRows = 5;  // block rows of the scale box
 constexpr int kQ4KScaleOff = 128 * kQ4KNibBox;   // scale area within the raw stage area
 constexpr int kQ4MNScaleOff = 64 * kQ4MNNibBox;
+constexpr int kQ4KRawBytes = kQ4KScaleOff + kQ4KScaleRows * 128 * 2;
+constexpr int kQ4MNRawBytes = kQ4MNScaleOff + kQ4MNScaleRows * 64 * 2;
 
 // Pointwise epilogue chunk: tokens per residual load / output store.  The
 // host builds the residual and output tensor maps with boxes of
@@ -81,7 +84,7 @@ struct GemmCfg {
     static constexpr int kBK = 64;
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kRawBytes = Q4 ? 7168 : 0;  // max(128*(32+16), 64*(80+32))
+    static constexpr int kRawBytes = Q4 ? 6144 : 0;  // >= max(kQ4KRawBytes, kQ4MNRawBytes), 1 KB granular
     static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
     static constexpr int kEpiLD = 36;                            // ConvT: row stride (carry at 3, columns at 4..35)
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
@@ -179,13 +182,13 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         uint8_t* r_dst = a_dst + Cfg::kABytes + Cfg::kBBytes;
         const int k0 = kb * Cfg::kBK;
         if (AK == kAQ4K) {
-            mbar_arrive_expect_tx(&raw_bar[st], 128 * (kQ4KNibBox + 2 * kQ4KScaleBox));
+            mbar_arrive_expect_tx(&raw_bar[st], kQ4KRawBytes);
             tma_load_2d(r_dst, &tmap_a, &raw_bar[st], kb * kQ4KNibBox, m0);
-            tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &raw_bar[st], (2 * kb) & ~7, m0);
+            tma_load_2d(r_dst + kQ4KScaleOff, &tmap_scale, &raw_bar[st], m0, 2 * kb);
         } else if (AK == kAQ4MN) {
-            mbar_arrive_expect_tx(&raw_bar[st], 64 * (kQ4MNNibBox + 2 * kQ4MNScaleBox));
+            mbar_arrive_expect_tx(&raw_bar[st], kQ4MNRawBytes);
             tma_load_2d(r_dst, &tmap_a, &raw_bar[st], (m0 >> 5) * 16, k0);
-            tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &raw_bar[st], (m0 >> 5) & ~7, k0);
+            tma_load_2d(r_dst + kQ4MNScaleOff, &tmap_scale, &raw_bar[st], k0, m0 >> 5);
         }
         mbar_arrive_expect_tx(&full_bar[st], kTx);
         if (AK == kAF16K) {
@@ -211,10 +214,10 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
             const int k0 = kb * Cfg::kBK;
             if (AK == kAQ4K) {
                 tma_prefetch_2d(&tmap_a, kb * kQ4KNibBox, m0);
-                if ((kb & 3) == 0) tma_prefetch_2d(&tmap_scale, (2 * kb) & ~7, m0);
+                tma_prefetch_2d(&tmap_scale, m0, 2 * kb);
             } else if (AK == kAQ4MN) {
                 tma_prefetch_2d(&tmap_a, (m0 >> 5) * 16, k0);
-                tma_prefetch_2d(&tmap_scale, (m0 >> 5) & ~7, k0);
+                tma_prefetch_2d(&tmap_scale, k0, m0 >> 5);
             } else if (AK == kAF16K) {
                 tma_prefetch_2d(&tmap_a, k0, m0);
             } else {
@@ -273,7 +276,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                     const int kl = i & 63, bi = i >> 6;
                     const int blk = b_first + bi;
                     mn_kl[j] = kl;
-                    mn_bi[j] = bi + (b_first & 7);  // scale position in the row's box of 16
+                    mn_bi[j] = bi;  // block row of the scale box
                     mn_mv[j] = blk * 32 < args.M;
                     mn_src[j] = bi < nblk ? static_cast<uint32_t>(kl * kQ4MNNibBox + bi * 16) : kNone;
 #pragma unroll
@@ -299,15 +302,15 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                 const int k0 = kb * Cfg::kBK;
                 if (AK == kAQ4K) {
                     // item i -> row m0 + (i & 127), block hb = i >> 7 of the
-                    // step's two (k0..k0+63): nibbles 16 B, the scale at
-                    // position (2 kb + hb) & 7 of the row's 8
+                    // step's two (k0..k0+63): nibbles 16 B, the scale in
+                    // block row hb of the box
 #pragma unroll
                     for (int i = t; i < 256; i += nthr) {
                         const int r = i & 127, hb = i >> 7;
                         const int m = m0 + r;
                         const bool valid = m < args.M && k0 + hb * 32 < args.K;
-                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff) + r * kQ4KScaleBox;
-                        const __half2 d2 = __half2half2(valid ? sc[(2 * kb + hb) & 7] : __float2half_rn(0.f));
+                        const __half* sc = reinterpret_cast<const __half*>(raw + kQ4KScaleOff);
+                        const __half2 d2 = __half2half2(valid ? sc[hb * 128 + r] : __float2half_rn(0.f));
                         const uint4 q = reinterpret_cast<const uint4*>(raw + r * kQ4KNibBox)[hb];
                         const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                         if (mn_src[j] == kNone) continue;
                         const int kl = mn_kl[j];
                         const bool valid = mn_mv[j] && k0 + kl < args.K;
-                        const __half2 d2 = __half2half2(valid ? sc[kl * kQ4MNScaleBox + mn_bi[j]] : __float2half_rn(0.f));
+                        const __half2 d2 = __half2half2(valid ? sc[mn_bi[j] * 64 + kl] : __float2half_rn(0.f));
                         const uint4 q = *reinterpret_cast<const uint4*>(raw + mn_src[j]);
                         const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll

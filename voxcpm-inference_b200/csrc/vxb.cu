@@ -134,8 +134,9 @@ int num_sms(int dev) {
 
 // A conv weight as a GEMM operand: fp16 bytes, or Q4_0 blocks split into
 // their 16 nibble bytes (p: [rows][pitch bytes], block b at 16 * b, pitch
-// >= 16 * blocks) and their fp16 scales (s: [rows][spitch bytes], spitch a
-// multiple of 16) -- both 16-byte aligned for TMA, the values unchanged.
+// >= 16 * blocks) and their fp16 scales transposed (s: [blocks][spitch
+// bytes], spitch a multiple of 16) -- both 16-byte aligned for TMA, the
+// values unchanged.
 struct WView {
     const void* p = nullptr;
     int type = 0;
@@ -146,8 +147,8 @@ struct WView {
 
 // Q4_0 rows [rows][nblk x 18 B] -> nibbles [rows][pitch B] (block bi at
 // bi * 16, its values 8w..8w+7 in word w in the q4_slot order) + scales
-// [rows][spitch / 2] fp16, one thread per block (the nibbles and scales are
-// moved, not re-quantised).
+// transposed [nblk][spitch / 2] fp16 (block bi of row r at bi * spitch + 2r),
+// one thread per block (the nibbles and scales are moved, not re-quantised).
 __global__ void q4_split_kernel(const uint8_t* __restrict__ src, int64_t rows, int nblk, uint8_t* __restrict__ q,
                                 int pitch, uint8_t* __restrict__ sc, int spitch) {
     const int64_t total = rows * nblk;
@@ -163,8 +164,8 @@ __global__ void q4_split_kernel(const uint8_t* __restrict__ src, int64_t rows, i
             w[e >> 3] |= v << (4 * q4_slot(e & 7));
         }
         *reinterpret_cast<uint4*>(q + r * pitch + bi * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        sc[r * spitch + bi * 2] = blk[0];
-        sc[r * spitch + bi * 2 + 1] = blk[1];
+        sc[int64_t(bi) * spitch + r * 2] = blk[0];  // scales transposed: [block][row]
+        sc[int64_t(bi) * spitch + r * 2 + 1] = blk[1];
     }
 }
 
@@ -201,8 +202,8 @@ int split_q4(const void* w, int64_t inner, int64_t rows, cudaStream_t st, bool a
     // rows at least as wide as the GEMMs' widest TMA boxes (80 nibble bytes,
     // 16 scales); the padding is zero and lies past the matrix
     out->pitch = std::max(nblk * 16, kQ4MNNibBox);
-    out->spitch = std::max((nblk * 2 + 15) / 16 * 16, 2 * kQ4MNScaleBox);
-    const size_t qb = size_t(out->pitch) * rows, sb = size_t(out->spitch) * rows;
+    out->spitch = static_cast<int>(std::max<int64_t>((rows * 2 + 15) / 16 * 16, 256));  // bytes per block row
+    const size_t qb = size_t(out->pitch) * rows, sb = size_t(out->spitch) * nblk;
     if (async_alloc) {
         CUDA_TRY(cudaMallocAsync(&out->q, qb, st));
         CUDA_TRY(cudaMallocAsync(&out->s, sb, st));
@@ -376,7 +377,7 @@ int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t 
         op->akind = kAQ4K;
         // per k step: 2 blocks of nibbles (32 B) and their 2 scales (box of 8) for 128 rows
         rc = make_tmap_u8(&op->ta, w.p, w.pitch, M, kQ4KNibBox, 128);
-        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M, kQ4KScaleBox, 128);
+        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, K / 32, 128, kQ4KScaleRows);
         return rc;
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "pointwise: weight type must be F16 or Q4_0");
@@ -406,7 +407,16 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     const int cpt = convt_cpt(s);
     if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");
     op->epi = kEpiConvT;
-    op->bn = fill_bn(pick_bn(N + 1), (Cout + cpt - 1) / cpt, N, 1);
+    const int m_tiles = (Cout + cpt - 1) / cpt;
+    if (w.type == VXB_TYPE_Q4_0 && m_tiles >= 32) {
+        // Q4_0 weights are dequantised once per (m tile, n tile): with many m
+        // tiles the SMs are filled by m alone, so the widest token tiles keep
+        // the dequantisation per FLOP lowest (b0/b1 at batch 32: 4 -> 1 and
+        // 13 -> 7 passes over the weights)
+        op->bn = N + 1 > 128 ? 256 : pick_bn(N + 1);
+    } else {
+        op->bn = fill_bn(pick_bn(N + 1), m_tiles, N, 1);
+    }
     op->grid = dim3(1);
     int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, op->bn);
     if (rc) return rc;
@@ -436,7 +446,7 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
         op->akind = kAQ4MN;
         // per k step: up to 5 blocks of nibbles (80 B) and 16 scales around them for 64 rows
         rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kQ4MNNibBox, 64);
-        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, Cin, kQ4MNScaleBox, 64);
+        if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M / 32, 64, kQ4MNScaleRows);
         return rc;
     } else {
         return fail(VXB_ERR_INVALID_ARGUMENT, "convt: weight type must be F16 or Q4_0");

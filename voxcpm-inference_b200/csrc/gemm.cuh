@@ -78,14 +78,21 @@ constexpr int kQ4MNRawBytes = kQ4MNScaleOff + kQ4MNScaleRows * 64 * 2;
 constexpr int kEpiChunk = 16;
 constexpr int kBarrierBytes = 512;  // mbarriers + TMEM slot + abort flag
 
-template <int BN, bool Q4, int EPI>
+// RESKB > 0 (Q4_0 only): "resident A" -- every CTA keeps one m tile (the
+// grid is a multiple of m_tiles) and dequantises that tile's whole weight
+// column (K <= 64 * RESKB) once, into RESKB k blocks kept in shared memory
+// for all its n tiles; the stages then carry only B tiles (and, for the
+// first tile, the raw Q4_0 blocks).
+template <int BN, bool Q4, int EPI, int RESKB = 0>
 struct GemmCfg {
     static constexpr int kBM = 128;
     static constexpr int kBK = 64;
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kRawBytes = Q4 ? 6144 : 0;  // >= max(kQ4KRawBytes, kQ4MNRawBytes), 1 KB granular
-    static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+    static constexpr int kResABytes = RESKB * kABytes;
+    static constexpr int kBOff = RESKB ? 0 : kABytes;            // B tile within a stage
+    static constexpr int kStageBytes = kBOff + kBBytes + kRawBytes;
     static constexpr int kEpiLD = 36;                            // ConvT: row stride (carry at 3, columns at 4..35)
     static constexpr int kChunk = kEpiChunk;                     // PW: tokens per residual/output chunk
     static constexpr int kResBytes = kChunk * 128 * 4;           // PW: fp32 [16 tokens][128 channels]
@@ -93,17 +100,18 @@ struct GemmCfg {
     // PW: residual / output chunk buffers per group; loads run kEpiAhead
     // chunks ahead.  Narrow tiles (one or two tiles per CTA on short
     // sequences) take a ring of 2 and spend the room on mainloop stages.
-    static constexpr int kEpiRing = BN <= 64 ? 2 : 4;
+    static constexpr int kEpiRing = (BN <= 64 || RESKB) ? 2 : 4;
     static constexpr int kEpiAhead = kEpiRing / 2;
     static constexpr int kGroupEpiBytes =
         EPI == kEpiConvT ? 128 * kEpiLD * 4 : kEpiRing * kResBytes + kEpiRing * kOut16Bytes;
     static constexpr int kEpiBytes = 2 * kGroupEpiBytes;         // two epilogue warpgroups
-    static constexpr int kBudget = 220 * 1024 - kEpiBytes - 1024 - kBarrierBytes;
+    static constexpr int kBudget = 220 * 1024 - kEpiBytes - 1024 - kBarrierBytes - kResABytes;
     static constexpr int kStagesFit = kBudget / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);   // two accumulators
     static constexpr int kAccStride = BN < 32 ? 32 : BN;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
+    static constexpr int kSmemBytes = kResABytes + kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
+    static_assert(RESKB == 0 || Q4, "resident A is for Q4_0 weights");
     static_assert((4 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
     static constexpr int kDqWarps = 4;                           // Q4_0: dequantiser warps (one per SM sub-partition)
     static constexpr int kThreads = Q4 ? 384 + 32 * kDqWarps : 384;
@@ -111,21 +119,24 @@ struct GemmCfg {
     static_assert(kStages >= 2, "pipeline needs two stages");
 };
 
-template <int AK, int BN, int EPI>
+template <int AK, int BN, int EPI, int RESKB = 0>
 __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, EPI>::kDqWarps : 384, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_res, const __grid_constant__ CUtensorMap tmap_out,
                 const __grid_constant__ CUtensorMap tmap_scale, const GemmArgs args) {
     constexpr bool kQ4 = AK >= kAQ4K;
     constexpr bool kMN = (AK == kAF16MN) || (AK == kAQ4MN);
-    using Cfg = GemmCfg<BN, kQ4, EPI>;
+    constexpr bool kRes = RESKB > 0;
+    using Cfg = GemmCfg<BN, kQ4, EPI, RESKB>;
     static_assert(EPI == kEpiConvT || (BN >= 32 && BN <= 128), "pointwise tiles are 32..128 tokens wide");
     constexpr int S = Cfg::kStages;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* sE = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes);
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + Cfg::kEpiBytes);
+    uint8_t* resA = smem;                          // kRes: the CTA's weight column, RESKB k blocks
+    uint8_t* stages = smem + Cfg::kResABytes;
+    float* sE = reinterpret_cast<float*>(stages + S * Cfg::kStageBytes);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(stages + S * Cfg::kStageBytes + Cfg::kEpiBytes);
     uint64_t* ready_bar = full_bar + S;   // A tile dequantised (Q4 only)
     uint64_t* empty_bar = ready_bar + S;  // stage consumed by the MMAs
     uint64_t* tfull_bar = empty_bar + S;  // accumulator [2] complete
@@ -178,8 +189,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
     // land, and full_bar[st] then expects the B tile only.
     constexpr uint32_t kTx = (kQ4 ? 0 : Cfg::kABytes) + Cfg::kBBytes;
     auto issue_a = [&](int st, int kb, int m0) {
-        uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-        uint8_t* r_dst = a_dst + Cfg::kABytes + Cfg::kBBytes;
+        uint8_t* a_dst = stages + st * Cfg::kStageBytes;
+        uint8_t* r_dst = a_dst + Cfg::kBOff + Cfg::kBBytes;
         const int k0 = kb * Cfg::kBK;
         if (AK == kAQ4K) {
             mbar_arrive_expect_tx(&raw_bar[st], kQ4KRawBytes);
@@ -265,6 +276,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         bool mn_mv[kMnItems];
         int it = 0, m0_prev = -1;
         for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+            if (kRes && tile != static_cast<int>(blockIdx.x)) break;  // the resident column is done
             const int m0 = (tile % args.m_tiles) * rows_per_tile;
             if (AK == kAQ4MN && m0 != m0_prev) {
                 m0_prev = m0;
@@ -297,8 +309,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                     ok = false;
                     break;
                 }
-                uint8_t* a_dst = smem + st * Cfg::kStageBytes;
-                const uint8_t* raw = a_dst + Cfg::kABytes + Cfg::kBBytes;
+                uint8_t* a_dst = kRes ? resA + kb * Cfg::kABytes : stages + st * Cfg::kStageBytes;
+                const uint8_t* raw = stages + st * Cfg::kStageBytes + Cfg::kBOff + Cfg::kBBytes;
                 const int k0 = kb * Cfg::kBK;
                 if (AK == kAQ4K) {
                     // item i -> row m0 + (i & 127), block hb = i >> 7 of the
@@ -354,9 +366,13 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                     if (it >= n_pre) {  // (the first n_pre A parts went out before the wait)
                         if (!mbar_wait(&empty_bar[st], ((it / S) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty))
                             break;
-                        issue_a(st, kb, m0);
+                        if (!kRes || it < num_kb) {
+                            issue_a(st, kb, m0);
+                        } else {
+                            mbar_arrive_expect_tx(&full_bar[st], kTx);  // B only: A is resident
+                        }
                     }
-                    tma_load_2d(smem + st * Cfg::kStageBytes + Cfg::kABytes, &tmap_b, &full_bar[st],
+                    tma_load_2d(stages + st * Cfg::kStageBytes + Cfg::kBOff, &tmap_b, &full_bar[st],
                                 kb * Cfg::kBK, n_start);
                 }
             }
@@ -381,13 +397,14 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % S;
                     if (!mbar_wait(&full_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull) ||
-                        (kQ4 && !mbar_wait(&ready_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull))) {
+                        (kQ4 && (!kRes || it < num_kb) &&
+                         !mbar_wait(&ready_bar[st], (it / S) & 1, abort_flag, args.status, kErrWaitFull))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + st * Cfg::kStageBytes);
-                    const uint32_t b_addr = a_addr + Cfg::kABytes;
+                    const uint32_t a_addr = smem_u32(kRes ? resA + kb * Cfg::kABytes : stages + st * Cfg::kStageBytes);
+                    const uint32_t b_addr = smem_u32(stages + st * Cfg::kStageBytes + Cfg::kBOff);
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
                         // K-major SW128: +32 B per 16 k inside the 128-B row.

@@ -275,23 +275,24 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-template <int AK, int BN, int EPI>
+template <int AK, int BN, int EPI, int RESKB = 0>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const CUtensorMap& to,
                   const CUtensorMap& ts,
-                  const GemmArgs& a, cudaStream_t st) {
-    constexpr int smem = GemmCfg<BN, (AK >= kAQ4K), EPI>::kSmemBytes;
-    constexpr int threads = GemmCfg<BN, (AK >= kAQ4K), EPI>::kThreads;
+                  const GemmArgs& a, cudaStream_t st, int grid_ctas = 0) {
+    constexpr int smem = GemmCfg<BN, (AK >= kAQ4K), EPI, RESKB>::kSmemBytes;
+    constexpr int threads = GemmCfg<BN, (AK >= kAQ4K), EPI, RESKB>::kThreads;
     static bool attr[64] = {};  // per device
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
     if (!attr[dev]) {
-        CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<AK, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<AK, BN, EPI, RESKB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem));
         attr[dev] = true;
     }
     const int tiles = a.m_tiles * a.n_tiles;
-    dim3 g(std::max(1, std::min(tiles, num_sms(dev))));
-    CUDA_TRY(launch_pdl(gemm_kernel<AK, BN, EPI>, g, dim3(threads), smem, st, ta, tb, tr, to, ts, a));
+    dim3 g(grid_ctas > 0 ? grid_ctas : std::max(1, std::min(tiles, num_sms(dev))));
+    CUDA_TRY(launch_pdl(gemm_kernel<AK, BN, EPI, RESKB>, g, dim3(threads), smem, st, ta, tb, tr, to, ts, a));
     return VXB_OK;
 }
 
@@ -318,10 +319,19 @@ std::string gemm_kernel_name(const GemmOp& op);
 
 struct GemmOp {
     int akind = 0, epi = 0, bn = 16;
+    int reskb = 0;    // > 0: resident-A kernel (Q4_0), grid = res_grid CTAs, each on one m tile
+    int res_grid = 0;
     dim3 grid;
     CUtensorMap ta{}, tb{}, tr{}, to{}, ts{};  // ts: Q4_0 scales (a copy of ta for fp16 weights)
     GemmArgs args{};
     int launch(cudaStream_t st) const {
+        if (reskb == 6 && akind == kAQ4K && epi == kEpiPW && bn == 128)
+            return launch_gemm_t<kAQ4K, 128, kEpiPW, 6>(ta, tb, tr, to, ts, args, st, res_grid);
+        if (reskb == 6 && akind == kAQ4MN && epi == kEpiConvT && bn == 256)
+            return launch_gemm_t<kAQ4MN, 256, kEpiConvT, 6>(ta, tb, tr, to, ts, args, st, res_grid);
+        if (reskb == 3 && akind == kAQ4MN && epi == kEpiConvT && bn == 256)
+            return launch_gemm_t<kAQ4MN, 256, kEpiConvT, 3>(ta, tb, tr, to, ts, args, st, res_grid);
+        if (reskb) return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported resident-A GEMM");
         switch (akind * 2 + epi) {
             case kAF16K * 2 + kEpiPW: return launch_gemm_bn<kAF16K, kEpiPW>(bn, ta, tb, tr, ts, to, args, st);
             case kAQ4K * 2 + kEpiPW: return launch_gemm_bn<kAQ4K, kEpiPW>(bn, ta, tb, tr, ts, to, args, st);
@@ -333,7 +343,26 @@ struct GemmOp {
 };
 
 std::string gemm_kernel_name(const GemmOp& op) {
-    return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(op.epi) + ">";
+    return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(op.epi) +
+           (op.reskb ? ", " + std::to_string(op.reskb) : std::string()) + ">";
+}
+
+// Resident A (Q4_0 weights): worth it when every CTA runs several n tiles
+// of one m tile, so that its weight column is dequantised once instead of
+// once per tile; the column (K) must fit RESKB k blocks of shared memory.
+void choose_resident(GemmOp* op, int num_kb) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = num_sms(dev);
+    const GemmArgs& a = op->args;
+    const int per_m = sms / a.m_tiles;  // CTAs per m tile
+    if (per_m < 1 || int64_t(a.n_tiles) < 2LL * per_m) return;
+    int kb = 0;
+    if (op->akind == kAQ4K && op->epi == kEpiPW && op->bn == 128 && num_kb <= 6) kb = 6;
+    if (op->akind == kAQ4MN && op->epi == kEpiConvT && op->bn == 256 && num_kb <= 6) kb = num_kb <= 3 ? 3 : 6;
+    if (!kb) return;
+    op->reskb = kb;
+    op->res_grid = per_m * a.m_tiles;
 }
 
 // Pointwise conv GEMM: W [M rows][K] (F16, or Q4_0 rows padded to w.pitch), x fp16 [N][K].
@@ -375,7 +404,8 @@ int setup_pointwise(GemmOp* op, WView w, int K, int M, const void* x16, int64_t 
     } else if (w.type == VXB_TYPE_Q4_0) {
         if (K % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 pointwise needs K % 32 == 0");
         op->akind = kAQ4K;
-        // per k step: 2 blocks of nibbles (32 B) and their 2 scales (box of 8) for 128 rows
+        choose_resident(op, (K + 63) / 64);
+        // per k step: 2 blocks of nibbles (32 B) for 128 rows, and their scales (2 block rows of 128)
         rc = make_tmap_u8(&op->ta, w.p, w.pitch, M, kQ4KNibBox, 128);
         if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, K / 32, 128, kQ4KScaleRows);
         return rc;
@@ -444,7 +474,8 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     } else if (w.type == VXB_TYPE_Q4_0) {
         if (M % 32) return fail(VXB_ERR_INVALID_ARGUMENT, "Q4_0 convt needs 2s*Cout % 32 == 0");
         op->akind = kAQ4MN;
-        // per k step: up to 5 blocks of nibbles (80 B) and 16 scales around them for 64 rows
+        choose_resident(op, (Cin + 63) / 64);
+        // per k step: up to 5 blocks of nibbles (80 B) for 64 rows, and their scales (5 block rows of 64)
         rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kQ4MNNibBox, 64);
         if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M / 32, 64, kQ4MNScaleRows);
         return rc;

@@ -56,6 +56,10 @@ __global__ void head_kernel(const float* __restrict__ z, const float* __restrict
 // (causal padding; snake(0) == 0).  No shared memory.  The arithmetic per
 // output is that of the reference unit (audio-vae.cpp:1481-1518): taps in
 // order from the bias, one fma per tap and lane.  Requires C % 2 == 0.
+// Three blocks per SM (80 registers): each thread's run is a chain bound by
+// latency, so the SM's throughput grows with the threads it holds (at 96
+// registers, two blocks, the 192/96-channel stages took 162 us instead of
+// 152 at batch 256).
 __host__ __device__ inline long long res_pre_threads(int C, int T, int B, int d, int run) {
     const long long J = (T + d - 1) / d;  // outputs per phase (at most)
     return static_cast<long long>(C / 2) * B * d * ((J + run - 1) / run);
@@ -69,7 +73,7 @@ inline int res_pre_run(int C, int T, int B, int d, int sms) {
     return 7;
 }
 
-__global__ void __launch_bounds__(256) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
+__global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
                                                       const float* __restrict__ i1,
                                                       const float* __restrict__ w /*[C][7]*/,
                                                       const float* __restrict__ bias,

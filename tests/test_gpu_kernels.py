@@ -107,7 +107,10 @@ def test_pointwise_epilogues(vxb, wt, res, snk, out16):
 @pytest.mark.parametrize("wt", ["f16", "q4"])
 @pytest.mark.parametrize("Cin,Cout,s,B,T", [(1536, 768, 8, 1, 6), (768, 384, 8, 1, 48), (384, 192, 5, 1, 384),
                                             (192, 96, 2, 1, 1920), (384, 192, 5, 3, 7), (192, 96, 2, 2, 300),
-                                            (64, 32, 3, 2, 50), (128, 64, 4, 1, 1)])
+                                            (64, 32, 3, 2, 50), (128, 64, 4, 1, 1),
+                                            # enough token tiles for the tokens-as-M kernel (Q4_0), with
+                                            # sequence starts inside its 124-token tiles
+                                            (384, 192, 5, 8, 400), (192, 96, 2, 5, 2500)])
 def test_convt_matches_oracle(vxb, Cin, Cout, s, B, T, wt):
     rng = np.random.default_rng(Cin + s + T)
     K = 2 * s

@@ -23,6 +23,7 @@
 #include "encoder.cuh"
 #include "gemm.cuh"
 #include "resunit.cuh"
+#include "convt_tm.cuh"
 #include "gguf_reader.h"
 #include "vxb.h"
 
@@ -100,6 +101,25 @@ int make_tmap_plain(CUtensorMap* m, const void* base, bool f16, uint64_t inner, 
                      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (plain) failed: " + std::to_string(r));
+    return VXB_OK;
+}
+
+// 2-D fp32 tensor [outer][inner] with the 128-byte swizzle (box rows of 128 B).
+int make_tmap_f32_sw128(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                        uint32_t box_outer) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    const uint64_t row_bytes = inner * 4;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || box_inner * 4 != 128)
+        return fail(VXB_ERR_INVALID_ARGUMENT, "swizzled fp32 tensor needs 16-byte aligned rows and 128-byte boxes");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VXB_ERR_BACKEND, "cuTensorMapEncodeTiled (f32 sw128) failed: " + std::to_string(r));
     return VXB_OK;
 }
 
@@ -317,14 +337,35 @@ int launch_gemm_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const C
 struct GemmOp;
 std::string gemm_kernel_name(const GemmOp& op);
 
+template <int SS, int CPT>
+int launch_convt_tm_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& ty,
+                      const ConvTmArgs& a, int grid, cudaStream_t st) {
+    constexpr int smem = ConvTmCfg<SS, CPT>::kSmemBytes;
+    static bool attr[64] = {};  // per device
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
+    if (!attr[dev]) {
+        CUDA_TRY(cudaFuncSetAttribute(convt_tm_kernel<SS, CPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr[dev] = true;
+    }
+    CUDA_TRY(launch_pdl(convt_tm_kernel<SS, CPT>, dim3(grid), dim3(kTmThreads), smem, st, tx, tw, ts, ty, a));
+    return VXB_OK;
+}
+
 struct GemmOp {
     int akind = 0, epi = 0, bn = 16;
     int reskb = 0;    // > 0: resident-A kernel (Q4_0), grid = res_grid CTAs, each on one m tile
     int res_grid = 0;
+    int tm_s = 0;     // > 0: transposed conv with the tokens as M (convt_tm_kernel<tm_s, tm.cpt>)
+    ConvTmArgs tm{};
     dim3 grid;
     CUtensorMap ta{}, tb{}, tr{}, to{}, ts{};  // ts: Q4_0 scales (a copy of ta for fp16 weights)
     GemmArgs args{};
     int launch(cudaStream_t st) const {
+        if (tm_s == 2 && tm.cpt == 32) return launch_convt_tm_t<2, 32>(tb, ta, ts, to, tm, res_grid, st);
+        if (tm_s == 5 && tm.cpt == 16) return launch_convt_tm_t<5, 16>(tb, ta, ts, to, tm, res_grid, st);
+        if (tm_s) return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported tokens-as-M transposed conv");
         if (reskb == 6 && akind == kAQ4K && epi == kEpiPW && bn == 128)
             return launch_gemm_t<kAQ4K, 128, kEpiPW, 6>(ta, tb, tr, to, ts, args, st, res_grid);
         if (reskb == 6 && akind == kAQ4MN && epi == kEpiConvT && bn == 256)
@@ -343,6 +384,7 @@ struct GemmOp {
 };
 
 std::string gemm_kernel_name(const GemmOp& op) {
+    if (op.tm_s) return "convt_tm_kernel<" + std::to_string(op.tm_s) + ", " + std::to_string(op.tm.cpt) + ">";
     return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(op.epi) +
            (op.reskb ? ", " + std::to_string(op.reskb) : std::string()) + ">";
 }
@@ -437,6 +479,52 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     const int cpt = convt_cpt(s);
     if (cpt == 0) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: stride too large");
     op->epi = kEpiConvT;
+    if (w.type == VXB_TYPE_Q4_0 && skip == 0 && M % 32 == 0) {
+        // Long stages of stride 2 and 5: the tokens-as-M kernel (its epilogue
+        // needs no gather); every CTA keeps one j tile's dequantised weight
+        // column (K <= 384) and walks at least two token tiles.
+        const int tcpt = s == 2 ? 32 : s == 5 ? 16 : 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int sms = num_sms(dev);
+        const int j_tiles = tcpt ? Cout / tcpt : 0;
+        const int64_t n_tiles = (N + kTmTokens - 1) / kTmTokens;
+        const int per_j = j_tiles ? sms / j_tiles : 0;
+        if (tcpt && Cout % tcpt == 0 && Cin % 64 == 0 && Cin <= 64 * tm_max_kb(s) && per_j >= 1 &&
+            n_tiles >= 2LL * per_j && n_tiles < (int64_t(1) << 30) / j_tiles) {
+            op->tm_s = s;
+            ConvTmArgs& t = op->tm;
+            t = ConvTmArgs{};
+            t.K = Cin;
+            t.N = static_cast<int>(N);
+            t.T = T;
+            t.s = s;
+            t.cout = Cout;
+            t.cpt = tcpt;
+            t.j_tiles = j_tiles;
+            t.n_tiles = static_cast<int>(n_tiles);
+            t.bias = bias;
+            t.out = y;
+            t.status = status;
+            op->res_grid = per_j * j_tiles;
+            op->bn = 2 * s * tcpt;
+            int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, 32);
+            if (!rc) rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kQ4MNNibBox, 64);
+            if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M / 32, 64, kQ4MNScaleRows);
+            // output rows of 128 B (stride 2): one TMA store box of 31 tokens' rows per epilogue warp
+            if (!rc && tcpt * 4 == 128) rc = make_tmap_f32_sw128(&op->to, y, Cout, uint64_t(N) * s, tcpt, 31 * s);
+            if (tcpt * 4 != 128) op->to = op->tb;  // unused
+            // GemmArgs filled for the plan's bookkeeping (op info), not read by the kernel
+            op->args = GemmArgs{};
+            op->args.M = M;
+            op->args.K = Cin;
+            op->args.N = static_cast<int>(N);
+            op->args.s = s;
+            op->args.cout = Cout;
+            op->args.status = status;
+            return rc;
+        }
+    }
     const int m_tiles = (Cout + cpt - 1) / cpt;
     if (w.type == VXB_TYPE_Q4_0 && m_tiles >= 32) {
         // Q4_0 weights are dequantised once per (m tile, n tile): with many m

@@ -14,17 +14,17 @@
 // not the MMAs or HBM, sets the time.  Here the GEMM is transposed:
 //   D[token][j] = sum_ci x[token][ci] * W[ci][j],   j = co*2s + r
 // A = activations (fp16 [N][Cin], K-major, TMA), B = the weights of BN = 2s*cpt
-// columns j (MN-major; Q4_0 blocks TMA'd and dequantised once per CTA into a
-// resident column of shared memory, as the resident-A GEMM does), D in TMEM
+// columns j (Q4_0 blocks TMA'd and dequantised once per CTA into a resident,
+// K-major column of shared memory, as the resident-A GEMM does), D in TMEM
 // with one token per lane: a thread holds every tap of its token, and tap
 // s + r of token n - 1 is one __shfl_up from the lane below.  Each epilogue
 // warp's 32 TMEM lanes are fed by their own 32-row TMA box that starts one
 // token early (lane 0 is the previous warp's last token, the carry), so no
 // value crosses warps: 124 new tokens per 128-row tile, no shared memory and
-// no barrier in the epilogue.  Where an output row segment is 128 B (stride
-// 2, 32 couts) each warp stages its rows in shared memory and sends them with
-// one TMA store per tile (16-byte stores scattered one per output row cost
-// more than the rest of the kernel); otherwise 16-byte stores per row.
+// no barrier in the epilogue.  Each warp stages its tokens' output rows in
+// shared memory and sends them with one TMA store per tile: 16-byte stores
+// scattered one per output row (stride s*Cout*4 between lanes) cost more
+// than the rest of the kernel.
 //
 // Warp roles (512 threads): warp 0 lane 0 TMA producer; warp 1 TMEM owner,
 // lane 0 issues the MMAs; warps 4-7 / 8-11 two epilogue warpgroups (group g
@@ -56,22 +56,24 @@ struct ConvTmArgs {
     int* status;
 };
 
-// Shared memory: the resident weight column (KB k blocks of [64 k][BNW j]
-// MN-major SW128, BNW = BN rounded up to 64), then S stages of
-// {A tile [128 tokens][64 k] K-major SW128 (16 KB), raw Q4_0 blocks (6 KB)},
-// then (rows of 128 B: CPT = 32 fp32) one output staging buffer per
-// epilogue warp: its 31 tokens' 31*s output rows x CPT couts, 128-byte
-// swizzled, sent out by one TMA store per tile.
+// Shared memory: the resident weight column (KB k blocks of [BN j][64 k],
+// K-major SW128: the dequantisers transpose the MN-major Q4_0 blocks once
+// per CTA), then S stages of {A tile [128 tokens][64 k] K-major SW128 (16 KB),
+// raw Q4_0 blocks (6 KB)}, then one output staging buffer per epilogue warp:
+// its 31 tokens' 31*s output rows of 128 B (32 couts, 128-byte swizzle), sent
+// by one TMA store per tile (kStaged: stride 2).  At stride 5 (16 couts, rows
+// of 64 B) the staging would leave the mainloop two stages beside the 120 KB
+// weight column (measured slower, with all 8 warps on every tile and rows of
+// 32 B): its epilogue stores 16 bytes per output row directly.
 template <int SS, int CPT>
 struct ConvTmCfg {
     static constexpr int BN = 2 * SS * CPT;
-    static constexpr int kBNW = (BN + 63) / 64 * 64;
-    static constexpr int kBTile = kBNW * 64 * 2;           // one k block of the weight column
+    static constexpr int kBTile = BN * 128;                // one k block of the weight column
     static constexpr int kResBytes = tm_max_kb(SS) * kBTile;
     static constexpr int kATile = 128 * 64 * 2;            // 16 KB
     static constexpr int kRawBytes = 6144;                 // >= kQ4MNRawBytes
     static constexpr int kStageBytes = kATile + kRawBytes;
-    static constexpr bool kStaged = CPT * 4 == 128;        // output rows of 128 B: TMA stores
+    static constexpr bool kStaged = CPT * 4 == 128;
     static constexpr int kStgRows = 31 * SS;
     static constexpr int kStgWarpBytes = kStaged ? (kStgRows * 128 + 1023) / 1024 * 1024 : 0;
     static constexpr int kStgBytes = 8 * kStgWarpBytes;
@@ -82,7 +84,7 @@ struct ConvTmCfg {
     static constexpr int kTmemCols = 2 * kAccStride;
     static_assert(BN % 32 == 0 && BN <= 160, "j tiles of whole Q4_0 blocks, at most 5 per k row");
     static_assert(kStages >= 2, "pipeline needs two stages");
-    static_assert(!kStaged || kStgRows <= 256, "one TMA box per warp");
+    static_assert(kStgRows <= 256, "one TMA box per warp");
 };
 
 // tcgen05.ld of 32 lanes x 8 columns.
@@ -115,7 +117,6 @@ __device__ __forceinline__ void tm_ld8_nowait(uint32_t taddr, uint32_t* r) {
 __device__ __forceinline__ void tm_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tm_pin(uint32_t& x) { asm volatile("" : "+r"(x)); }
 
-constexpr int kTmG = 1;  // cout quads whose TMEM columns are loaded per wait (2 and 4 measured no faster)
 
 // SS = stride s, CPT = couts per j tile (BN = 2 * SS * CPT weight columns).
 template <int SS, int CPT>
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull_bar[i], 1);
-            mbar_init(&tempty_bar[i], 4);
+            mbar_init(&tempty_bar[i], 4);  // the 4 warps of the group that drains the accumulator
         }
         mbar_init(done_bar, 1);
         *abort_flag = 0;
@@ -222,9 +223,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
     } else if (warp >= 12) {
         // ------------------------------------------------- dequantisers --
-        // First tile only: k block kb of the weight column, MN-major SW128
-        // [64 k][BNW j] (64-column blocks 8 KB apart).  Item i -> k row
-        // kl = i % 64 and Q4_0 block bi = i / 64 of the BN / 32 in the row.
+        // First tile only: k block kb of the weight column, K-major SW128
+        // [BN j][64 k] (the B operand's layout).  Item i -> k row kl = i % 64
+        // and Q4_0 block bi = i / 64 of the BN / 32 in the row; its 32 values
+        // (consecutive j) are transposed into 32 two-byte stores, once per CTA.
         const int t = threadIdx.x - 384;
         const __half zero = __float2half_rn(0.f);
         for (int kb = 0; kb < num_kb && static_cast<int>(blockIdx.x) < num_tiles; ++kb) {
@@ -241,10 +243,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {  // word c: columns bi*32 + 8c .. + 7
-                    const int jl = bi * 32 + c * 8;
-                    const int hh = jl >> 6, mc = (jl & 63) >> 3;
-                    *reinterpret_cast<uint4*>(b_dst + hh * 8192 + (kl >> 3) * 1024 + (kl & 7) * 128 +
-                                              (((mc ^ kl) & 7) << 4)) = q4_dequant8_split(qw[c], d2);
+                    const uint4 h8 = q4_dequant8_split(qw[c], d2);
+                    const __half* hv = reinterpret_cast<const __half*>(&h8);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        *reinterpret_cast<__half*>(b_dst + sw128_kmajor_off(bi * 32 + c * 8 + e, kl)) = hv[e];
                 }
             }
             fence_proxy_async_smem();
@@ -255,8 +258,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------- MMA issuer --
-            // A K-major (tokens x k), B MN-major (weight columns contiguous).
-            constexpr uint32_t idesc = make_idesc_f16(128, BN, 0) | (1u << 16);
+            // A (tokens x k) and B (weight columns x k) both K-major.
+            constexpr uint32_t idesc = make_idesc_f16(128, BN, 0);
             int it = 0, tl = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tl) {
                 const int acc = tl & 1;
@@ -277,10 +280,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                     const uint32_t b_addr = smem_u32(resB + kb * Cfg::kBTile);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        // A: +32 B per 16 k inside the 128-B row; B: +2 KB per 16 k
-                        // (two 8-row k groups of 1 KB), 64-column blocks 8 KB apart (LBO)
+                        // K-major SW128: +32 B per 16 k inside the 128-B rows
                         const uint64_t adesc = make_sdesc(a_addr + kk * 32, 16, 1024);
-                        const uint64_t bdesc = make_sdesc(b_addr + kk * 2048, 8192, 1024);
+                        const uint64_t bdesc = make_sdesc(b_addr + kk * 32, 16, 1024);
                         umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
                     }
                     umma_commit(&empty_bar[st]);
@@ -292,21 +294,24 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
     } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------- epilogue --
-        // Group eg drains accumulator eg (the CTA's tiles eg, eg + 2, ...).
-        // Lane l of warp q holds token n = n0 + 31q + l - 1 (lane 0: the
-        // carry, whose taps s..2s-1 only feed lane 1).  Per 4 couts, the 8s
-        // columns co*2s + r come from TMEM; tap s + r of token n - 1 is one
-        // shuffle up; y = (tap r + b) + tap s + r of n - 1 (absent at a
-        // sequence start).  Rows of 128 B (kStaged): each warp writes its 31
-        // tokens' 31*s rows into its own swizzled buffer and sends them with
-        // one TMA store; otherwise one 16-byte store per output row.
+        // Lane l of warp q (TMEM quadrant q = warp % 4) holds token
+        // n = n0 + 31q + l - 1 (lane 0: the carry, whose taps s..2s-1 only
+        // feed lane 1).  Per 4 couts, the 8s columns co*2s + r come from TMEM;
+        // tap s + r of token n - 1 is one shuffle up; y = (tap r + b) + tap
+        // s + r of n - 1 (absent at a sequence start).  The warp writes its
+        // 31 tokens' rows into its staging buffer (row (l - 1)*s + r) and
+        // sends them with one TMA store per tile (kStaged), or stores each
+        // row's 16 bytes directly.  Group eg drains accumulator eg (the CTA's
+        // tiles eg, eg + 2, ...).
         const int eg = (warp - 4) >> 2;
         const int q = warp & 3;
-        const int co_lo = jt * CPT;  // the host requires Cout % CPT == 0
-        grid_dep_sync();             // the output may be a buffer the previous kernel still reads
+        const int co_lo = jt * CPT;                // the host requires Cout % CPT == 0
+        uint8_t* stg_w = stg + (warp - 4) * Cfg::kStgWarpBytes;
+        grid_dep_sync();                           // the output may be a buffer the previous kernel still reads
         int tl = eg;
         for (int tile = blockIdx.x + eg * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, tl += 2) {
-            const bool ok = mbar_wait(&tfull_bar[eg], (tl >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
+            const int acc = eg;
+            const bool ok = mbar_wait(&tfull_bar[acc], (tl >> 1) & 1, abort_flag, args.status, kErrWaitAccum);
             if (__any_sync(0xffffffffu, !ok)) break;
             tc_fence_after();
             const int n0 = (tile / args.j_tiles) * kTmTokens;
@@ -314,38 +319,23 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             const bool tok = lane >= 1 && n < args.N;
             const bool seq_start = tok && n % args.T == 0;
             float* orow = args.out + (static_cast<size_t>(tok ? n : 0) * SS) * args.cout + co_lo;  // row n*s
-            uint8_t* stg_w = stg + (warp - 4) * Cfg::kStgWarpBytes;
+            const uint32_t t_row = tmem_base + acc * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
             if (Cfg::kStaged) {
-                // this warp's store of its previous tile has read the buffer
-                if (lane == 0) bulk_wait_read<0>();
+                if (lane == 0) bulk_wait_read<0>();  // the warp's store of its previous tile has read the buffer
                 __syncwarp();
             }
-            const uint32_t t_row = tmem_base + eg * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
-            constexpr int G = (8 * SS * kTmG > 80) ? (kTmG > 2 ? 2 : kTmG) : kTmG;  // <= 80 loaded columns
-            static_assert((CPT / 4) % G == 0, "quads per load group");
 #pragma unroll 1
-            for (int cq0 = 0; cq0 < CPT / 4; cq0 += G) {
-              uint32_t vr[G][8 * SS];
+            for (int cq = 0; cq < CPT / 4; ++cq) {
+                uint32_t vr[8 * SS];
 #pragma unroll
-              for (int g = 0; g < G; ++g) {
+                for (int c = 0; c + 16 <= 8 * SS; c += 16) tm_ld16_nowait(t_row + cq * 8 * SS + c, vr + c);
+                if ((8 * SS) % 16) tm_ld8_nowait(t_row + cq * 8 * SS + (8 * SS) / 16 * 16, vr + (8 * SS) / 16 * 16);
+                tm_ld_wait();
 #pragma unroll
-                for (int c = 0; c + 16 <= 8 * SS; c += 16) tm_ld16_nowait(t_row + (cq0 + g) * 8 * SS + c, vr[g] + c);
-                if ((8 * SS) % 16)
-                    tm_ld8_nowait(t_row + (cq0 + g) * 8 * SS + (8 * SS) / 16 * 16, vr[g] + (8 * SS) / 16 * 16);
-              }
-              tm_ld_wait();
-#pragma unroll
-              for (int g = 0; g < G; ++g) {
-#pragma unroll
-                for (int c = 0; c < 8 * SS; ++c) tm_pin(vr[g][c]);
-              }
-#pragma unroll
-              for (int g = 0; g < G; ++g) {
-                const int cq = cq0 + g;
+                for (int c = 0; c < 8 * SS; ++c) tm_pin(vr[c]);
                 float v[8 * SS];
 #pragma unroll
-                for (int c = 0; c < 8 * SS; ++c) v[c] = __uint_as_float(vr[g][c]);
-                const bool on = tok && co_lo + cq * 4 < args.cout;
+                for (int c = 0; c < 8 * SS; ++c) v[c] = __uint_as_float(vr[c]);
                 const float4 bq = __ldg(reinterpret_cast<const float4*>(args.bias + co_lo) + cq);
 #pragma unroll
                 for (int r = 0; r < SS; ++r) {
@@ -368,17 +358,17 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                         // row (lane - 1)*s + r of the box, chunk cq (128-byte swizzle)
                         const uint32_t row = static_cast<uint32_t>((lane - 1) * SS + r);
                         if (lane >= 1)
-                            *reinterpret_cast<float4*>(stg_w + row * 128u + (((static_cast<uint32_t>(cq) ^ row) & 7u) << 4)) = y;
-                    } else if (on) {
+                            *reinterpret_cast<float4*>(stg_w + row * 128u +
+                                                       (((static_cast<uint32_t>(cq) ^ row) & 7u) << 4)) = y;
+                    } else if (tok) {
                         *reinterpret_cast<float4*>(orow + r * args.cout + cq * 4) = y;
                     }
                 }
-              }
             }
-            // accumulator fully read: the MMAs of tile tl + 2 may reuse it
+            // accumulator read: the MMAs of tile tl + 2 may reuse it
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[eg]);
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
             if (Cfg::kStaged) {
                 fence_proxy_async_smem();
                 __syncwarp();

@@ -511,7 +511,8 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
             int rc = make_tmap_f16(&op->tb, x16, Cin, N, uint64_t(Cin) * 2, 64, 32);
             if (!rc) rc = make_tmap_u8(&op->ta, w.p, w.pitch, Cin, kQ4MNNibBox, 64);
             if (!rc) rc = make_tmap_plain(&op->ts, w.s, true, uint64_t(w.spitch) / 2, M / 32, 64, kQ4MNScaleRows);
-            // output rows of 128 B (stride 2): one TMA store box of 31 tokens' rows per epilogue warp
+            // stride 2: one TMA store box of 31 tokens' output rows (32 couts, 128-byte
+            // swizzle) per epilogue warp; stride 5 stores directly
             if (!rc && tcpt * 4 == 128) rc = make_tmap_f32_sw128(&op->to, y, Cout, uint64_t(N) * s, tcpt, 31 * s);
             if (tcpt * 4 != 128) op->to = op->tb;  // unused
             // GemmArgs filled for the plan's bookkeeping (op info), not read by the kernel

@@ -490,7 +490,9 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
         const int j_tiles = tcpt ? Cout / tcpt : 0;
         const int64_t n_tiles = (N + kTmTokens - 1) / kTmTokens;
         const int per_j = j_tiles ? sms / j_tiles : 0;
-        if (tcpt && Cout % tcpt == 0 && Cin % 64 == 0 && Cin <= 64 * tm_max_kb(s) && per_j >= 1 &&
+        // (stride 5 stores 32 bytes per output row: a 32-byte aligned output)
+        const bool out_ok = s == 2 || (Cout % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 31) == 0);
+        if (tcpt && out_ok && Cout % tcpt == 0 && Cin % 64 == 0 && Cin <= 64 * tm_max_kb(s) && per_j >= 1 &&
             n_tiles >= 2LL * per_j && n_tiles < (int64_t(1) << 30) / j_tiles) {
             op->tm_s = s;
             ConvTmArgs& t = op->tm;

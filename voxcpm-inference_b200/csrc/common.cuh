@@ -152,6 +152,13 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_
                  : "memory");
 }
 
+// One 32-byte global store (sm_100: st.global.v8; p 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(float* p, const float4& a, const float4& b) {
+    asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(a.x), "f"(a.y), "f"(a.z),
+                 "f"(a.w), "f"(b.x), "f"(b.y), "f"(b.z), "f"(b.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int x, int y, int z) {

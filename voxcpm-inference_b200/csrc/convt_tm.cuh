@@ -118,12 +118,6 @@ __device__ __forceinline__ void tm_ld8_nowait(uint32_t taddr, uint32_t* r) {
 __device__ __forceinline__ void tm_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tm_pin(uint32_t& x) { asm volatile("" : "+r"(x)); }
 
-// One 32-byte global store (sm_100: st.global.v8; p 32-byte aligned).
-__device__ __forceinline__ void st_global_v8(float* p, const float4& a, const float4& b) {
-    asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(a.x), "f"(a.y), "f"(a.z),
-                 "f"(a.w), "f"(b.x), "f"(b.y), "f"(b.z), "f"(b.w)
-                 : "memory");
-}
 
 
 // SS = stride s, CPT = couts per j tile (BN = 2 * SS * CPT weight columns).

@@ -51,6 +51,8 @@ struct GemmArgs {
     int s, cout, cpt, seq_len;  // ConvT: stride, Cout, couts per tile, frames per sequence
     int skip;                 // ConvT: leading input frames per sequence whose outputs are not written
                               // (a streaming window's history row); output rows shift down by skip*s
+    int v8;                   // ConvT: cpt == 8, Cout % 8 == 0, output 32-byte aligned: one 32-byte
+                              // store per output row (both cout quads of a row on one thread)
     int* status;              // device status word (bounded-wait failures)
 };
 
@@ -544,7 +546,8 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                 int rco[8];                             // (phase << 16) | cout offset of each quad, -1 if none
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    const int qd = ew + 4 * k;
+                    // v8 (qpr == 2): quads k = 2i, 2i + 1 are couts 0-3 and 4-7 of phase ew + 4i
+                    const int qd = args.v8 ? (ew + 4 * (k >> 1)) * 2 + (k & 1) : ew + 4 * k;
                     const int r = qd / qpr;
                     const int co = (qd - r * qpr) * 4;
                     const bool on = qd < nquads && co < cpt;
@@ -574,6 +577,32 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                         float* orow = out + orow_n * s * args.cout + co_lo;  // y row (n*s + 0)
                         const float* sgl = sG + 4 + lane;
                         const int rs = 2 * s * Cfg::kEpiLD;                                  // next cout
+                        if (args.v8) {
+#pragma unroll
+                            for (int k = 0; k < 8; k += 2) {
+                                if (rco[k] < 0) continue;  // (quads k, k + 1 exist together)
+                                const int r = rco[k] >> 16;
+                                float4 y2[2];
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    const float* pa = sgl + ((4 * h) * 2 * s + r) * Cfg::kEpiLD;  // D[co*2s + r][c]
+                                    const float* pb = pa + s * Cfg::kEpiLD - 1;  // D[co*2s + s + r][c - 1]
+                                    float4 y;
+                                    y.x = pa[0] + bq[k + h].x;
+                                    y.y = pa[rs] + bq[k + h].y;
+                                    y.z = pa[2 * rs] + bq[k + h].z;
+                                    y.w = pa[3 * rs] + bq[k + h].w;
+                                    if (!seq_start) {
+                                        y.x += pb[0];
+                                        y.y += pb[rs];
+                                        y.z += pb[2 * rs];
+                                        y.w += pb[3 * rs];
+                                    }
+                                    y2[h] = y;
+                                }
+                                st_global_v8(orow + r * args.cout, y2[0], y2[1]);
+                            }
+                        } else {
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
                             if (rco[k] < 0) continue;
@@ -593,6 +622,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                                 y.w += pb[3 * rs];
                             }
                             *reinterpret_cast<float4*>(orow + r * args.cout + co) = y;
+                        }
                         }
                     }
                     epi_bar(bar_id);

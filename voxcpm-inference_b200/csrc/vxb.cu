@@ -556,6 +556,7 @@ int setup_convt(GemmOp* op, WView w, int Cin, int Cout, int s, const void* x16, 
     a.cpt = cpt;
     a.seq_len = T;
     a.skip = skip;
+    a.v8 = cpt == 8 && Cout % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 31) == 0;
     a.status = status;
     if (w.type == VXB_TYPE_F16) {
         if ((uint64_t(M) * 2) % 16) return fail(VXB_ERR_INVALID_ARGUMENT, "convt: 2s*Cout must be a multiple of 8");

@@ -154,53 +154,35 @@ __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict
 // Final conv: y[b][t] = tanh(bias + sum_{c,k} w[c][k] * s[b*T + t + k - 6][c])
 // over the (already Snake-activated) last stage, held in fp16 (the reference
 // rounds this conv's input to fp16 in its im2col + F16 mul_mat,
-// audio-vae.cpp:218-234).  A block covers kFinTT time steps of one
-// sequence: rows [t0 - 6, t0 + kFinTT) are staged in shared memory as fp32
-// from 16-byte loads.  Each warp then computes 8 consecutive outputs
-// at once: lane = channel quad, the 14 rows they read are loaded once, every
-// lane accumulates its channels' share of all 8 sums, and one exchange of
-// halves (xor 16, 8, 4) followed by xor 2, 1 leaves each sum complete on four
-// lanes (9 shuffles for 8 outputs).  Requires C % 8 == 0 and C <= 128.
-constexpr int kFinTT = 64;
+// audio-vae.cpp:218-234).  A block covers tt (64 or 128) time steps of one
+// sequence: rows [t0 - 6, t0 + tt) are copied into shared memory as
+// they are (fp16) by cp.async, rows before the sequence start zero-filled,
+// with no register staging (the taps and the sums are all a thread holds).
+// Each warp then computes 8 consecutive outputs at a time: lane = channel
+// quad, the 14 rows they read are loaded once (8 bytes, widened to fp32),
+// every lane accumulates its channels' share of all 8 sums, and one
+// exchange of halves (xor 16, 8, 4) followed by xor 2, 1 leaves each sum
+// complete on four lanes (9 shuffles for 8 outputs).  The kernel is
+// issue-bound: the products are paired FMAs (fma.rn.f32x2), the even and
+// odd channels of a quad summed in the two halves.  Requires C % 8 == 0 and
+// C <= 128.
+// Shared memory of final_kernel: tt + 6 rows of C fp16 channels.
+__host__ __device__ inline size_t final_smem_bytes(int C, int tt) { return size_t(tt + 6) * C * 2; }
 
 // t_off: s holds T + t_off rows per sequence, the first t_off a streaming
 // window's history; y holds T outputs per sequence (output t reads rows up to t + t_off).
 __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
-                                                    float bias, float* __restrict__ y, int C, int T, int t_off) {
-    extern __shared__ float4 fsh4[];  // [(kFinTT + 6)][C/4]
-    const int c4n = C / 4;
-    const int t0 = blockIdx.x * kFinTT;
+                                                    float bias, float* __restrict__ y, int C, int T, int t_off,
+                                                    int tt) {
+    extern __shared__ uint4 fsh16[];  // [tt + 6][C] fp16, 8 channels per 16 bytes
+    const int c8n = C / 8, c4n = C / 4;
+    const int t0 = blockIdx.x * tt;
     const int b = blockIdx.y;
-    const int rows = min(kFinTT, T - t0) + 6;
+    const int rows = min(tt, T - t0) + 6;
     const __half* sb = s + static_cast<long long>(b) * (T + t_off) * C + static_cast<long long>(t_off) * C;
-    if (threadIdx.x * 32 < C * 7) prefetch_l2(w + threadIdx.x * 32);  // taps: constant, into L2 before the wait
-    grid_dep_sync();
-    // 16-byte loads of 8 fp16 channels, widened to two float4 in shared memory
-    const int c8n = C / 8;
-    constexpr int kMaxLd = ((kFinTT + 6) * 16 + 255) / 256;  // 8-channel groups per thread for C <= 128
-    uint4 v[kMaxLd];
-#pragma unroll
-    for (int j = 0; j < kMaxLd; ++j) {  // every load issued before any is stored
-        const int i = threadIdx.x + j * 256;
-        const int r = i / c8n, cq = i - r * c8n;
-        const int t = t0 - 6 + r;
-        v[j] = (i < rows * c8n && t >= -t_off) ? __ldg(reinterpret_cast<const uint4*>(sb + static_cast<long long>(t) * C) + cq)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int j = 0; j < kMaxLd; ++j) {
-        const int i = threadIdx.x + j * 256;
-        if (i < rows * c8n) {
-            const __half2* h = reinterpret_cast<const __half2*>(&v[j]);
-            const float2 a = __half22float2(h[0]), b2 = __half22float2(h[1]);
-            const float2 c2 = __half22float2(h[2]), d2 = __half22float2(h[3]);
-            fsh4[2 * i] = make_float4(a.x, a.y, b2.x, b2.y);
-            fsh4[2 * i + 1] = make_float4(c2.x, c2.y, d2.x, d2.y);
-        }
-    }
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // each lane owns channel quad `lane` (C <= 128)
+    // each lane owns channel quad `lane` (C <= 128); the taps are constant:
+    // read before the grid dependency wait
     float4 wk[7];
     const bool lv = lane < c4n;
 #pragma unroll
@@ -209,25 +191,47 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
         wk[k] = lv ? make_float4(w[(cc + 0) * 7 + k], w[(cc + 1) * 7 + k], w[(cc + 2) * 7 + k], w[(cc + 3) * 7 + k])
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const int q0 = warp * 8;  // this warp's outputs q0..q0+7 (smem rows q0..q0+13)
-    if (t0 + q0 >= T) return;
-    float acc[8];
+    grid_dep_sync();
+    for (int i = threadIdx.x; i < rows * c8n; i += 256) {
+        const int r = i / c8n, cq = i - r * c8n;
+        const int t = t0 - 6 + r;
+        const bool valid = t >= -t_off;  // rows before the sequence start are the causal zero padding
+        cp_async16(&fsh16[i], valid ? static_cast<const void*>(sb + static_cast<long long>(t) * C + cq * 8)
+                                    : static_cast<const void*>(sb),
+                   valid ? 16u : 0u);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const uint2* fq = reinterpret_cast<const uint2*>(fsh16);  // [row][channel quad], 4 fp16 each
+#pragma unroll 1
+    for (int grp = 0; grp < tt / 64; ++grp) {
+    const int q0 = warp * (tt / 8) + grp * 8;  // this group's outputs q0..q0+7 (smem rows q0..q0+13)
+    if (t0 + q0 >= T) break;
+    // paired FMAs: channels (0, 1) and (2, 3) of the quad accumulate in the
+    // two lanes of a float2, added at the end
+    float2 acc2[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 8; ++j) acc2[j] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < 14; ++r) {
-        const float4 u = (lv && q0 + r < rows) ? fsh4[(q0 + r) * c4n + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+        if (lv && q0 + r < rows) {
+            const uint2 hq = fq[(q0 + r) * c4n + lane];
+            lo = __half22float2(*reinterpret_cast<const __half2*>(&hq.x));
+            hi = __half22float2(*reinterpret_cast<const __half2*>(&hq.y));
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int k = r - j;  // tap of row q0 + r for output q0 + j
             if (k >= 0 && k < 7) {
-                acc[j] = fmaf(u.x, wk[k].x, acc[j]);
-                acc[j] = fmaf(u.y, wk[k].y, acc[j]);
-                acc[j] = fmaf(u.z, wk[k].z, acc[j]);
-                acc[j] = fmaf(u.w, wk[k].w, acc[j]);
+                acc2[j] = ffma2(lo, make_float2(wk[k].x, wk[k].y), acc2[j]);
+                acc2[j] = ffma2(hi, make_float2(wk[k].z, wk[k].w), acc2[j]);
             }
         }
     }
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = acc2[j].x + acc2[j].y;
     // exchange halves: after xor 16 a lane keeps 4 sums (outputs 0-3 or 4-7),
     // after xor 8 two, after xor 4 one
     const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
@@ -255,6 +259,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
     const int j = (h16 ? 4 : 0) + (h8 ? 2 : 0) + (h4 ? 1 : 0);  // output this lane's sum belongs to
     const int t = t0 + q0 + j;
     if ((lane & 3) == 0 && t < T) y[static_cast<long long>(b) * T + t] = tanhf(sum + bias);
+    }
 }
 
 // Failure probe: one thread waits on an mbarrier that nothing ever arrives

@@ -729,6 +729,12 @@ int launch_res_pre(const float* x, const float* a1, const float* i1, const float
     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("prologue launch: ") + cudaGetErrorString(e));
 }
 
+// Final-conv tile: 128 time steps per block on long stages, 64 where that
+// leaves fewer than two blocks per SM (short streaming steps).
+int final_tile(int B, int T, int sms) {
+    return int64_t(B) * ((T + 127) / 128) >= 2LL * sms ? 128 : 64;
+}
+
 int grid_1d(int64_t work, int threads) {
     const int64_t b = (work + threads - 1) / threads;
     return static_cast<int>(std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 32));
@@ -1421,9 +1427,10 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
             const int Tq = Tb, Bq = B;
             rc = sink.kernel(
                 [=](cudaStream_t s) {
-                    dim3 grid((Tq + kFinTT - 1) / kFinTT, Bq);
-                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), sizeof(float) * (kFinTT + 6) * C,
-                                                     s, sx, w, fb, o, C, Tq, 0);
+                    const int tt = final_tile(Bq, Tq, sms);
+                    dim3 grid((Tq + tt - 1) / tt, Bq);
+                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), final_smem_bytes(C, tt),
+                                                     s, sx, w, fb, o, C, Tq, 0, tt);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
                 {"final_conv", 14.0 * C * double(n), double(n) * C * 2 + double(n) * 4, "final_kernel"});
@@ -2415,9 +2422,10 @@ int emit_stream_push(vxb_stream* st, int p, OpSink& sink) {
             const int Tq = static_cast<int>(m);
             rc = sink.kernel(
                 [=](cudaStream_t s) {
-                    dim3 grid((Tq + kFinTT - 1) / kFinTT, 1);
-                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), sizeof(float) * (kFinTT + 6) * C, s,
-                                                     sx, w, fb, o, C, Tq, 6);
+                    const int tt = final_tile(1, Tq, sms);
+                    dim3 grid((Tq + tt - 1) / tt, 1);
+                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), final_smem_bytes(C, tt), s,
+                                                     sx, w, fb, o, C, Tq, 6, tt);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
                 {"final_conv", 14.0 * C * double(m), double(m) * C * 2, "final_kernel"});

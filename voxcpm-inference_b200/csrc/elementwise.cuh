@@ -212,14 +212,20 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
     float2 acc2[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc2[j] = make_float2(0.f, 0.f);
+    // branch-free rows: every lane reads inside the tt + 6 staged rows (lanes
+    // past the channel quads read quad 0, rows past `rows` read stale data)
+    // and selects zero where the value is not used
+    const int lq = lv ? lane : 0;
 #pragma unroll
     for (int r = 0; r < 14; ++r) {
-        float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-        if (lv && q0 + r < rows) {
-            const uint2 hq = fq[(q0 + r) * c4n + lane];
-            lo = __half22float2(*reinterpret_cast<const __half2*>(&hq.x));
-            hi = __half22float2(*reinterpret_cast<const __half2*>(&hq.y));
-        }
+        const bool use = lv && q0 + r < rows;
+        const uint2 hq = fq[(q0 + r) * c4n + lq];
+        float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&hq.x));
+        float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hq.y));
+        lo.x = use ? lo.x : 0.f;
+        lo.y = use ? lo.y : 0.f;
+        hi.x = use ? hi.x : 0.f;
+        hi.y = use ? hi.y : 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int k = r - j;  // tap of row q0 + r for output q0 + j

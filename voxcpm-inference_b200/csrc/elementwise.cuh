@@ -192,10 +192,12 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     grid_dep_sync();
-    for (int i = threadIdx.x; i < rows * c8n; i += 256) {
+    for (int i = threadIdx.x; i < (tt + 6) * c8n; i += 256) {
         const int r = i / c8n, cq = i - r * c8n;
         const int t = t0 - 6 + r;
-        const bool valid = t >= -t_off;  // rows before the sequence start are the causal zero padding
+        // rows before the sequence start (the causal zero padding) and past
+        // the tile's last row are zero-filled
+        const bool valid = t >= -t_off && r < rows;
         cp_async16(&fsh16[i], valid ? static_cast<const void*>(sb + static_cast<long long>(t) * C + cq * 8)
                                     : static_cast<const void*>(sb),
                    valid ? 16u : 0u);
@@ -212,20 +214,15 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
     float2 acc2[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc2[j] = make_float2(0.f, 0.f);
-    // branch-free rows: every lane reads inside the tt + 6 staged rows (lanes
-    // past the channel quads read quad 0, rows past `rows` read stale data)
-    // and selects zero where the value is not used
+    // branch-free rows: every lane reads inside the tt + 6 staged rows (rows
+    // past the tile are zero); lanes past the channel quads read quad 0 and
+    // their sums are dropped before the reduction
     const int lq = lv ? lane : 0;
 #pragma unroll
     for (int r = 0; r < 14; ++r) {
-        const bool use = lv && q0 + r < rows;
         const uint2 hq = fq[(q0 + r) * c4n + lq];
-        float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&hq.x));
-        float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hq.y));
-        lo.x = use ? lo.x : 0.f;
-        lo.y = use ? lo.y : 0.f;
-        hi.x = use ? hi.x : 0.f;
-        hi.y = use ? hi.y : 0.f;
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&hq.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hq.y));
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int k = r - j;  // tap of row q0 + r for output q0 + j
@@ -237,7 +234,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
     }
     float acc[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = acc2[j].x + acc2[j].y;
+    for (int j = 0; j < 8; ++j) acc[j] = lv ? acc2[j].x + acc2[j].y : 0.f;
     // exchange halves: after xor 16 a lane keeps 4 sums (outputs 0-3 or 4-7),
     // after xor 8 two, after xor 4 one
     const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;

@@ -12,6 +12,8 @@
 //                    unit entry points.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace vxb {
@@ -73,6 +75,10 @@ inline int res_pre_run(int C, int T, int B, int d, int sms) {
     return 7;
 }
 
+// KW = false (the usual case): the thread index and every row offset inside
+// one sequence fit 32 bits (the host checks), so the index arithmetic and the
+// per-load / per-store address arithmetic are 32-bit; KW = true: 64-bit.
+template <bool KW>
 __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict__ x, const float* __restrict__ a1,
                                                       const float* __restrict__ i1,
                                                       const float* __restrict__ w /*[C][7]*/,
@@ -80,17 +86,18 @@ __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict
                                                       const float* __restrict__ a2,
                                                       const float* __restrict__ i2, __half* __restrict__ out,
                                                       int C, int T, int B, int d, int run, int t_off) {
+    using idx_t = typename std::conditional<KW, long long, int>::type;
     // T outputs per sequence; x holds T + t_off rows per sequence, the first
     // t_off of them a streaming window's history (output t reads row t + t_off)
     const int Tx = T + t_off;
     const int Q = C >> 1;
     const int J = (T + d - 1) / d;
     const int R = (J + run - 1) / run;
-    const long long total = static_cast<long long>(Q) * B * d * R;
-    const long long i = blockIdx.x * 256LL + threadIdx.x;
+    const idx_t total = static_cast<idx_t>(Q) * B * d * R;
+    const idx_t i = static_cast<idx_t>(blockIdx.x) * 256 + static_cast<idx_t>(threadIdx.x);
     const bool active = i < total;
     const int q = active ? static_cast<int>(i % Q) : 0;
-    long long r = i / Q;
+    idx_t r = i / Q;
     const int jr = static_cast<int>(r % R);
     r /= R;
     const int phase = static_cast<int>(r % d);
@@ -111,9 +118,11 @@ __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict
     const float* xb = x + static_cast<long long>(b) * Tx * C + static_cast<long long>(t_off) * C + c;
     __half* ob = out + static_cast<long long>(b) * T * C + c;
     const int t_first = phase + (jr * run - 6) * d;  // row m of the run is t_first + m*d
+    // rows -t_off .. T - 1 exist (one unsigned compare); rows before are the causal zero padding
     auto load = [&](int t) {
-        return (t >= -t_off && t < T) ? __ldg(reinterpret_cast<const float2*>(xb + static_cast<long long>(t) * C))
-                                      : make_float2(0.f, 0.f);
+        return static_cast<unsigned>(t + t_off) < static_cast<unsigned>(Tx)
+                   ? __ldg(reinterpret_cast<const float2*>(xb + static_cast<idx_t>(t) * C))
+                   : make_float2(0.f, 0.f);
     };
     // window slot of row m is m % 7; rows 0..5 are the warm-up (before the first output)
     float2 win[7];
@@ -145,7 +154,7 @@ __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict
             const int t = tg + s * d;
             if (t < T) {
                 const float2 y = snake2(acc, al2, iv2);
-                *reinterpret_cast<__half2*>(ob + static_cast<long long>(t) * C) = __floats2half2_rn(y.x, y.y);
+                *reinterpret_cast<__half2*>(ob + static_cast<idx_t>(t) * C) = __floats2half2_rn(y.x, y.y);
             }
         }
     }
@@ -192,8 +201,10 @@ __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     grid_dep_sync();
-    for (int i = threadIdx.x; i < (tt + 6) * c8n; i += 256) {
-        const int r = i / c8n, cq = i - r * c8n;
+    // thread -> 16-byte chunk cq = tid % 16 of rows tid / 16, + 16 per step (C <= 128: c8n <= 16)
+    const int cq = threadIdx.x & 15;
+    for (int r = threadIdx.x >> 4; r < tt + 6 && cq < c8n; r += 16) {
+        const int i = r * c8n + cq;
         const int t = t0 - 6 + r;
         // rows before the sequence start (the causal zero padding) and past
         // the tile's last row are zero-filled

@@ -717,6 +717,16 @@ int setup_resunit(ResUnitOp* op, const void* w, int w_type, int C, int d, const 
     return make_tmap_x3d(&op->ty, y, C, T, B, 32, true);
 }
 
+// Whether a prologue launch needs 64-bit index arithmetic: its thread count
+// (rounded to whole blocks) or a sequence's rows x channels reach 2^31.
+bool res_pre_wide(int C, int B, int T, int d, int t_off, int sms) {
+    const long long threads = res_pre_threads(C, T, B, d, res_pre_run(C, T, B, d, sms));
+    return (threads + 255) / 256 * 256 >= (1LL << 31) || static_cast<long long>(T + t_off) * C >= (1LL << 31);
+}
+std::string res_pre_kernel_name(int C, int B, int T, int d, int t_off, int sms) {  // as ncu names it
+    return res_pre_wide(C, B, T, d, t_off, sms) ? "res_pre_kernel<true>" : "res_pre_kernel<false>";
+}
+
 // Residual-unit prologue over x [B][T][C] -> h fp16, dilation d.
 int launch_res_pre(const float* x, const float* a1, const float* i1, const float* dw, const float* db, const float* a2,
                    const float* i2, __half* h, int C, int B, int T, int d, int sms, cudaStream_t s, int t_off = 0) {
@@ -724,8 +734,9 @@ int launch_res_pre(const float* x, const float* a1, const float* i1, const float
     const int run = res_pre_run(C, T, B, d, sms);
     const long long threads = res_pre_threads(C, T, B, d, run);
     if (threads > (1LL << 40)) return fail(VXB_ERR_INVALID_ARGUMENT, "prologue: too many threads");
-    const cudaError_t e = launch_pdl(res_pre_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
-                                     s, x, a1, i1, dw, db, a2, i2, h, C, T, B, d, run, t_off);
+    const cudaError_t e = launch_pdl(res_pre_wide(C, B, T, d, t_off, sms) ? res_pre_kernel<true> : res_pre_kernel<false>,
+                                     dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, s, x, a1, i1,
+                                     dw, db, a2, i2, h, C, T, B, d, run, t_off);
     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, std::string("prologue launch: ") + cudaGetErrorString(e));
 }
 
@@ -1361,7 +1372,7 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                               sms, s);
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(n) * C * 20.0,
-                     double(n) * C * (4 + 2) + C * 11 * 4, "res_pre_kernel"});
+                     double(n) * C * (4 + 2) + C * 11 * 4, res_pre_kernel_name(C, B, Tb, dl, 0, sms)});
                 if (rc) return rc;
             }
             if (resunit_hg_fits(C) && int64_t(B) * ((Tb + kRuTT - 1) / kRuTT) >= sms) {
@@ -1619,7 +1630,7 @@ int emit_encode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                                               sms, s);
                     },
                     {"res_pre_" + nm, double(n) * C * 20.0, double(n) * C * (4 + 2) + C * 11 * 4,
-                     "res_pre_kernel"});
+                     res_pre_kernel_name(C, B, Lb, dl, 0, sms)});
                 if (rc) return rc;
             }
             if (resunit_hg_fits(C) && int64_t(B) * ((Lb + kRuTT - 1) / kRuTT) >= sms) {
@@ -2392,7 +2403,7 @@ int emit_stream_push(vxb_stream* st, int p, OpSink& sink) {
                                               sms, s, 6 * dl);
                     },
                     {"res_pre_b" + std::to_string(bi) + "u" + std::to_string(r), double(m) * C * 20.0,
-                     double(m) * C * 6, "res_pre_kernel"});
+                     double(m) * C * 6, res_pre_kernel_name(C, 1, static_cast<int>(m), dl, 6 * dl, sms)});
                 if (rc) return rc;
             }
             GemmOp op;

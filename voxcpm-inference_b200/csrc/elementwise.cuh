@@ -141,8 +141,18 @@ __global__ void __launch_bounds__(256, 3) res_pre_kernel(const float* __restrict
 #pragma unroll
         for (int s = 0; s < 7; ++s) cur[s] = nxt[s];
         if (g + 7 < run) {  // the next group's rows, loaded while this one computes
+            const int tn = tg + 7 * d;  // its first row
+            if (static_cast<unsigned>(tn + t_off) < static_cast<unsigned>(Tx) &&
+                static_cast<unsigned>(tn + 6 * d + t_off) < static_cast<unsigned>(Tx)) {
+                // all 7 rows inside the sequence (the usual case): no per-row checks
+                const float* pn = xb + static_cast<idx_t>(tn) * C;
+                const idx_t dC = static_cast<idx_t>(d) * C;
 #pragma unroll
-            for (int s = 0; s < 7; ++s) nxt[s] = load(tg + (7 + s) * d);
+                for (int s = 0; s < 7; ++s) nxt[s] = __ldg(reinterpret_cast<const float2*>(pn + s * dC));
+            } else {
+#pragma unroll
+                for (int s = 0; s < 7; ++s) nxt[s] = load(tn + s * d);
+            }
         }
 #pragma unroll
         for (int s = 0; s < 7; ++s) {
@@ -180,9 +190,14 @@ __host__ __device__ inline size_t final_smem_bytes(int C, int tt) { return size_
 
 // t_off: s holds T + t_off rows per sequence, the first t_off a streaming
 // window's history; y holds T outputs per sequence (output t reads rows up to t + t_off).
+// CT > 0: the channel count as a compile-time constant (shared-memory
+// offsets become immediates; 96 is the VoxCPM decoder's last stage); CT = 0
+// takes it from the argument.
+template <int CT>
 __global__ void __launch_bounds__(256) final_kernel(const __half* __restrict__ s, const float* __restrict__ w /*[C][7]*/,
-                                                    float bias, float* __restrict__ y, int C, int T, int t_off,
+                                                    float bias, float* __restrict__ y, int c_arg, int T, int t_off,
                                                     int tt) {
+    const int C = CT > 0 ? CT : c_arg;
     extern __shared__ uint4 fsh16[];  // [tt + 6][C] fp16, 8 channels per 16 bytes
     const int c8n = C / 8, c4n = C / 4;
     const int t0 = blockIdx.x * tt;

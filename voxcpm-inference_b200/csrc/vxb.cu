@@ -1440,11 +1440,13 @@ int emit_decode(vxb_ctx* c, const DecodeBufs& d, int B, int T, OpSink& sink) {
                 [=](cudaStream_t s) {
                     const int tt = final_tile(Bq, Tq, sms);
                     dim3 grid((Tq + tt - 1) / tt, Bq);
-                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), final_smem_bytes(C, tt),
+                    const cudaError_t e = launch_pdl(C == 96 ? final_kernel<96> : final_kernel<0>, grid, dim3(256),
+                                                     final_smem_bytes(C, tt),
                                                      s, sx, w, fb, o, C, Tq, 0, tt);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
-                {"final_conv", 14.0 * C * double(n), double(n) * C * 2 + double(n) * 4, "final_kernel"});
+                {"final_conv", 14.0 * C * double(n), double(n) * C * 2 + double(n) * 4,
+                 C == 96 ? "final_kernel<96>" : "final_kernel<0>"});
             if (rc) return rc;
         }
     }
@@ -2435,11 +2437,13 @@ int emit_stream_push(vxb_stream* st, int p, OpSink& sink) {
                 [=](cudaStream_t s) {
                     const int tt = final_tile(1, Tq, sms);
                     dim3 grid((Tq + tt - 1) / tt, 1);
-                    const cudaError_t e = launch_pdl(final_kernel, grid, dim3(256), final_smem_bytes(C, tt), s,
+                    const cudaError_t e = launch_pdl(C == 96 ? final_kernel<96> : final_kernel<0>, grid, dim3(256),
+                                                     final_smem_bytes(C, tt), s,
                                                      sx, w, fb, o, C, Tq, 6, tt);
                     return e == cudaSuccess ? VXB_OK : fail(VXB_ERR_BACKEND, "final launch");
                 },
-                {"final_conv", 14.0 * C * double(m), double(m) * C * 2, "final_kernel"});
+                {"final_conv", 14.0 * C * double(m), double(m) * C * 2,
+                 C == 96 ? "final_kernel<96>" : "final_kernel<0>"});
             if (rc) return rc;
             seg_rows(S.wf, O.wf, m, 6, C, 2);
         }

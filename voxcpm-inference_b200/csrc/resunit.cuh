@@ -71,7 +71,8 @@ constexpr int kRuMaxRows = kRuTT + 6 * 9;  // slice rows for dilation <= 9
 constexpr int kRuThreads = 480;
 constexpr int kRuSlotBytes = kRuMaxRows * kRuSlice * 4;  // 182 rows x 128 B
 constexpr int kRuBoxBytes = kRuTT * kRuSlice * 4;        // 128 rows x 128 B
-constexpr int kRuNE = 3;                                 // residual boxes in flight
+constexpr int kRuNE = 3;                                 // residual boxes in flight (fused kernel)
+constexpr int kRuMaxNE = 6;                              // HG: as many as shared memory holds, up to 6
 constexpr int kRuNH = 2;                                 // H buffers
 constexpr int kRuMaxSlots = 4;
 constexpr int kRuBarBytes = 256;
@@ -79,10 +80,11 @@ constexpr int kRuSmemLimit = 227 * 1024;
 
 // Shared-memory layout for C channels (W, H, E 1024-byte aligned):
 //   W  KB k-blocks of [C rows][128 B]   H  2 x KB k-blocks of [128 rows][128 B]
-//   E  kRuNE residual boxes             P  per-channel parameters (12 C floats)
+//   E  ne residual boxes                P  per-channel parameters (12 C floats)
 //   X  slots of [182 rows][128 B]
 struct RuLayout {
     int kb, w_bytes, h_off, e_off, p_off, x_off, bar_off, slots, total;
+    int ne;  // residual boxes in flight
 };
 
 // hg: the H tiles come from global memory (the pointwise-only variant), no
@@ -93,7 +95,15 @@ __host__ __device__ inline RuLayout ru_layout(int C, bool hg = false) {
     L.w_bytes = L.kb * C * 128;
     L.h_off = L.w_bytes;
     L.e_off = L.h_off + kRuNH * L.kb * kRuTT * 128;
-    L.p_off = L.e_off + kRuNE * kRuBoxBytes;
+    // HG: the residual ring is what keeps the loads ahead of the epilogue (one
+    // box less in flight made the unit 40 % slower), so where the room left
+    // holds kRuMaxNE boxes it takes them (96 channels, batch 256: 182 -> 162 us
+    // per unit); otherwise, and in the fused kernel, 3.  The kernel takes the
+    // count as a template argument (a run-time modulo on the ring index cost
+    // the 192-channel and Snake-output units 2-5 %).
+    L.ne = kRuNE;
+    if (hg && (kRuSmemLimit - 1024 - kRuBarBytes - L.e_off) / kRuBoxBytes >= kRuMaxNE) L.ne = kRuMaxNE;
+    L.p_off = L.e_off + L.ne * kRuBoxBytes;
     L.x_off = L.p_off + (hg ? 0 : (12 * C * 4 + 127) / 128 * 128);
     const int room = kRuSmemLimit - 1024 - kRuBarBytes - L.x_off;
     L.slots = hg ? 0 : room / kRuSlotBytes;
@@ -138,13 +148,14 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // output [B*T][C]) arrive by TMA (tmap_h, boxes {64 k, 128 tokens}, 128-byte
 // swizzle) into the H buffers, issued by the loader warp; the producer warps
 // idle.  Everything else is the same kernel.
-template <int EPI, bool HG>
+template <int EPI, bool HG, int NE>
 __global__ void __launch_bounds__(kRuThreads, 1)
     resunit_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_res,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_h,
                    const ResUnitArgs args) {
     const int C = args.C;
-    const RuLayout L = ru_layout(C, HG);
+    static_assert(NE >= 1 && NE <= kRuMaxNE, "residual ring");
+    const RuLayout L = ru_layout(C, HG);  // L.ne == NE (the host picks the instance)
     const int NS = L.slots;
     extern __shared__ uint8_t ru_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ru_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,9 +174,9 @@ __global__ void __launch_bounds__(kRuThreads, 1)
     float* sI2 = sA2 + C;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [NS] slice landed (TMA bytes)
     uint64_t* empty = full + kRuMaxSlots;                            // [NS] slice consumed (8 producer warps)
-    uint64_t* efull = empty + kRuMaxSlots;                           // [NE] residual box landed
-    uint64_t* eempty = efull + kRuNE;                                // [NE] residual box released
-    uint64_t* hfull = eempty + kRuNE;                                // [NH] H written (8 producer warps)
+    uint64_t* efull = empty + kRuMaxSlots;                           // [ne] residual box landed
+    uint64_t* eempty = efull + kRuMaxNE;                             // [ne] residual box released
+    uint64_t* hfull = eempty + kRuMaxNE;                             // [NH] H written (8 producer warps)
     uint64_t* hempty = hfull + kRuNH;                                // [NH] H read by the MMAs
     uint64_t* afull = hempty + kRuNH;                                // [2] accumulator complete
     uint64_t* aempty = afull + 2;                                    // [2] accumulator drained (4 warps)
@@ -184,7 +195,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
-        for (int i = 0; i < kRuNE; ++i) {
+        for (int i = 0; i < NE; ++i) {
             mbar_init(&efull[i], 1);
             mbar_init(&eempty[i], 4);  // one arrival per epilogue warp
         }
@@ -301,8 +312,8 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 const int t0 = (tile - b * args.t_tiles) * kRuTT;
                 bool ok = true;
                 for (int j = 0; j < nslices; ++j, ++g) {
-                    const int e = g % kRuNE;
-                    if (!mbar_wait(&eempty[e], ((g / kRuNE) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) {
+                    const int e = g % NE;
+                    if (!mbar_wait(&eempty[e], ((g / NE) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) {
                         ok = false;
                         break;
                     }
@@ -486,13 +497,13 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&aempty[acc]);
                 }
-                const bool landed = mbar_wait(&efull[g % kRuNE], (g / kRuNE) & 1, abort_flag, args.status,
+                const bool landed = mbar_wait(&efull[g % NE], (g / NE) & 1, abort_flag, args.status,
                                               kErrWaitFull);
                 if (__any_sync(0xffffffffu, !landed)) {
                     ok = false;
                     break;
                 }
-                uint8_t* box = sE + (g % kRuNE) * kRuBoxBytes;
+                uint8_t* box = sE + (g % NE) * kRuBoxBytes;
                 uint8_t* own = box + q * 32 * 128;  // this warp's rows (4 KB, 1024-byte aligned)
                 uint2 h16[8];
 #pragma unroll
@@ -529,7 +540,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                 if (lane == 0) {
                     // the warp's store of box g - 1 has read its rows: release that box
                     bulk_wait_read<0>();
-                    if (g > 0) mbar_arrive(&eempty[(g - 1) % kRuNE]);
+                    if (g > 0) mbar_arrive(&eempty[(g - 1) % NE]);
                     // rows past the sequence end fall outside the tensor and are not written
                     tma_store_3d(&tmap_y, own, c0, t0 + q * 32, b);
                     bulk_commit();

@@ -602,7 +602,7 @@ int make_tmap_x3d(CUtensorMap* m, const void* base, uint64_t C, uint64_t T, uint
     return VXB_OK;
 }
 
-template <int EPI, bool HG>
+template <int EPI, bool HG, int NE>
 int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtensorMap& ty, const CUtensorMap& th,
                      const ResUnitArgs& a, int grid, cudaStream_t st) {
     static bool attr[64] = {};  // per device
@@ -610,12 +610,14 @@ int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtenso
     CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
     if (!attr[dev]) {
-        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI, HG, NE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kRuSmemLimit));
         attr[dev] = true;
     }
-    const size_t smem = static_cast<size_t>(ru_layout(a.C, HG).total);
-    CUDA_TRY(launch_pdl(resunit_kernel<EPI, HG>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, th, a));
+    const RuLayout L = ru_layout(a.C, HG);
+    if (L.ne != NE) return fail(VXB_ERR_BACKEND, "residual unit: ring size mismatch");
+    const size_t smem = static_cast<size_t>(L.total);
+    CUDA_TRY(launch_pdl(resunit_kernel<EPI, HG, NE>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, th, a));
     return VXB_OK;
 }
 
@@ -625,18 +627,28 @@ struct ResUnitOp {
     CUtensorMap tx{}, tr{}, ty{}, th{};
     ResUnitArgs args{};
     int launch(cudaStream_t st) const {
-        switch (epi * 2 + (hg ? 1 : 0)) {
-            case kResPlain * 2: return launch_resunit_t<kResPlain, false>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF16 * 2: return launch_resunit_t<kResSnakeF16, false>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF32 * 2: return launch_resunit_t<kResSnakeF32, false>(tx, tr, ty, th, args, grid, st);
-            case kResPlain * 2 + 1: return launch_resunit_t<kResPlain, true>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF16 * 2 + 1: return launch_resunit_t<kResSnakeF16, true>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF32 * 2 + 1: return launch_resunit_t<kResSnakeF32, true>(tx, tr, ty, th, args, grid, st);
+        const bool deep = hg && ru_layout(args.C, true).ne == kRuMaxNE;  // deep residual ring
+        switch (epi * 4 + (hg ? 2 : 0) + (deep ? 1 : 0)) {
+            case kResPlain * 4: return launch_resunit_t<kResPlain, false, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 4: return launch_resunit_t<kResSnakeF16, false, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 4: return launch_resunit_t<kResSnakeF32, false, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResPlain * 4 + 2: return launch_resunit_t<kResPlain, true, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 4 + 2:
+                return launch_resunit_t<kResSnakeF16, true, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 4 + 2:
+                return launch_resunit_t<kResSnakeF32, true, kRuNE>(tx, tr, ty, th, args, grid, st);
+            case kResPlain * 4 + 3: return launch_resunit_t<kResPlain, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 4 + 3:
+                return launch_resunit_t<kResSnakeF16, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 4 + 3:
+                return launch_resunit_t<kResSnakeF32, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
             default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported fused residual unit");
         }
     }
     std::string kernel_name() const {
-        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "1" : "0") + ">";  // as ncu names it
+        const int ne = hg ? ru_layout(args.C, true).ne : kRuNE;
+        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "1" : "0") + ", " + std::to_string(ne) +
+               ">";  // as ncu names it
     }
 };
 

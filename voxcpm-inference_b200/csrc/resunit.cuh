@@ -85,16 +85,19 @@ constexpr int kRuSmemLimit = 227 * 1024;
 struct RuLayout {
     int kb, w_bytes, h_off, e_off, p_off, x_off, bar_off, slots, total;
     int ne;  // residual boxes in flight
+    int nh;  // H buffers
 };
 
 // hg: the H tiles come from global memory (the pointwise-only variant), no
-// parameters or slices.
-__host__ __device__ inline RuLayout ru_layout(int C, bool hg = false) {
+// parameters or slices.  nh: H buffers (2, or 1 for the pointwise-only units
+// that ru_nh picks; a compile-time constant in the kernel).
+__host__ __device__ inline RuLayout ru_layout(int C, bool hg = false, int nh = kRuNH) {
     RuLayout L;
     L.kb = (C + 63) / 64;
     L.w_bytes = L.kb * C * 128;
     L.h_off = L.w_bytes;
-    L.e_off = L.h_off + kRuNH * L.kb * kRuTT * 128;
+    L.nh = nh;
+    L.e_off = L.h_off + nh * L.kb * kRuTT * 128;
     // HG: the residual ring is what keeps the loads ahead of the epilogue (one
     // box less in flight made the unit 40 % slower), so where the room left
     // holds kRuMaxNE boxes it takes them (96 channels, batch 256: 182 -> 162 us
@@ -111,6 +114,16 @@ __host__ __device__ inline RuLayout ru_layout(int C, bool hg = false) {
     L.bar_off = L.x_off + (L.slots > 0 ? L.slots : 0) * kRuSlotBytes;
     L.total = L.bar_off + kRuBarBytes + 1024;
     return L;
+}
+
+// H buffers of a unit.  A pointwise-only unit with the plain epilogue whose
+// two H buffers leave no room for kRuMaxNE residual boxes (C > 128) keeps one:
+// the loader refills it as soon as the tile's MMAs have read it, and the next
+// MMAs also wait for the epilogue to drain an accumulator, which takes longer
+// (192 channels, batch 256: 189 -> 163 us per unit).  The Snake epilogues keep
+// two H buffers and 3 boxes there (measured 182 us against 190 with one).
+inline int ru_nh(int C, bool hg, int epi) {
+    return hg && epi == kResPlain && ru_layout(C, true).ne < kRuMaxNE ? 1 : kRuNH;
 }
 
 // Byte offset of (row, channel c < 32) in a residual box: rows of 128 B with
@@ -148,14 +161,14 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // output [B*T][C]) arrive by TMA (tmap_h, boxes {64 k, 128 tokens}, 128-byte
 // swizzle) into the H buffers, issued by the loader warp; the producer warps
 // idle.  Everything else is the same kernel.
-template <int EPI, bool HG, int NE>
+template <int EPI, bool HG, int NE, int NH>
 __global__ void __launch_bounds__(kRuThreads, 1)
     resunit_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_res,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_h,
                    const ResUnitArgs args) {
     const int C = args.C;
-    static_assert(NE >= 1 && NE <= kRuMaxNE, "residual ring");
-    const RuLayout L = ru_layout(C, HG);  // L.ne == NE (the host picks the instance)
+    static_assert(NE >= 1 && NE <= kRuMaxNE && NH >= 1 && NH <= kRuNH && (NH == kRuNH || HG), "rings");
+    const RuLayout L = ru_layout(C, HG, NH);  // L.ne == NE (the host picks the instance)
     const int NS = L.slots;
     extern __shared__ uint8_t ru_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ru_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -199,7 +212,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             mbar_init(&efull[i], 1);
             mbar_init(&eempty[i], 4);  // one arrival per epilogue warp
         }
-        for (int i = 0; i < kRuNH; ++i) {
+        for (int i = 0; i < NH; ++i) {
             mbar_init(&hfull[i], HG ? 1 : 8);
             mbar_init(&hempty[i], 1);
         }
@@ -269,8 +282,9 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             if (HG) {
                 int i = 0;
                 for (int tile = blockIdx.x; tile < args.tiles && !*abort_flag; tile += gridDim.x, ++i) {
-                    const int hbuf = i & 1;
-                    if (!mbar_wait(&hempty[hbuf], ((i >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitEmpty)) break;
+                    const int hbuf = i % NH;
+                    const uint32_t hph = (i / NH) & 1;
+                    if (!mbar_wait(&hempty[hbuf], hph ^ 1, abort_flag, args.status, kErrWaitEmpty)) break;
                     const int b = tile / args.t_tiles;
                     const int t0 = (tile - b * args.t_tiles) * kRuTT;
                     mbar_arrive_expect_tx(&hfull[hbuf], static_cast<uint32_t>(L.kb) * kRuTT * 128);
@@ -445,11 +459,13 @@ __global__ void __launch_bounds__(kRuThreads, 1)
             int i = 0;
             for (int tile = blockIdx.x; tile < args.tiles; tile += gridDim.x, ++i) {
                 const int acc = i & 1;
+                const int hbuf = i % NH;
+                const uint32_t hph = (i / NH) & 1;
                 if (!mbar_wait(&aempty[acc], ((i >> 1) & 1) ^ 1, abort_flag, args.status, kErrWaitAccum)) break;
-                if (!mbar_wait(&hfull[acc], (i >> 1) & 1, abort_flag, args.status, kErrWaitFull)) break;
+                if (!mbar_wait(&hfull[hbuf], hph, abort_flag, args.status, kErrWaitFull)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * acc_cols;
-                const uint32_t h_addr = smem_u32(sH + acc * L.kb * (kRuTT * 128));
+                const uint32_t h_addr = smem_u32(sH + hbuf * L.kb * (kRuTT * 128));
                 const uint32_t w_addr = smem_u32(sW);
                 for (int k16 = 0; k16 < C / 16; ++k16) {
                     const int kb = k16 >> 2, kk = k16 & 3;
@@ -457,7 +473,7 @@ __global__ void __launch_bounds__(kRuThreads, 1)
                     const uint64_t bdesc = make_sdesc(w_addr + kb * (C * 128) + kk * 32, 16, 1024);
                     umma_f16(d_tmem, adesc, bdesc, idesc, k16 != 0);
                 }
-                umma_commit(&hempty[acc]);
+                umma_commit(&hempty[hbuf]);
                 umma_commit(&afull[acc]);
             }
         }

@@ -602,7 +602,7 @@ int make_tmap_x3d(CUtensorMap* m, const void* base, uint64_t C, uint64_t T, uint
     return VXB_OK;
 }
 
-template <int EPI, bool HG, int NE>
+template <int EPI, bool HG, int NE, int NH>
 int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtensorMap& ty, const CUtensorMap& th,
                      const ResUnitArgs& a, int grid, cudaStream_t st) {
     static bool attr[64] = {};  // per device
@@ -610,14 +610,14 @@ int launch_resunit_t(const CUtensorMap& tx, const CUtensorMap& tr, const CUtenso
     CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(VXB_ERR_BACKEND, "device index out of range");
     if (!attr[dev]) {
-        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI, HG, NE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CUDA_TRY(cudaFuncSetAttribute(resunit_kernel<EPI, HG, NE, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kRuSmemLimit));
         attr[dev] = true;
     }
-    const RuLayout L = ru_layout(a.C, HG);
-    if (L.ne != NE) return fail(VXB_ERR_BACKEND, "residual unit: ring size mismatch");
+    const RuLayout L = ru_layout(a.C, HG, NH);
+    if (L.ne != NE || ru_nh(a.C, HG, EPI) != NH) return fail(VXB_ERR_BACKEND, "residual unit: ring size mismatch");
     const size_t smem = static_cast<size_t>(L.total);
-    CUDA_TRY(launch_pdl(resunit_kernel<EPI, HG, NE>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, th, a));
+    CUDA_TRY(launch_pdl(resunit_kernel<EPI, HG, NE, NH>, dim3(grid), dim3(kRuThreads), smem, st, tx, tr, ty, th, a));
     return VXB_OK;
 }
 
@@ -627,28 +627,35 @@ struct ResUnitOp {
     CUtensorMap tx{}, tr{}, ty{}, th{};
     ResUnitArgs args{};
     int launch(cudaStream_t st) const {
-        const bool deep = hg && ru_layout(args.C, true).ne == kRuMaxNE;  // deep residual ring
-        switch (epi * 4 + (hg ? 2 : 0) + (deep ? 1 : 0)) {
-            case kResPlain * 4: return launch_resunit_t<kResPlain, false, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF16 * 4: return launch_resunit_t<kResSnakeF16, false, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF32 * 4: return launch_resunit_t<kResSnakeF32, false, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResPlain * 4 + 2: return launch_resunit_t<kResPlain, true, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF16 * 4 + 2:
-                return launch_resunit_t<kResSnakeF16, true, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResSnakeF32 * 4 + 2:
-                return launch_resunit_t<kResSnakeF32, true, kRuNE>(tx, tr, ty, th, args, grid, st);
-            case kResPlain * 4 + 3: return launch_resunit_t<kResPlain, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
+        // rings (residual boxes, H buffers): the fused unit (3, 2); pointwise-only
+        // (6, 2) for C <= 128, above that (6, 1) plain and (3, 2) with Snake
+        const int nh = ru_nh(args.C, hg, epi);
+        const int ne = ru_layout(args.C, hg, nh).ne;
+        const int ring = !hg ? 0 : (ne == kRuMaxNE ? (nh == kRuNH ? 1 : 2) : 3);
+        switch (epi * 4 + ring) {
+            case kResPlain * 4: return launch_resunit_t<kResPlain, false, kRuNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 4:
+                return launch_resunit_t<kResSnakeF16, false, kRuNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 4:
+                return launch_resunit_t<kResSnakeF32, false, kRuNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResPlain * 4 + 1:
+                return launch_resunit_t<kResPlain, true, kRuMaxNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF16 * 4 + 1:
+                return launch_resunit_t<kResSnakeF16, true, kRuMaxNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResSnakeF32 * 4 + 1:
+                return launch_resunit_t<kResSnakeF32, true, kRuMaxNE, kRuNH>(tx, tr, ty, th, args, grid, st);
+            case kResPlain * 4 + 2: return launch_resunit_t<kResPlain, true, kRuMaxNE, 1>(tx, tr, ty, th, args, grid, st);
             case kResSnakeF16 * 4 + 3:
-                return launch_resunit_t<kResSnakeF16, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
+                return launch_resunit_t<kResSnakeF16, true, kRuNE, kRuNH>(tx, tr, ty, th, args, grid, st);
             case kResSnakeF32 * 4 + 3:
-                return launch_resunit_t<kResSnakeF32, true, kRuMaxNE>(tx, tr, ty, th, args, grid, st);
+                return launch_resunit_t<kResSnakeF32, true, kRuNE, kRuNH>(tx, tr, ty, th, args, grid, st);
             default: return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported fused residual unit");
         }
     }
     std::string kernel_name() const {
-        const int ne = hg ? ru_layout(args.C, true).ne : kRuNE;
-        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "1" : "0") + ", " + std::to_string(ne) +
-               ">";  // as ncu names it
+        const int nh = ru_nh(args.C, hg, epi);
+        return "resunit_kernel<" + std::to_string(epi) + ", " + (hg ? "1" : "0") + ", " +
+               std::to_string(ru_layout(args.C, hg, nh).ne) + ", " + std::to_string(nh) + ">";  // as ncu names it
     }
 };
 

@@ -37,6 +37,8 @@ enum AKind : int {
 enum Epi : int {
     kEpiPW = 0,     // y[n][m] = acc + b[m] (+ r[n][m]) [-> snake]  -> fp32 or fp16
     kEpiConvT = 1,  // y[(n*s + r)][co] = D[co*2s + r][n] + D[co*2s + s + r][n-1] + b[co]
+    kEpiPW32 = 2,   // as kEpiPW with fp32 output only (resident-A kernels): no fp16 staging
+                    // buffers, their room spent on a residual ring twice as deep
 };
 
 struct GemmArgs {
@@ -91,7 +93,8 @@ struct GemmCfg {
     static constexpr int kBK = 64;
     static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kRawBytes = Q4 ? 6144 : 0;  // >= max(kQ4KRawBytes, kQ4MNRawBytes), 1 KB granular
+    // >= max(kQ4KRawBytes, kQ4MNRawBytes), 1 KB granular; kEpiPW32 (K-major only): >= kQ4KRawBytes
+    static constexpr int kRawBytes = Q4 ? (EPI == kEpiPW32 ? 5120 : 6144) : 0;
     static constexpr int kResABytes = RESKB * kABytes;
     static constexpr int kBOff = RESKB ? 0 : kABytes;            // B tile within a stage
     static constexpr int kStageBytes = kBOff + kBBytes + kRawBytes;
@@ -102,18 +105,23 @@ struct GemmCfg {
     // PW: residual / output chunk buffers per group; loads run kEpiAhead
     // chunks ahead.  Narrow tiles (one or two tiles per CTA on short
     // sequences) take a ring of 2 and spend the room on mainloop stages.
-    static constexpr int kEpiRing = (BN <= 64 || RESKB) ? 2 : 4;
+    // kEpiPW32 keeps a ring of 4 with the resident A (2 chunks ahead: the
+    // residual loads were the epilogue's wait at a ring of 2).
+    static constexpr int kEpiRing = EPI == kEpiPW32 ? 4 : ((BN <= 64 || RESKB) ? 2 : 4);
     static constexpr int kEpiAhead = kEpiRing / 2;
     static constexpr int kGroupEpiBytes =
-        EPI == kEpiConvT ? 128 * kEpiLD * 4 : kEpiRing * kResBytes + kEpiRing * kOut16Bytes;
+        EPI == kEpiConvT ? 128 * kEpiLD * 4 : kEpiRing * kResBytes + (EPI == kEpiPW ? kEpiRing * kOut16Bytes : 0);
     static constexpr int kEpiBytes = 2 * kGroupEpiBytes;         // two epilogue warpgroups
-    static constexpr int kBudget = 220 * 1024 - kEpiBytes - 1024 - kBarrierBytes - kResABytes;
+    static constexpr int kBudget =
+        (EPI == kEpiPW32 ? 227 : 220) * 1024 - kEpiBytes - 1024 - kBarrierBytes - kResABytes;
     static constexpr int kStagesFit = kBudget / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);   // two accumulators
     static constexpr int kAccStride = BN < 32 ? 32 : BN;
     static constexpr int kSmemBytes = kResABytes + kStages * kStageBytes + kEpiBytes + 1024 + kBarrierBytes;
     static_assert(RESKB == 0 || Q4, "resident A is for Q4_0 weights");
+    static_assert(EPI != kEpiPW32 || !Q4 || kRawBytes >= kQ4KRawBytes, "fp32-output kernel: Q4_0 K-major raw blocks");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
     static_assert((4 * kStages + 12) * 8 + 8 <= kBarrierBytes, "barrier area too small");
     static constexpr int kDqWarps = 4;                           // Q4_0: dequantiser warps (one per SM sub-partition)
     static constexpr int kThreads = Q4 ? 384 + 32 * kDqWarps : 384;
@@ -131,6 +139,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
     constexpr bool kRes = RESKB > 0;
     using Cfg = GemmCfg<BN, kQ4, EPI, RESKB>;
     static_assert(EPI == kEpiConvT || (BN >= 32 && BN <= 128), "pointwise tiles are 32..128 tokens wide");
+    constexpr bool kPW = EPI != kEpiConvT;  // kEpiPW or kEpiPW32
     constexpr int S = Cfg::kStages;
 
     extern __shared__ uint8_t smem_raw[];
@@ -174,7 +183,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         prefetch_tmap(&tmap_b);
         prefetch_tmap(&tmap_a);
         if (kQ4) prefetch_tmap(&tmap_scale);
-        if (EPI == kEpiPW) {
+        if (kPW) {
             prefetch_tmap(&tmap_out);
             if (args.res) prefetch_tmap(&tmap_res);
         }
@@ -244,7 +253,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         const int tile = blockIdx.x + ((warp - 4) >> 2) * gridDim.x;
         if (tile < num_tiles) {
             const int mt = tile % args.m_tiles, qq = warp & 3;
-            if (EPI == kEpiPW) {
+            if (kPW) {
                 const int m = mt * Cfg::kBM + qq * 32;
                 if (m < args.M) {
                     prefetch_l2(args.bias + m);
@@ -444,7 +453,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
         // chunk g is processed, once the store of chunk g - A has read its
         // buffer; the first A go out before the group's first accumulator is
         // complete.
-        constexpr int CPT = EPI == kEpiPW ? BN / Cfg::kChunk : 1;
+        constexpr int CPT = kPW ? BN / Cfg::kChunk : 1;
         auto issue_res = [&](int gl) {  // residual chunk gl of this group's sequence, if any
             const int tt = blockIdx.x + (eg + 2 * (gl / CPT)) * gridDim.x;
             if (tt >= num_tiles) return;
@@ -453,7 +462,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
             tma_load_2d(sG + jb * (Cfg::kResBytes / 4), &tmap_res, &rbar[jb], (tt % args.m_tiles) * Cfg::kBM,
                         (tt / args.m_tiles) * BN + (gl % CPT) * Cfg::kChunk);
         };
-        if (EPI == kEpiPW && args.res != nullptr && et == 0) {
+        if (kPW && args.res != nullptr && et == 0) {
             for (int l = 0; l < Cfg::kEpiAhead; ++l) issue_res(l);
         }
         if (kQ4 && dq_help) dequant(kDqThreads + threadIdx.x - 128, dq_threads);
@@ -470,7 +479,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
             const uint32_t t_row = tmem_base + acc * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
             const int mt = tile % args.m_tiles;
             const int nt = tile / args.m_tiles;
-            if (EPI == kEpiPW) {
+            if (kPW) {
                 // The result is written in place (fp32) or to the chunk's fp16
                 // buffer, and a TMA store sends it out.  Chunks past N load
                 // zeros and store nothing (TMA clips).
@@ -508,7 +517,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                         for (int i = 0; i < 16; ++i) {
                             float y = v[i] + b + r[i];
                             if (args.snake_alpha) y = snake(y, al, iv);
-                            if (args.out_f16) {
+                            if (EPI == kEpiPW && args.out_f16) {
                                 obuf[i * 128 + row] = __float2half_rn(y);
                             } else {
                                 rbuf[i * 128 + row] = y;
@@ -521,7 +530,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
                         break;
                     }
                     if (et == 0) {
-                        tma_store_2d(&tmap_out, args.out_f16 ? static_cast<const void*>(obuf) : rbuf, m0,
+                        tma_store_2d(&tmap_out, (EPI == kEpiPW && args.out_f16) ? static_cast<const void*>(obuf) : rbuf, m0,
                                      n_start + ch * Cfg::kChunk);
                         bulk_commit();
                     }
@@ -633,7 +642,7 @@ __global__ void __launch_bounds__((AK >= kAQ4K) ? 384 + 32 * GemmCfg<BN, true, E
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
             if (!ok) break;
         }
-        if (EPI == kEpiPW && et == 0) bulk_wait_all();  // stores done before the CTA's smem goes away
+        if (kPW && et == 0) bulk_wait_all();  // stores done before the CTA's smem goes away
     }
 
     tc_fence_before();

@@ -367,7 +367,8 @@ struct GemmOp {
         if (tm_s == 5 && tm.cpt == 16) return launch_convt_tm_t<5, 16>(tb, ta, ts, to, tm, res_grid, st);
         if (tm_s) return fail(VXB_ERR_INVALID_ARGUMENT, "unsupported tokens-as-M transposed conv");
         if (reskb == 6 && akind == kAQ4K && epi == kEpiPW && bn == 128)
-            return launch_gemm_t<kAQ4K, 128, kEpiPW, 6>(ta, tb, tr, to, ts, args, st, res_grid);
+            return args.out_f16 ? launch_gemm_t<kAQ4K, 128, kEpiPW, 6>(ta, tb, tr, to, ts, args, st, res_grid)
+                                : launch_gemm_t<kAQ4K, 128, kEpiPW32, 6>(ta, tb, tr, to, ts, args, st, res_grid);
         if (reskb == 6 && akind == kAQ4MN && epi == kEpiConvT && bn == 256)
             return launch_gemm_t<kAQ4MN, 256, kEpiConvT, 6>(ta, tb, tr, to, ts, args, st, res_grid);
         if (reskb == 3 && akind == kAQ4MN && epi == kEpiConvT && bn == 256)
@@ -385,7 +386,9 @@ struct GemmOp {
 
 std::string gemm_kernel_name(const GemmOp& op) {
     if (op.tm_s) return "convt_tm_kernel<" + std::to_string(op.tm_s) + ", " + std::to_string(op.tm.cpt) + ">";
-    return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(op.epi) +
+    // the resident-A pointwise kernel with fp32 output runs as kEpiPW32
+    const int epi = (op.reskb && op.epi == kEpiPW && !op.args.out_f16) ? int(kEpiPW32) : op.epi;
+    return "gemm_kernel<" + std::to_string(op.akind) + ", " + std::to_string(op.bn) + ", " + std::to_string(epi) +
            (op.reskb ? ", " + std::to_string(op.reskb) : std::string()) + ">";
 }
 

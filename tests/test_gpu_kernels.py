@@ -104,6 +104,15 @@ def test_pointwise_epilogues(vxb, wt, res, snk, out16):
     _pw_case(vxb, 384, 192, 300, wt, res, snk, out16, seed=7)
 
 
+@pytest.mark.parametrize("res,snk,out16", [(True, False, False), (False, False, False), (True, True, True)])
+def test_pointwise_resident_weight_column(vxb, res, snk, out16):
+    """Q4_0 at 384 channels over enough tokens that every CTA keeps its m tile's
+    dequantised weight column resident across several n tiles (the resident-A
+    kernels: fp32 output with the 4-deep residual ring, fp16 Snake output with
+    the staging buffers); 12 871 tokens leave a ragged last tile."""
+    _pw_case(vxb, 384, 384, 12871, "q4", res, snk, out16, seed=11)
+
+
 @pytest.mark.parametrize("wt", ["f16", "q4"])
 @pytest.mark.parametrize("Cin,Cout,s,B,T", [(1536, 768, 8, 1, 6), (768, 384, 8, 1, 48), (384, 192, 5, 1, 384),
                                             (192, 96, 2, 1, 1920), (384, 192, 5, 3, 7), (192, 96, 2, 2, 300),
